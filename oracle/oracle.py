@@ -1,0 +1,313 @@
+"""ctypes binding of the CPU oracle (oracle/_build/liboracle.so).
+
+TEST INFRASTRUCTURE ONLY. Imported by tests/, by __graft_entry__.smoke() as the checker and by
+bench.py's CPU-baseline leg; the product library never uses it.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB = HERE / "_build" / "liboracle.so"
+
+P = C.c_void_p
+I32 = C.c_int
+I64 = C.c_int64
+U64 = C.c_uint64
+F32 = C.c_float
+F64 = C.c_double
+
+NL_APPROX, NL_GPU, NL_MPC = 0, 1, 2
+
+_SIGS = {
+    "orc_set_threads": (None, [I32]),
+    "orc_max_threads": (I32, []),
+    "orc_linear_f32": (None, [P, P, I32, I32, P, P, P, P, I32]),
+    "orc_linear_bf16": (None, [P, P, I32, I32, P, P, P, P, I32]),
+    "orc_linear_abs_bf16": (None, [P, I32, I32, P, P]),
+    "orc_linear_ring": (None, [P, P, I32, I32, P, P, P, P, I32, I32]),
+    "orc_plaintext_linear_ring": (None, [P, P, I32, I32, P, P, I32]),
+    "orc_fixed_from_f64": (I32, [F64, I32, P]),
+    "orc_fixed_mul": (I32, [I32, I32, I32, P]),
+    "orc_beaver_f32": (None, [P] * 14 + [I64]),
+    "orc_beaver_ring": (None, [P] * 14 + [I64, I32]),
+    "orc_philox_words": (None, [U64, U64, U64, P, I64]),
+    "orc_fill_uniform": (None, [U64, U64, F32, F32, P, I64]),
+    "orc_triples_f32": (None, [U64, U64, I64] + [P] * 9),
+    "orc_triples_ring": (None, [U64, U64, I64] + [P] * 6),
+    "orc_embed_shares": (None, [P, I32, I32, U64, U64, P, P]),
+    "orc_rope_table": (None, [I32, I32, F32, P, P]),
+    "orc_rope_apply": (None, [P, I32, I32, P, P, P]),
+    "orc_rmsnorm_reshare": (None, [P, P, P, F32, I32, P, P, P, I32]),
+    "orc_swiglu_reshare": (None, [P, P, P, P, I32, P, P, P, I32]),
+    "orc_silu_reshare": (None, [P, P, I32, P, P, P, I32]),
+    "orc_softmax_approx": (None, [P, P, I32, P]),
+    "orc_attention": (None, [P, P, P, I32, I32, I32, I32, I32, P, P, P]),
+    "orc_argmax_last": (I32, [P, P, I32]),
+    "orc_model_create": (P, [I32, I32, I32, I32, I32, I32, I32, F32, F32, I32]),
+    "orc_model_destroy": (None, [P]),
+    "orc_model_set_layer": (None, [P, I32] + [P] * 12),
+    "orc_model_set_head": (None, [P, P, P]),
+    "orc_model_reset": (None, [P]),
+    "orc_model_forward": (I32, [P, P, P, I32, I32, P, I64, I32, P, P, P, P]),
+}
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        srcs = list(HERE.glob("*.cpp"))
+        if not LIB.exists() or max(s.stat().st_mtime for s in srcs) > LIB.stat().st_mtime:
+            subprocess.run(["make", "-C", str(HERE)], check=True, capture_output=True)
+        _lib = C.CDLL(str(LIB))
+        for n, (res, args) in _SIGS.items():
+            f = getattr(_lib, n)
+            f.restype = res
+            f.argtypes = args
+    return _lib
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data
+
+
+def _c(a, dt):
+    return np.ascontiguousarray(np.asarray(a, dtype=dt))
+
+
+def set_threads(n: int) -> None:
+    lib().orc_set_threads(int(n))
+
+
+def max_threads() -> int:
+    return int(lib().orc_max_threads())
+
+
+def linear_f32(w_in_out, bias, xc, xs):
+    """SecureLinear::forward_secure on [M][in] shares; w [in][out] f32."""
+    w = _c(w_in_out, np.float32)
+    xc, xs = np.atleast_2d(_c(xc, np.float32)), np.atleast_2d(_c(xs, np.float32))
+    M, K = xc.shape
+    N = w.size // K
+    yc, ys = np.empty((M, N), np.float32), np.empty((M, N), np.float32)
+    lib().orc_linear_f32(_p(w), _p(None if bias is None else _c(bias, np.float32)), K, N, _p(xc), _p(xs), _p(yc), _p(ys), M)
+    return yc, ys
+
+
+def linear_bf16(w_in_out_u16, bias, xc, xs):
+    w = _c(w_in_out_u16, np.uint16)
+    xc, xs = np.atleast_2d(_c(xc, np.float32)), np.atleast_2d(_c(xs, np.float32))
+    M, K = xc.shape
+    N = w.size // K
+    yc, ys = np.empty((M, N), np.float32), np.empty((M, N), np.float32)
+    b = None if bias is None else _c(bias, np.float32)
+    lib().orc_linear_bf16(_p(w), _p(b), K, N, _p(xc), _p(xs), _p(yc), _p(ys), M)
+    return yc, ys
+
+
+def linear_abs_bf16(w_in_out_u16, x):
+    w = _c(w_in_out_u16, np.uint16)
+    x = _c(x, np.float32).reshape(-1)
+    K = x.size
+    N = w.size // K
+    y = np.empty(N, np.float64)
+    lib().orc_linear_abs_bf16(_p(w), K, N, _p(x), _p(y))
+    return y
+
+
+def linear_ring(w_in_out, bias, xc, xs, scale=16):
+    w = _c(w_in_out, np.int32)
+    xc, xs = np.atleast_2d(_c(xc, np.int32)), np.atleast_2d(_c(xs, np.int32))
+    M, K = xc.shape
+    N = w.size // K
+    yc, ys = np.empty((M, N), np.int32), np.empty((M, N), np.int32)
+    b = None if bias is None else _c(bias, np.int32)
+    lib().orc_linear_ring(_p(w), _p(b), K, N, _p(xc), _p(xs), _p(yc), _p(ys), M, scale)
+    return yc, ys
+
+
+def plaintext_linear_ring(w_in_out, bias, x, scale=16):
+    w = _c(w_in_out, np.int32)
+    x = _c(x, np.int32).reshape(-1)
+    N = w.size // x.size
+    y = np.empty(N, np.int32)
+    lib().orc_plaintext_linear_ring(_p(w), _p(None if bias is None else _c(bias, np.int32)), x.size, N, _p(x), _p(y), scale)
+    return y
+
+
+class FixedPointError(ValueError):
+    pass
+
+
+def fixed_from_f64(v: float, scale: int = 16) -> int:
+    out = np.zeros(1, np.int32)
+    rc = lib().orc_fixed_from_f64(float(v), scale, _p(out))
+    if rc == 1:
+        raise FixedPointError(f"Overflow {{ value: {v} }}")
+    if rc == 2:
+        raise FixedPointError(f"Underflow {{ value: {v} }}")
+    if rc == 3:
+        raise FixedPointError(f"InvalidScale({scale})")
+    return int(out[0])
+
+
+def fixed_mul(a: int, b: int, scale: int = 16) -> int:
+    out = np.zeros(1, np.int32)
+    if lib().orc_fixed_mul(int(a), int(b), scale, _p(out)) != 0:
+        raise FixedPointError("Overflow")
+    return int(out[0])
+
+
+def beaver_f32(xc, xs, yc, ys, ac, as_, bc, bs, cc, cs):
+    arrs = [_c(a, np.float32) for a in (xc, xs, yc, ys, ac, as_, bc, bs, cc, cs)]
+    n = arrs[0].size
+    d, e, zc, zs = (np.empty(n, np.float32) for _ in range(4))
+    lib().orc_beaver_f32(*[_p(a) for a in arrs], _p(d), _p(e), _p(zc), _p(zs), n)
+    return zc, zs, d, e
+
+
+def beaver_ring(xc, xs, yc, ys, ac, as_, bc, bs, cc, cs, trunc_shift=0):
+    arrs = [_c(a, np.uint32) for a in (xc, xs, yc, ys, ac, as_, bc, bs, cc, cs)]
+    n = arrs[0].size
+    d, e, zc, zs = (np.empty(n, np.uint32) for _ in range(4))
+    lib().orc_beaver_ring(*[_p(a) for a in arrs], _p(d), _p(e), _p(zc), _p(zs), n, trunc_shift)
+    return zc, zs, d, e
+
+
+def philox_words(seed, stream, offset, n):
+    out = np.empty(n, np.uint32)
+    lib().orc_philox_words(seed, stream, offset, _p(out), n)
+    return out
+
+
+def fill_uniform(seed, offset, lo, hi, n):
+    out = np.empty(n, np.float32)
+    lib().orc_fill_uniform(seed, offset, lo, hi, _p(out), n)
+    return out
+
+
+def triples_f32(seed, offset, n):
+    out = [np.empty(n, np.float32) for _ in range(9)]
+    lib().orc_triples_f32(seed, offset, n, *[_p(a) for a in out])
+    return out  # a, b, c, a_c, a_s, b_c, b_s, c_c, c_s
+
+
+def triples_ring(seed, offset, n):
+    out = [np.empty(n, np.uint32) for _ in range(6)]
+    lib().orc_triples_ring(seed, offset, n, *[_p(a) for a in out])
+    return out  # a_c, a_s, b_c, b_s, c_c, c_s
+
+
+def embed_shares(table_u16, hidden, token, seed, counter):
+    t = _c(table_u16, np.uint16)
+    hc, hs = np.empty(hidden, np.float32), np.empty(hidden, np.float32)
+    lib().orc_embed_shares(_p(t), hidden, int(token), seed, counter, _p(hc), _p(hs))
+    return hc, hs
+
+
+def rope_table(head_dim, max_seq, theta):
+    c = np.empty((max_seq, head_dim // 2), np.float32)
+    s = np.empty((max_seq, head_dim // 2), np.float32)
+    lib().orc_rope_table(head_dim, max_seq, theta, _p(c), _p(s))
+    return c, s
+
+
+def rope_apply(share, n_heads, head_dim, cos_row, sin_row):
+    x = _c(share, np.float32)
+    out = np.empty_like(x)
+    lib().orc_rope_apply(_p(x), n_heads, head_dim, _p(_c(cos_row, np.float32)), _p(_c(sin_row, np.float32)), _p(out))
+    return out
+
+
+def rmsnorm_reshare(xc, xs, gamma, eps, variant, mask=None):
+    xc, xs, g = _c(xc, np.float32), _c(xs, np.float32), _c(gamma, np.float32)
+    n = xc.size
+    yc, ys = np.empty(n, np.float32), np.empty(n, np.float32)
+    lib().orc_rmsnorm_reshare(_p(xc), _p(xs), _p(g), eps, variant, _p(None if mask is None else _c(mask, np.float32)), _p(yc), _p(ys), n)
+    return yc, ys
+
+
+def swiglu_reshare(gc, gs, uc, us, variant, mask=None):
+    a = [_c(v, np.float32) for v in (gc, gs, uc, us)]
+    n = a[0].size
+    yc, ys = np.empty(n, np.float32), np.empty(n, np.float32)
+    lib().orc_swiglu_reshare(*[_p(v) for v in a], variant, _p(None if mask is None else _c(mask, np.float32)), _p(yc), _p(ys), n)
+    return yc, ys
+
+
+def silu_reshare(xc, xs, variant, mask=None):
+    xc, xs = _c(xc, np.float32), _c(xs, np.float32)
+    n = xc.size
+    yc, ys = np.empty(n, np.float32), np.empty(n, np.float32)
+    lib().orc_silu_reshare(_p(xc), _p(xs), variant, _p(None if mask is None else _c(mask, np.float32)), _p(yc), _p(ys), n)
+    return yc, ys
+
+
+def softmax_approx(sc, ss):
+    sc, ss = _c(sc, np.float32), _c(ss, np.float32)
+    w = np.empty(sc.size, np.float32)
+    lib().orc_softmax_approx(_p(sc), _p(ss), sc.size, _p(w))
+    return w
+
+
+def attention(q, kcache, vcache, H, Hkv, d, variant, mask=None):
+    q, k, v = _c(q, np.float32), _c(kcache, np.float32), _c(vcache, np.float32)
+    kv_len = k.size // (Hkv * d)
+    oc, os_ = np.empty(H * d, np.float32), np.empty(H * d, np.float32)
+    lib().orc_attention(_p(q), _p(k), _p(v), kv_len, H, Hkv, d, variant, _p(None if mask is None else _c(mask, np.float32)), _p(oc), _p(os_))
+    return oc, os_
+
+
+def argmax_last(lc, ls):
+    lc, ls = _c(lc, np.float32), _c(ls, np.float32)
+    return int(lib().orc_argmax_last(_p(lc), _p(ls), lc.size))
+
+
+class Model:
+    """CPU layer loop of the reference (oracle_model.cpp); weights bf16 in [in][out] layout."""
+
+    def __init__(self, h, L, H, Hkv, d, I, V, theta=1e6, eps=1e-6, max_seq=2048):
+        self.h, self.L, self.H, self.Hkv, self.d, self.I, self.V = h, L, H, Hkv, d, I, V
+        self._keep = []
+        self.ptr = lib().orc_model_create(h, L, H, Hkv, d, I, V, theta, eps, max_seq)
+
+    def set_layer(self, l, wq, wk, wv, wo, wg, wu, wd, bq, bk, bv, g1, g2):
+        arrs = [_c(a, np.uint16) for a in (wq, wk, wv, wo, wg, wu, wd)]
+        arrs += [None if a is None else _c(a, np.float32) for a in (bq, bk, bv)]
+        arrs += [_c(g1, np.float32), _c(g2, np.float32)]
+        self._keep.append(arrs)
+        lib().orc_model_set_layer(self.ptr, l, *[_p(a) for a in arrs])
+
+    def set_head(self, lm_head_in_out, final_norm):
+        a = [_c(lm_head_in_out, np.uint16), _c(final_norm, np.float32)]
+        self._keep.append(a)
+        lib().orc_model_set_head(self.ptr, _p(a[0]), _p(a[1]))
+
+    def reset(self):
+        lib().orc_model_reset(self.ptr)
+
+    def forward(self, hc, hs, variant=NL_APPROX, attn_variant=NL_APPROX, masks=None, n_layers=0):
+        hc, hs = _c(hc, np.float32), _c(hs, np.float32)
+        mk = None if masks is None else _c(masks, np.float32)
+        stride = 0 if mk is None else mk.size // self.L
+        oc, os_ = np.empty(self.h, np.float32), np.empty(self.h, np.float32)
+        want_logits = n_layers in (0, self.L)
+        lc = np.empty(self.V, np.float32) if want_logits else None
+        ls = np.empty(self.V, np.float32) if want_logits else None
+        rc = lib().orc_model_forward(self.ptr, _p(hc), _p(hs), variant, attn_variant, _p(mk), stride,
+                                     n_layers, _p(oc), _p(os_), _p(lc), _p(ls))
+        if rc != 0:
+            raise RuntimeError("oracle model: position beyond max_seq")
+        return oc, os_, lc, ls
+
+    def __del__(self):
+        try:
+            lib().orc_model_destroy(self.ptr)
+        except Exception:
+            pass

@@ -1,0 +1,103 @@
+"""ctypes binding of libshardlm_cuda.so (the C ABI declared in include/shardlm_cuda.h).
+
+There is no fallback: if the library cannot be loaded (or built with nvcc when it is missing or
+older than its sources), every entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import threading
+
+from . import build as _build
+
+P = C.c_void_p
+I32 = C.c_int
+I64 = C.c_int64
+U64 = C.c_uint64
+F32 = C.c_float
+PP = C.POINTER(C.c_void_p)
+
+SHD_OK = 0
+SHD_ERR_ARG = -1
+SHD_ERR_CUDA = -2
+SHD_ERR_NCCL = -3
+SHD_ERR_TIMEOUT = -4
+SHD_ERR_UNSUPPORTED = -5
+SHD_ERR_NUMERIC = -6
+
+NL_APPROX, NL_GPU, NL_MPC = 0, 1, 2
+ROWS_PLAIN, ROWS_QKV, ROWS_GATEUP = 0, 1, 2
+
+_ERR_NAMES = {
+    SHD_ERR_ARG: "SHD_ERR_ARG",
+    SHD_ERR_CUDA: "SHD_ERR_CUDA",
+    SHD_ERR_NCCL: "SHD_ERR_NCCL",
+    SHD_ERR_TIMEOUT: "SHD_ERR_TIMEOUT",
+    SHD_ERR_UNSUPPORTED: "SHD_ERR_UNSUPPORTED",
+    SHD_ERR_NUMERIC: "SHD_ERR_NUMERIC",
+}
+
+# name -> (restype, argtypes); mirrors include/shardlm_cuda.h
+SIGNATURES: dict[str, tuple] = {
+    "shd_init": (I32, [I32, PP]),
+    "shd_destroy": (I32, [P]),
+    "shd_set_stream": (I32, [P, P]),
+    "shd_last_error": (C.c_char_p, [P]),
+    "shd_sync": (I32, [P]),
+    "shd_launch_count": (I64, [P]),
+    "shd_weight_upload_f32_as_bf16": (I32, [P, P, I32, I32, PP]),
+    "shd_weight_from_bf16": (I32, [P, P, P, I32, I32, I32, I32, PP]),
+    "shd_weight_upload_i32": (I32, [P, P, P, I32, I32, PP]),
+    "shd_weight_destroy": (I32, [P]),
+    "shd_weight_device_bytes": (I64, [P]),
+    "shd_linear_dual_f32": (I32, [P, P, P, P, P, P, P, I32, P, P]),
+    "shd_linear_dual_ring": (I32, [P, P, P, P, P, P, P, I32, I32]),
+    "shd_reconstruct_f32": (I32, [P, P, P, P, I64]),
+    "shd_reshare_f32": (I32, [P, P, P, P, P, I64]),
+    "shd_add_shares": (I32, [P, P, P, P, P, P, P, I64]),
+    "shd_beaver_mul_f32": (I32, [P] + [P] * 14 + [I64]),
+    "shd_beaver_mul_ring": (I32, [P] + [P] * 14 + [I64, I32]),
+    "shd_beaver_triples_f32": (I32, [P, U64, U64, I64] + [P] * 9),
+    "shd_beaver_triples_ring": (I32, [P, U64, U64, I64] + [P] * 6),
+    "shd_fill_uniform_f32": (I32, [P, U64, U64, F32, F32, P, I64]),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+class ShdError(RuntimeError):
+    def __init__(self, code: int, message: str):
+        self.code = code
+        super().__init__(f"{_ERR_NAMES.get(code, code)}: {message}")
+
+
+def lib() -> C.CDLL:
+    """Load libshardlm_cuda.so, building it first when missing or stale."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if _build.library_stale() and os.environ.get("SHD_NO_BUILD") != "1":
+            _build.build_library()
+        if not _build.LIB.exists():
+            raise RuntimeError(f"libshardlm_cuda.so missing at {_build.LIB}")
+        handle = C.CDLL(str(_build.LIB), mode=C.RTLD_GLOBAL)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+def check(rc: int, ctx_ptr=None) -> None:
+    if rc != SHD_OK:
+        msg = ""
+        if ctx_ptr:
+            raw = lib().shd_last_error(ctx_ptr)
+            msg = raw.decode() if raw else ""
+        raise ShdError(rc, msg)

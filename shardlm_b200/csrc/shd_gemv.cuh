@@ -1,0 +1,101 @@
+// Internal interface of the dual-share GEMV family (used by the C ABI and by the model loop).
+#pragma once
+
+#include "shd_common.cuh"
+
+namespace shd {
+
+constexpr int kTileRows = 32;          // weight rows per tile
+constexpr int kChunkBf16 = 256;        // bf16 columns per chunk (16 KB block)
+constexpr int kChunkI32 = 128;         // i32 columns per chunk (16 KB block)
+constexpr int kBlockBytes = 16384;     // one tiled weight block = one pipeline stage of weights
+constexpr int kConsumerWarps = 8;
+constexpr int kGemvThreads = (kConsumerWarps + 1) * 32;
+
+enum WeightKind { WK_BF16 = 0, WK_I32 = 1 };
+
+// Epilogues of the f32-share GEMV.
+enum Epi {
+  EPI_STORE = 0,   // yc = acc_c (+rc), ys = acc_s + bias (+rs)
+  EPI_QKV = 1,     // bias, RoPE per share on q/k, reconstruct; q -> Q, k/v -> KV cache
+  EPI_GATEUP = 2,  // reconstruct gate/up, SwiGLU, reshare (y - mask, mask)
+  EPI_LOGITS = 3,  // logit shares out + fused greedy argmax (last index among equal maxima)
+};
+
+}  // namespace shd
+
+struct shd_weight {
+  shd_ctx* ctx = nullptr;
+  int kind = shd::WK_BF16;
+  int N = 0, K = 0;        // logical out, in
+  int nT = 0, nKC = 0;     // tiles, chunks
+  int rows = SHD_ROWS_PLAIN;
+  int head_dim = 0;
+  void* d_tiles = nullptr;  // nT * nKC blocks of 16 KB
+  float* d_bias = nullptr;  // f32 bias in tile row order (nT*32), nullable
+  int32_t* d_bias_i32 = nullptr;
+  int64_t bytes = 0;
+};
+
+namespace shd {
+
+struct GemvArgs {
+  const uint8_t* W;
+  int N, K, nT, nKC;
+  const float* Xc;
+  const float* Xs;
+  int ldx;
+  // EPI_STORE
+  const float* bias;  // tile row order
+  const float* Rc;
+  const float* Rs;
+  int ldr;
+  float* Yc;
+  float* Ys;
+  int ldy;
+  // EPI_QKV
+  int q_dim, kv_dim, head_dim;
+  const float* rope_cos;  // [max_seq][head_dim/2]
+  const float* rope_sin;
+  int rope_max_seq;
+  const int* pos;  // [M] positions
+  const int* seq;  // [M] sequence slots (nullable -> 0)
+  float* Q;
+  int ldq;
+  float* Kcache;
+  float* Vcache;
+  int64_t kv_seq_stride;  // floats between sequence slots in the cache
+  // EPI_GATEUP
+  int variant;
+  const float* mask;  // [M][N/2], nullable
+  int ldmask;
+  // EPI_LOGITS
+  unsigned long long* amax;  // [M]
+  // scratch
+  float* partials;
+  int* counters;
+  int* err;
+};
+
+// Launch the f32-share GEMV for M rows with the given epilogue.
+int launch_gemv_f32(shd_ctx* ctx, const shd_weight* w, int M, int epi, GemvArgs a);
+
+struct RingArgs {
+  const uint8_t* W;
+  int N, K, nT, nKC;
+  const int32_t* Xc;
+  const int32_t* Xs;
+  int ldx;
+  const int32_t* bias;  // nullable, [N]
+  int32_t* Yc;
+  int32_t* Ys;
+  int ldy;
+  int scale;
+  long long* partials;
+  int* counters;
+  int* err;
+};
+
+int launch_gemv_ring(shd_ctx* ctx, const shd_weight* w, int M, RingArgs a);
+
+}  // namespace shd

@@ -1,0 +1,178 @@
+"""Pin the CPU oracle against the reference's own known-answer tests (no GPU needed).
+
+Each case restates a Rust test of the reference with the same inputs, expected values and
+tolerances (tests/golden/reference_known_answers.json, made by make_known_answers.py).
+"""
+import json
+import pathlib
+
+import numpy as np
+import pytest
+
+GOLD = json.loads((pathlib.Path(__file__).parent / "golden" / "reference_known_answers.json").read_text())
+
+
+def _shares_f32(x, seed):
+    rng = np.random.default_rng(seed)
+    xs = rng.uniform(-10, 10, size=len(x)).astype(np.float32)
+    xc = (np.asarray(x, np.float32) - xs).astype(np.float32)
+    return xc, xs
+
+
+def _shares_ring(x_fixed, seed):
+    rng = np.random.default_rng(seed)
+    xs = rng.integers(-2**31, 2**31, size=len(x_fixed), dtype=np.int64).astype(np.int32)
+    xc = (np.asarray(x_fixed, np.int64) - xs.astype(np.int64)).astype(np.int32)  # wrapping
+    return xc, xs
+
+
+@pytest.mark.parametrize("name", ["f32_linear_known_answer", "f32_linear_shares_not_plaintext"])
+def test_f32_linear_known_answers(orc, name):
+    c = GOLD[name]
+    for seed in (c["share_seed"], 1, 2, 3):
+        xc, xs = _shares_f32(c["x"], seed)
+        yc, ys = orc.linear_f32(c["weight_in_out"], c["bias"], xc, xs)
+        y = (yc + ys)[0]
+        # random U(-10,10) server shares: f32 share rounding (|x_s| <= 10) stays under 1e-5 * 10
+        assert np.all(np.abs(y - np.asarray(c["expected"], np.float32)) < c["tol"] * 10), (y, c["expected"])
+        # shares individually are not the plaintext output
+        assert not np.allclose(yc[0], c["expected"]) and not np.allclose(ys[0], c["expected"])
+    # with a zero server share the sum is exactly the reference's tolerance bound
+    yc, ys = orc.linear_f32(c["weight_in_out"], c["bias"], np.asarray(c["x"], np.float32), np.zeros(c["in"], np.float32))
+    assert np.all(np.abs((yc + ys)[0] - np.asarray(c["expected"])) < c["tol"])
+
+
+def _fixed_vec(orc, xs, scale=16):
+    return np.array([orc.fixed_from_f64(v, scale) for v in xs], np.int32)
+
+
+@pytest.mark.parametrize("name", ["ring_identity", "ring_bias", "ring_matrix_multiply"])
+def test_ring_known_answers(orc, name):
+    c = GOLD[name]
+    if "weight_f64_in_out" in c:
+        w = _fixed_vec(orc, c["weight_f64_in_out"], c["scale"])
+    else:
+        w = np.asarray(c["weight_in_out"], np.int32)
+    x = _fixed_vec(orc, c["x_f64"], c["scale"])
+    for seed in range(8):
+        xc, xs = _shares_ring(x, seed)
+        yc, ys = orc.linear_ring(w, c["bias"], xc, xs, c["scale"])
+        y = (yc.astype(np.int64) + ys.astype(np.int64)).astype(np.int32)[0]
+        y_f = y.astype(np.float64) / (1 << c["scale"])
+        assert np.all(np.abs(y_f - np.asarray(c["expected"])) < c["tol"]), (name, seed, y_f)
+
+
+def test_ring_matches_plaintext_within_one_lsb(orc):
+    c = GOLD["ring_matches_plaintext"]
+    w = np.asarray(c["weight_in_out"], np.int32)
+    x = _fixed_vec(orc, c["x_f64"], c["scale"])
+    p = orc.plaintext_linear_ring(w, None, x, c["scale"])
+    for seed in range(32):
+        xc, xs = _shares_ring(x, seed)
+        yc, ys = orc.linear_ring(w, None, xc, xs, c["scale"])
+        y = (yc.astype(np.int64) + ys.astype(np.int64)).astype(np.int32)[0]
+        assert np.all(np.abs(y.astype(np.int64) - p.astype(np.int64)) <= c["max_lsb_vs_plaintext"])
+
+
+def test_ring_large_dimension(orc):
+    c = GOLD["ring_large_dimension"]
+    w_f = np.asarray(c["weight_f64_in_out"])
+    w = _fixed_vec(orc, w_f, c["scale"])
+    x = _fixed_vec(orc, c["x_f64"], c["scale"])
+    expected = np.asarray(c["x_f64"]) @ w_f.reshape(c["in"], c["out"])
+    for seed in range(4):
+        xc, xs = _shares_ring(x, seed)
+        yc, ys = orc.linear_ring(w, None, xc, xs, c["scale"])
+        y = (yc.astype(np.int64) + ys.astype(np.int64)).astype(np.int32)[0] / (1 << c["scale"])
+        for i in c["check_indices"]:
+            assert abs(y[i] - expected[i]) < c["tol"]
+
+
+def test_fixed_point_known_answers(orc):
+    c = GOLD["fixed_roundtrip"]
+    for v in c["values"]:
+        assert abs(orc.fixed_from_f64(v) / 65536.0 - v) < c["tol"]
+    a, b = orc.fixed_from_f64(GOLD["fixed_add"]["a"]), orc.fixed_from_f64(GOLD["fixed_add"]["b"])
+    assert abs(((a + b) & 0xFFFFFFFF) / 65536.0 - GOLD["fixed_add"]["expected"]) < 1e-4
+    a, b = orc.fixed_from_f64(GOLD["fixed_sub"]["a"]), orc.fixed_from_f64(GOLD["fixed_sub"]["b"])
+    assert abs((a - b) / 65536.0 - GOLD["fixed_sub"]["expected"]) < 1e-4
+    a, b = orc.fixed_from_f64(GOLD["fixed_mul"]["a"]), orc.fixed_from_f64(GOLD["fixed_mul"]["b"])
+    assert abs(orc.fixed_mul(a, b) / 65536.0 - GOLD["fixed_mul"]["expected"]) < 1e-4
+    with pytest.raises(orc.FixedPointError, match="Overflow"):
+        orc.fixed_from_f64(GOLD["fixed_overflow"]["value"], GOLD["fixed_overflow"]["scale"])
+    assert orc.fixed_from_f64(1.0) == 1 << 16
+    # round half away from zero, as f64::round
+    assert orc.fixed_from_f64(0.5 / 65536) == 1 and orc.fixed_from_f64(-0.5 / 65536) == -1
+
+
+def test_beaver_known_properties(orc):
+    c = GOLD["beaver_triple_correctness"]
+    a, b, cc_, ac, as_, bc, bs, ccl, cs = orc.triples_f32(seed=7, offset=0, n=c["trials"])
+    assert np.all(np.abs(ac + as_ - a) < c["tol"])
+    assert np.all(np.abs(bc + bs - b) < c["tol"])
+    assert np.all(np.abs(ccl + cs - cc_) < c["tol"])
+    assert np.all(np.abs(cc_ - a * b) < c["tol"])
+    m = GOLD["beaver_multiply_correctness"]
+    rng = np.random.default_rng(0)
+    n = m["trials"]
+    x = rng.uniform(-10, 10, n).astype(np.float32)
+    y = rng.uniform(-10, 10, n).astype(np.float32)
+    xs_ = rng.uniform(-10, 10, n).astype(np.float32)
+    ys_ = rng.uniform(-10, 10, n).astype(np.float32)
+    xc_, yc_ = (x - xs_).astype(np.float32), (y - ys_).astype(np.float32)
+    zc, zs, d, e = orc.beaver_f32(xc_, xs_, yc_, ys_, ac, as_, bc, bs, ccl, cs)
+    # the reference compares against x*y of the values it split (x, y), tolerance 1e-4
+    assert np.all(np.abs((zc + zs) - x * y) < m["tol"]), np.max(np.abs((zc + zs) - x * y))
+
+
+def test_nonlinear_known_properties(orc):
+    c = GOLD["softmax_sums_to_one"]
+    w = orc.softmax_approx(c["scores_c"], c["scores_s"])
+    assert abs(w.sum() - 1.0) < c["sum_tol"] and w[2] > w[1] > w[0]
+    c = GOLD["rms_norm_unit_rms"]
+    yc, ys = orc.rmsnorm_reshare(c["x_c"], c["x_s"], c["gamma"], c["eps"], orc.NL_APPROX)
+    assert abs(np.sqrt(np.mean(yc.astype(np.float64) ** 2)) - 1.0) < c["rms_tol"]
+    assert np.all(ys == 0)
+    c = GOLD["silu_positive"]
+    yc, ys = orc.silu_reshare(c["x_c"], c["x_s"], orc.NL_APPROX)
+    for x, r in zip(c["x_c"], yc + ys):
+        if x > 0:
+            assert r > 0
+
+
+def _philox_py(block, stream, seed):
+    m = 0xFFFFFFFF
+    c = [block & m, block >> 32, stream & m, stream >> 32]
+    k0, k1 = seed & m, seed >> 32
+    for r in range(10):
+        if r:
+            k0 = (k0 + 0x9E3779B9) & m
+            k1 = (k1 + 0xBB67AE85) & m
+        p0 = 0xD2511F53 * c[0]
+        p1 = 0xCD9E8D57 * c[2]
+        c = [((p1 >> 32) ^ c[1] ^ k0) & m, p1 & m, ((p0 >> 32) ^ c[3] ^ k1) & m, p0 & m]
+    return c
+
+
+def test_philox_against_independent_python(orc):
+    words = orc.philox_words(0x1234_5678_9ABC_DEF0, 3, 5, 40)
+    ref = []
+    for i in range(5, 45):
+        ref.append(_philox_py(i >> 2, 3, 0x1234_5678_9ABC_DEF0)[i & 3])
+    assert words.tolist() == ref
+    # Random123's published known-answer vector for philox4x32-10 with zero counter and key
+    assert _philox_py(0, 0, 0) == [0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8]
+
+
+def test_rope_table_matches_reference_formula(orc):
+    c, s = orc.rope_table(128, 16, 1e6)
+    inv = (1.0 / np.power(np.float32(1e6), np.arange(0, 64, dtype=np.float32) * 2 / np.float32(128))).astype(np.float32)
+    ang = (np.arange(16, dtype=np.float32)[:, None] * inv[None, :]).astype(np.float32)
+    assert np.allclose(c, np.cos(ang), atol=1e-5) and np.allclose(s, np.sin(ang), atol=1e-5)
+    assert np.all(c[0] == 1.0) and np.all(s[0] == 0.0)
+
+
+def test_argmax_last_index_on_ties(orc):
+    lc = np.array([1.0, 3.0, 2.0, 3.0, -1.0], np.float32)
+    assert orc.argmax_last(lc, np.zeros(5, np.float32)) == 3
+    assert orc.argmax_last(np.array([np.nan, 1.0], np.float32), np.zeros(2, np.float32)) == -1
