@@ -100,11 +100,12 @@ int64_t shd_weight_device_bytes(const shd_weight* w);
 
 /* GpuSecureLinear::forward_secure_gpu_tensor (crates/v2/sharing/src/secure_linear.rs:357-404):
  *   yc = xc . W^T (+ residual_c),   ys = xs . W^T + bias (+ residual_s)
- * xc, xs: [M][in]; yc, ys, residual_*: [M][out]. One pass over W serves both shares and all M rows
- * (M <= 8). bias (device, nullable, [out]) overrides the bias stored with the weight when given.
+ * xc, xs: [M][in]; yc, ys, residual_*: [M][out]. One pass over W serves both shares and up to 8 rows
+ * (larger M is processed in groups of 8). bias (device, nullable, [out]) overrides the bias stored with the weight when given.
  * residual_c/residual_s are both null or both set (secure_add_gpu fused in,
- * crates/v2/sharing/src/secure_nonlinear_gpu.rs:195-212). Requires in % 8 == 0 and 16-byte aligned
- * rows. f32 result within the tolerance stated in tests/test_linear.py of the reference's order. */
+ * crates/v2/sharing/src/secure_nonlinear_gpu.rs:195-212). Inputs whose rows are not 16-byte
+ * aligned (in % 4 != 0) are first copied into context scratch. The f32 result agrees with the
+ * reference's sequential order within the f32 summation bound 2*gamma_in*sum|x||W|. */
 int shd_linear_dual_f32(shd_ctx* ctx, const shd_weight* w, const float* bias, const float* xc,
                         const float* xs, float* yc, float* ys, int M, const float* residual_c,
                         const float* residual_s);
@@ -112,7 +113,7 @@ int shd_linear_dual_f32(shd_ctx* ctx, const shd_weight* w, const float* bias, co
 /* LinearServer::handle_request / multiply_vector (crates/sharing/src/linear.rs:204-274), bit-exact:
  *   acc_j = sum_i (i64)x_i * (i64)W_ij (wrapping), y_j = (i32)(acc_j >> scale),
  *   ys_j = ys_j wrapping_add bias_j (bias from the weight, or `bias` when non-null).
- * xc, xs: [M][in] i32; yc, ys: [M][out] i32; M <= 8; in % 4 == 0. */
+ * xc, xs: [M][in] i32; yc, ys: [M][out] i32; any M and in (rows are staged when unaligned). */
 int shd_linear_dual_ring(shd_ctx* ctx, const shd_weight* w, const int32_t* bias, const int32_t* xc,
                          const int32_t* xs, int32_t* yc, int32_t* ys, int M, int scale);
 
@@ -165,6 +166,135 @@ int shd_beaver_triples_ring(shd_ctx* ctx, uint64_t seed, uint64_t offset, int64_
 /* Uniform f32 in [lo, hi) from the same generator (reshare masks, share generation). */
 int shd_fill_uniform_f32(shd_ctx* ctx, uint64_t seed, uint64_t offset, float lo, float hi,
                          float* out, int64_t n);
+
+/* ----------------------------------------------------------------------------------------------
+ * Nonlinear reconstruct -> compute -> reshare ops, RoPE, attention, embedding shares, sampling
+ * -------------------------------------------------------------------------------------------- */
+
+/* secure_rms_norm_gpu / _approx / _mpc (crates/v2/sharing/src/secure_nonlinear_gpu.rs:53-95,
+ * secure_nonlinear.rs:174-205, secure_nonlinear_mpc.rs:63-110) on M rows of n: reconstruct,
+ * y = x * inv_rms * gamma (variant formula), reshare (y - mask, mask) (mask NULL -> (y, 0)). */
+int shd_rmsnorm_reshare(shd_ctx* ctx, const float* xc, const float* xs, const float* gamma,
+                        float eps, int variant, const float* mask, float* yc, float* ys, int M,
+                        int n);
+/* secure_swiglu_gpu / _approx / _mpc (secure_nonlinear_gpu.rs:131-158, secure_nonlinear.rs:354-380,
+ * secure_nonlinear_mpc.rs:112-163): silu(g) * u on reconstructed values, then reshare. */
+int shd_swiglu_reshare(shd_ctx* ctx, const float* gc, const float* gs, const float* uc,
+                       const float* us, int variant, const float* mask, float* yc, float* ys,
+                       int64_t n);
+/* secure_silu_gpu / secure_silu_approx (secure_nonlinear_gpu.rs:28-48, secure_nonlinear.rs:131-158). */
+int shd_silu_reshare(shd_ctx* ctx, const float* xc, const float* xs, int variant, const float* mask,
+                     float* yc, float* ys, int64_t n);
+/* RopeFrequencies::new (crates/v2/sharing/src/secure_attention.rs:42-63): the cos/sin table is built
+ * on the host with libm powf/cosf/sinf in f32 exactly as the reference does, then uploaded. */
+int shd_rope_init(shd_ctx* ctx, int head_dim, int max_seq, float theta);
+/* RopeFrequencies::apply_to_share (secure_attention.rs:84-121) on both shares, in place, rows m at
+ * positions pos + m: [x0 c - x1 s, x0 s + x1 c] with the reference's rounding (no FMA). */
+int shd_rope_shares(shd_ctx* ctx, float* xc, float* xs, int M, int n_heads, int head_dim, int pos);
+/* secure_attention_approx (crates/v2/sharing/src/secure_nonlinear.rs:287-333; variant APPROX/GPU)
+ * or compute_mpc_attention_on_shares (crates/v2/server/src/routes/secure_inference_mpc.rs:568-663;
+ * variant MPC) for M query rows: q [M][H*d] reconstructed, caches [kv_capacity][Hkv*d]
+ * reconstructed, row m attends positions [0, pos_host[m]]. Output reshared (attn - mask, mask). */
+int shd_attn_decode(shd_ctx* ctx, const float* q, const float* k_cache, const float* v_cache,
+                    int kv_capacity, int H, int Hkv, int head_dim, const int32_t* pos_host, int M,
+                    int variant, const float* mask, float* out_c, float* out_s);
+/* Server-side embedding share generation (get_embeddings_direct, crates/v2/server/src/routes/
+ * secure_inference.rs:387-460): e = bf16 table row, server share uniform [0,1) (24-bit, rand's
+ * Standard f32 construction) from Philox(seed, counter + m), client share e - s. */
+int shd_embed_shares(shd_ctx* ctx, const uint16_t* table, int vocab, int hidden,
+                     const int32_t* tokens, int M, uint64_t seed, uint64_t counter, float* hc,
+                     float* hs);
+/* Client reconstruct + greedy sample (crates/v2/client/src/lib.rs:604-640): argmax of lc + ls,
+ * the LAST index among equal maxima (Iterator::max_by). NaN -> SHD_ERR_NUMERIC at shd_sync. */
+int shd_argmax_reconstruct(shd_ctx* ctx, const float* lc, const float* ls, int V, int M,
+                           int32_t* tokens);
+
+/* ----------------------------------------------------------------------------------------------
+ * Tensor parallelism (NCCL over NVLink, loaded at run time). Replaces the host-mediated
+ * GpuCommunicator::all_reduce_sum (crates/v2/core/src/comm.rs:95-136, "TODO: Implement NCCL" :105).
+ * -------------------------------------------------------------------------------------------- */
+/* ncclGetUniqueId into 128 bytes (rank 0 creates it and shares it with the others). */
+int shd_tp_unique_id(void* out_128_bytes);
+/* Join the TP group as `rank` of `world` on the context's device (world == 1: no NCCL). */
+int shd_tp_init(shd_ctx* ctx, int rank, int world, const void* unique_id_128_bytes);
+int shd_tp_destroy(shd_ctx* ctx);
+/* In-place sum over the group of n floats on the context's stream -- the packed [2][M][h] partial
+ * shares of a row-parallel projection -- then a host wait bounded by timeout_ms (<= 0: unbounded);
+ * on timeout the communicator is aborted and SHD_ERR_TIMEOUT returned. */
+int shd_allreduce_shares(shd_ctx* ctx, float* buf, size_t n, int timeout_ms);
+
+/* ----------------------------------------------------------------------------------------------
+ * Whole-model secret-shared forward pass: the layer loops of batched_full_forward_gpu /
+ * generate_token_gpu (crates/v2/server/src/routes/secure_inference.rs:1553-1796), batched_prefill_
+ * gpu_v3 (:2299-2632) and mpc_prefill (routes/secure_inference_mpc.rs:163-562), with the KV cache
+ * resident on the device (reconstructed f32, as the reference holds it) and decode steps replayed
+ * from a CUDA graph. Tensor parallel over tp_world ranks (one process per GPU): column-parallel
+ * q/k/v and gate/up, row-parallel o/down with an NCCL all-reduce of the packed partial shares.
+ * -------------------------------------------------------------------------------------------- */
+typedef struct shd_model_config {
+  int hidden, n_layers, n_heads, n_kv_heads, head_dim, intermediate, vocab;
+  float rope_theta, rms_eps;
+  int max_seq;          /* KV capacity per sequence slot (also the RoPE table length) */
+  int max_batch;        /* sequence slots decoded together (<= 8)                      */
+  int variant_decode;   /* SHD_NL_* for norms / SwiGLU in decode (reference: APPROX)   */
+  int variant_prefill;  /* SHD_NL_* in prefill (reference V3: GPU; V3-MPC: MPC)        */
+  int variant_attn;     /* SHD_NL_APPROX or SHD_NL_MPC                                 */
+  uint64_t share_seed;  /* seed of the embedding-share generator                       */
+  int tp_rank, tp_world;
+} shd_model_config;
+
+/* This rank's slice of the model under tensor parallelism (computed by shd_model_create). */
+typedef struct shd_shard_info {
+  int q_head_begin, q_head_count;   /* local query heads                                  */
+  int kv_head_begin, kv_head_count; /* kv heads those query heads use (may be replicated) */
+  int inter_begin, inter_count;     /* local slice of the MLP intermediate dimension      */
+  int vocab_begin, vocab_count;     /* local lm_head rows                                 */
+} shd_shard_info;
+
+int shd_model_create(shd_ctx* ctx, const shd_model_config* cfg, shd_model** out);
+int shd_model_destroy(shd_model* m);
+int shd_model_shard_info(const shd_model* m, shd_shard_info* out);
+/* Layer weights of this rank's shard, DEVICE bf16 in [out][in] (safetensors) layout; copied.
+ * wq [q_count*d][h], wk/wv [kv_count*d][h], wo [h][q_count*d], wg/wu [inter_count][h],
+ * wd [h][inter_count]; biases f32 (nullable); norms f32 [h]. */
+int shd_model_set_layer(shd_model* m, int layer, const uint16_t* wq, const uint16_t* wk,
+                        const uint16_t* wv, const uint16_t* wo, const uint16_t* wg,
+                        const uint16_t* wu, const uint16_t* wd, const float* bq, const float* bk,
+                        const float* bv, const float* input_norm, const float* post_attn_norm);
+/* Embedding table bf16 [vocab][h] (full, every rank), lm_head bf16 [vocab_count][h] of this rank
+ * (tied models pass the embedding rows), final norm f32 [h]. Device pointers; copied. */
+int shd_model_set_embedding(shd_model* m, const uint16_t* table);
+int shd_model_set_head(shd_model* m, const uint16_t* lm_head, const float* final_norm);
+/* V3-MPC reshare masks: per layer `stride` floats (device), sliced as mpc_prefill slices its
+ * triple store: [0,h) input norm, [h, h+H*d) attention, [2h,3h) post-attention norm, [3h, 3h+I)
+ * SwiGLU; the final norm uses layer L-1's [0,h). NULL clears (V3: reshare (y, 0)). */
+int shd_model_set_masks(shd_model* m, const float* masks, int64_t stride);
+/* Forget all sequences. */
+int shd_model_reset(shd_model* m);
+/* Prefill a prompt into sequence slot `slot` (chunks of <= 8 positions); writes the greedy next
+ * token to *next_token_host and leaves the slot ready to decode. Synchronous. */
+int shd_model_prefill(shd_model* m, int slot, const int32_t* tokens_host, int n,
+                      int32_t* next_token_host);
+/* Enqueue n_steps greedy decode steps for slots [0, n_active) from a captured CUDA graph; no host
+ * synchronisation. Tokens accumulate on the device; read them with shd_model_read_tokens. */
+int shd_model_decode_async(shd_model* m, int n_steps);
+/* Copy the last `count` decoded steps' tokens ([count][n_active]) to the host (synchronises). */
+int shd_model_read_tokens(shd_model* m, int count, int32_t* tokens_host);
+/* generate_token_gpu semantics with host buffers (secure_inference.rs:1744-1796): hidden shares in
+ * (H2D), all layers at the slot's next position, final norm, lm_head; logit shares out (D2H, the
+ * full vocabulary on every rank). Synchronous. */
+int shd_model_forward_host(shd_model* m, int slot, const float* hc_host, const float* hs_host,
+                           float* logits_c_host, float* logits_s_host);
+/* Current length (positions held in the KV cache) of a slot. */
+int shd_model_seq_len(const shd_model* m, int slot);
+/* Kernels launched by one captured decode step (0 before the first decode). */
+int64_t shd_model_step_launches(const shd_model* m);
+/* Profiling: when on, the captured decode step records CUDA events around every share-wise linear
+ * launch; shd_model_linear_times then returns, for the most recent step, the summed device time
+ * (ms) and the summed weight bytes of the launches of each kind: [0] qkv, [1] o, [2] gate/up,
+ * [3] down, [4] lm_head. Turning it on or off re-captures the graph at the next decode. */
+int shd_model_set_profiling(shd_model* m, int on);
+int shd_model_linear_times(shd_model* m, float* ms_out5, double* bytes_out5);
 
 #ifdef __cplusplus
 }

@@ -53,6 +53,7 @@ _SIGS = {
     "orc_model_set_layer": (None, [P, I32] + [P] * 12),
     "orc_model_set_head": (None, [P, P, P]),
     "orc_model_reset": (None, [P]),
+    "orc_model_set_len": (None, [P, I32]),
     "orc_model_forward": (I32, [P, P, P, I32, I32, P, I64, I32, P, P, P, P]),
 }
 
@@ -291,6 +292,9 @@ class Model:
 
     def reset(self):
         lib().orc_model_reset(self.ptr)
+
+    def set_len(self, n: int):
+        lib().orc_model_set_len(self.ptr, int(n))
 
     def forward(self, hc, hs, variant=NL_APPROX, attn_variant=NL_APPROX, masks=None, n_layers=0):
         hc, hs = _c(hc, np.float32), _c(hs, np.float32)

@@ -287,6 +287,16 @@ ORC_API void orc_model_set_head(void* p, const uint16_t* lm_head, const float* f
   m->final_norm = final_norm;
 }
 
+// Give every layer a zero-filled cache of `len` positions (a bounded CPU sample at a late position
+// without prefilling: attention cost depends on the length, not on the cached values).
+ORC_API void orc_model_set_len(void* p, int len) {
+  OrcModel* m = static_cast<OrcModel*>(p);
+  const size_t kvd = (size_t)m->Hkv * m->d;
+  for (auto& k : m->kcache) k.assign((size_t)len * kvd, 0.0f);
+  for (auto& v : m->vcache) v.assign((size_t)len * kvd, 0.0f);
+  m->len = len;
+}
+
 ORC_API void orc_model_reset(void* p) {
   OrcModel* m = static_cast<OrcModel*>(p);
   for (auto& k : m->kcache) k.clear();

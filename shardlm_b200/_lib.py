@@ -61,7 +61,58 @@ SIGNATURES: dict[str, tuple] = {
     "shd_beaver_triples_f32": (I32, [P, U64, U64, I64] + [P] * 9),
     "shd_beaver_triples_ring": (I32, [P, U64, U64, I64] + [P] * 6),
     "shd_fill_uniform_f32": (I32, [P, U64, U64, F32, F32, P, I64]),
+    "shd_rmsnorm_reshare": (I32, [P, P, P, P, F32, I32, P, P, P, I32, I32]),
+    "shd_swiglu_reshare": (I32, [P, P, P, P, P, I32, P, P, P, I64]),
+    "shd_silu_reshare": (I32, [P, P, P, I32, P, P, P, I64]),
+    "shd_rope_init": (I32, [P, I32, I32, F32]),
+    "shd_rope_shares": (I32, [P, P, P, I32, I32, I32, I32]),
+    "shd_attn_decode": (I32, [P, P, P, P, I32, I32, I32, I32, P, I32, I32, P, P, P]),
+    "shd_embed_shares": (I32, [P, P, I32, I32, P, I32, U64, U64, P, P]),
+    "shd_argmax_reconstruct": (I32, [P, P, P, I32, I32, P]),
+    "shd_tp_unique_id": (I32, [P]),
+    "shd_tp_init": (I32, [P, I32, I32, P]),
+    "shd_tp_destroy": (I32, [P]),
+    "shd_allreduce_shares": (I32, [P, P, C.c_size_t, I32]),
+    "shd_model_create": (I32, [P, P, PP]),
+    "shd_model_destroy": (I32, [P]),
+    "shd_model_shard_info": (I32, [P, P]),
+    "shd_model_set_layer": (I32, [P, I32] + [P] * 12),
+    "shd_model_set_embedding": (I32, [P, P]),
+    "shd_model_set_head": (I32, [P, P, P]),
+    "shd_model_set_masks": (I32, [P, P, I64]),
+    "shd_model_reset": (I32, [P]),
+    "shd_model_prefill": (I32, [P, I32, P, I32, P]),
+    "shd_model_decode_async": (I32, [P, I32]),
+    "shd_model_read_tokens": (I32, [P, I32, P]),
+    "shd_model_forward_host": (I32, [P, I32, P, P, P, P]),
+    "shd_model_seq_len": (I32, [P, I32]),
+    "shd_model_step_launches": (I64, [P]),
+    "shd_model_set_profiling": (I32, [P, I32]),
+    "shd_model_linear_times": (I32, [P, P, P]),
 }
+
+
+class ModelConfigC(C.Structure):
+    """shd_model_config of include/shardlm_cuda.h."""
+    _fields_ = [
+        ("hidden", I32), ("n_layers", I32), ("n_heads", I32), ("n_kv_heads", I32),
+        ("head_dim", I32), ("intermediate", I32), ("vocab", I32),
+        ("rope_theta", F32), ("rms_eps", F32),
+        ("max_seq", I32), ("max_batch", I32),
+        ("variant_decode", I32), ("variant_prefill", I32), ("variant_attn", I32),
+        ("share_seed", U64),
+        ("tp_rank", I32), ("tp_world", I32),
+    ]
+
+
+class ShardInfoC(C.Structure):
+    """shd_shard_info of include/shardlm_cuda.h."""
+    _fields_ = [
+        ("q_head_begin", I32), ("q_head_count", I32),
+        ("kv_head_begin", I32), ("kv_head_count", I32),
+        ("inter_begin", I32), ("inter_count", I32),
+        ("vocab_begin", I32), ("vocab_count", I32),
+    ]
 
 _lib = None
 _lock = threading.Lock()

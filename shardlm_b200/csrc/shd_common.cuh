@@ -38,6 +38,12 @@ struct shd_ctx {
   int rope_head_dim = 0;
   int rope_max_seq = 0;
   float rope_theta = 0.f;
+  // staging for activations whose rows are not 16-byte aligned (in_features % 4 != 0)
+  void* d_xpad = nullptr;
+  size_t xpad_bytes = 0;
+  // split partials of the decode attention kernel
+  float* d_attn_part = nullptr;
+  size_t attn_part_floats = 0;
   // NCCL (tensor parallelism), loaded at run time
   void* nccl_comm = nullptr;
   int tp_rank = 0, tp_world = 1;

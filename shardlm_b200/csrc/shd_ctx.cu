@@ -64,6 +64,8 @@ extern "C" int shd_destroy(shd_ctx* ctx) {
   cudaFree(ctx->d_counters);
   cudaFree(ctx->d_rope_cos);
   cudaFree(ctx->d_rope_sin);
+  cudaFree(ctx->d_xpad);
+  cudaFree(ctx->d_attn_part);
   delete ctx;
   return SHD_OK;
 }

@@ -17,11 +17,18 @@
 
 namespace shd {
 
+// Dynamic shared memory available per CTA on sm_100 (227 KB) minus room for the tile result and
+// the barriers; the pipeline gets as many stages as fit, at most 12.
+constexpr int kSmemBudget = 232448 - 4608;
+constexpr int stages_for(int stage_bytes) {
+  return (kSmemBudget / stage_bytes) > 12 ? 12 : (kSmemBudget / stage_bytes);
+}
+
 template <int M>
 struct F32Cfg {
-  static constexpr int S = (M <= 4) ? 8 : 6;           // pipeline depth
   static constexpr int XB = kChunkBf16 * 4;             // bytes of one (row, share) x chunk
   static constexpr int STAGE = kBlockBytes + M * 2 * XB;
+  static constexpr int S = stages_for(STAGE);           // pipeline depth
   static constexpr int V = 4 * 2 * M;                   // accumulators per lane
   static constexpr int TSUM = kTileRows * 2 * M;        // floats of one tile's result
   static constexpr size_t SMEM = (size_t)S * STAGE + TSUM * 4 + (2 * S + 2) * 8 + 16;
@@ -29,9 +36,9 @@ struct F32Cfg {
 
 template <int M>
 struct RingCfg {
-  static constexpr int S = (M <= 4) ? 8 : 6;
   static constexpr int XB = kChunkI32 * 4;
   static constexpr int STAGE = kBlockBytes + M * 2 * XB;
+  static constexpr int S = stages_for(STAGE);
   static constexpr int V = 4 * 2 * M;
   static constexpr int TSUM = kTileRows * 2 * M;
   static constexpr size_t SMEM = (size_t)S * STAGE + TSUM * 8 + (2 * S + 2) * 8 + 16;
@@ -291,7 +298,7 @@ __device__ void epilogue_f32(const GemvArgs& a, int t, const float* tsum, int ct
         }
         const float l = __fadd_rn(yc, ys);
         nan = isnan(l);
-        key = argmax_key(l, n);
+        key = argmax_key(l, n + a.idx_offset);
       }
       if (__any_sync(0xffffffffu, nan) && lane == 0) atomicOr(err, SHD_DEVERR_NONFINITE);
       // a warp's 32 entries share one m because 32 divides the tile height
@@ -671,7 +678,7 @@ static int launch_f32_m(shd_ctx* ctx, const shd_weight* w, int M, GemvArgs a) {
 int launch_gemv_f32(shd_ctx* ctx, const shd_weight* w, int M, int epi, GemvArgs a) {
   a.W = reinterpret_cast<const uint8_t*>(w->d_tiles);
   a.N = w->N;
-  a.K = w->K;
+  a.K = (w->K + 3) / 4 * 4;  // x extent copied per row (rows padded to 16 bytes)
   a.nT = w->nT;
   a.nKC = w->nKC;
   a.partials = ctx->d_partials;
@@ -706,7 +713,7 @@ static int launch_ring_t(shd_ctx* ctx, const shd_weight* w, RingArgs a) {
 int launch_gemv_ring(shd_ctx* ctx, const shd_weight* w, int M, RingArgs a) {
   a.W = reinterpret_cast<const uint8_t*>(w->d_tiles);
   a.N = w->N;
-  a.K = w->K;
+  a.K = (w->K + 3) / 4 * 4;
   a.nT = w->nT;
   a.nKC = w->nKC;
   a.partials = reinterpret_cast<long long*>(ctx->d_partials);
@@ -729,6 +736,43 @@ int launch_gemv_ring(shd_ctx* ctx, const shd_weight* w, int M, RingArgs a) {
 // ------------------------------------------------------------------------------------------------
 using namespace shd;
 
+// Copy [M][K] 4-byte rows into [M][K4] rows (K4 = K rounded up to 4, zero tail) so every row
+// starts on a 16-byte boundary, as the bulk copies require.
+__global__ void pad_rows_kernel(const uint32_t* __restrict__ a, const uint32_t* __restrict__ b,
+                                uint32_t* __restrict__ pa, uint32_t* __restrict__ pb, int M, int K,
+                                int K4) {
+  const long long n = (long long)M * K4;
+  for (long long v = blockIdx.x * (long long)blockDim.x + threadIdx.x; v < n;
+       v += (long long)gridDim.x * blockDim.x) {
+    const int m = (int)(v / K4), k = (int)(v % K4);
+    pa[v] = k < K ? a[(size_t)m * K + k] : 0u;
+    pb[v] = k < K ? b[(size_t)m * K + k] : 0u;
+  }
+}
+
+static int stage_padded(shd_ctx* ctx, const void* xc, const void* xs, int M, int K, int K4,
+                        const void** oc, const void** os) {
+  const size_t need = (size_t)2 * M * K4 * 4;
+  if (need > ctx->xpad_bytes) {
+    SHD_CHECK_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    cudaFree(ctx->d_xpad);
+    ctx->d_xpad = nullptr;
+    ctx->xpad_bytes = 0;
+    SHD_CHECK_CUDA(ctx, cudaMalloc(&ctx->d_xpad, need));
+    ctx->xpad_bytes = need;
+  }
+  uint32_t* pa = reinterpret_cast<uint32_t*>(ctx->d_xpad);
+  uint32_t* pb = pa + (size_t)M * K4;
+  const long long n = (long long)M * K4;
+  int grid = (int)std::min<long long>((n + 255) / 256, (long long)ctx->num_sms * 8);
+  pad_rows_kernel<<<grid < 1 ? 1 : grid, 256, 0, ctx->stream>>>(
+      reinterpret_cast<const uint32_t*>(xc), reinterpret_cast<const uint32_t*>(xs), pa, pb, M, K, K4);
+  SHD_CHECK_LAUNCH(ctx, "pad_rows_kernel");
+  *oc = pa;
+  *os = pb;
+  return SHD_OK;
+}
+
 // Split M into launches of 8, 4, 2, 1 rows.
 static int next_m(int rem) { return rem >= 8 ? 8 : rem >= 4 ? 4 : rem >= 2 ? 2 : 1; }
 
@@ -743,16 +787,22 @@ extern "C" int shd_linear_dual_f32(shd_ctx* ctx, const shd_weight* w, const floa
   SHD_REQUIRE(ctx, xc && xs && yc && ys, "shd_linear_dual_f32: null share pointer");
   SHD_REQUIRE(ctx, (residual_c == nullptr) == (residual_s == nullptr),
               "shd_linear_dual_f32: residual_c and residual_s must both be set or both null");
-  SHD_REQUIRE(ctx, w->K % 4 == 0, "shd_linear_dual_f32: in_features must be a multiple of 4");
-  SHD_REQUIRE(ctx, shd_aligned16(xc) && shd_aligned16(xs),
-              "shd_linear_dual_f32: share inputs must be 16-byte aligned");
   SHD_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
+  int ldx = w->K;
+  if (w->K % 4 != 0 || !shd_aligned16(xc) || !shd_aligned16(xs)) {
+    ldx = (w->K + 3) / 4 * 4;
+    const void *pc, *ps;
+    const int rc = stage_padded(ctx, xc, xs, M, w->K, ldx, &pc, &ps);
+    if (rc) return rc;
+    xc = reinterpret_cast<const float*>(pc);
+    xs = reinterpret_cast<const float*>(ps);
+  }
   for (int m0 = 0; m0 < M;) {
     const int mm = next_m(M - m0);
     GemvArgs a{};
-    a.Xc = xc + (size_t)m0 * w->K;
-    a.Xs = xs + (size_t)m0 * w->K;
-    a.ldx = w->K;
+    a.Xc = xc + (size_t)m0 * ldx;
+    a.Xs = xs + (size_t)m0 * ldx;
+    a.ldx = ldx;
     a.bias = bias ? bias : w->d_bias;
     a.Rc = residual_c ? residual_c + (size_t)m0 * w->N : nullptr;
     a.Rs = residual_s ? residual_s + (size_t)m0 * w->N : nullptr;
@@ -776,16 +826,22 @@ extern "C" int shd_linear_dual_ring(shd_ctx* ctx, const shd_weight* w, const int
   SHD_REQUIRE(ctx, scale >= 0 && scale <= 30, "shd_linear_dual_ring: scale outside 0..30 (MAX_SCALE)");
   if (M == 0) return SHD_OK;
   SHD_REQUIRE(ctx, xc && xs && yc && ys, "shd_linear_dual_ring: null share pointer");
-  SHD_REQUIRE(ctx, w->K % 4 == 0, "shd_linear_dual_ring: in_features must be a multiple of 4");
-  SHD_REQUIRE(ctx, shd_aligned16(xc) && shd_aligned16(xs),
-              "shd_linear_dual_ring: share inputs must be 16-byte aligned");
   SHD_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
+  int ldx = w->K;
+  if (w->K % 4 != 0 || !shd_aligned16(xc) || !shd_aligned16(xs)) {
+    ldx = (w->K + 3) / 4 * 4;
+    const void *pc, *ps;
+    const int rc = stage_padded(ctx, xc, xs, M, w->K, ldx, &pc, &ps);
+    if (rc) return rc;
+    xc = reinterpret_cast<const int32_t*>(pc);
+    xs = reinterpret_cast<const int32_t*>(ps);
+  }
   for (int m0 = 0; m0 < M;) {
     const int mm = next_m(M - m0);
     RingArgs a{};
-    a.Xc = xc + (size_t)m0 * w->K;
-    a.Xs = xs + (size_t)m0 * w->K;
-    a.ldx = w->K;
+    a.Xc = xc + (size_t)m0 * ldx;
+    a.Xs = xs + (size_t)m0 * ldx;
+    a.ldx = ldx;
     a.bias = bias ? bias : w->d_bias_i32;
     a.Yc = yc + (size_t)m0 * w->N;
     a.Ys = ys + (size_t)m0 * w->N;

@@ -71,6 +71,7 @@ struct GemvArgs {
   int ldmask;
   // EPI_LOGITS
   unsigned long long* amax;  // [M]
+  int idx_offset;            // global index of local row 0 (vocabulary-parallel lm_head)
   // scratch
   float* partials;
   int* counters;

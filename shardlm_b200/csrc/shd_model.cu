@@ -1,0 +1,763 @@
+// Whole-model secret-shared forward pass: the per-token layer loop of the reference
+// (batched_full_forward_gpu / generate_token_gpu, crates/v2/server/src/routes/secure_inference.rs:
+// 1553-1796; batched_prefill_gpu_v3, :2299-2632; mpc_prefill, routes/secure_inference_mpc.rs:
+// 163-562), run entirely on the device:
+//
+//   h = H + D                      (residual of the previous sublayer, per share)
+//   x = reshare(RMSNorm(h_c+h_s))  norm_reshare_kernel
+//   q,k,v shares = x W_qkv^T + b   gemv EPI_QKV: one weight pass for both shares; RoPE per share;
+//                                  q reconstructed, k/v reconstructed into the KV cache
+//   a = reshare(attn(q, K, V))     attn_decode_kernel (split-K, deterministic combine)
+//   D = a W_o^T                    gemv EPI_STORE            [TP: all-reduce D, both shares]
+//   h' = h + D; x = norm(h')       norm_reshare_kernel
+//   act = reshare(silu(g) u)       gemv EPI_GATEUP (gate/up interleaved per tile)
+//   D = act W_down^T               gemv EPI_STORE            [TP: all-reduce D]
+//   final norm, logits shares, greedy argmax (gemv EPI_LOGITS)  [TP: all-reduce max of keys]
+//
+// Activations are [2][M][width] per buffer (client rows, then server rows), so one collective
+// covers both shares. Decode steps for all active slots are captured once into a CUDA graph.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include "shd_gemv.cuh"
+#include "shd_model.cuh"
+#include "shd_nonlinear.cuh"
+
+using namespace shd;
+
+int shd_attn_splits(int num_sms, int H, int M, int max_len);
+
+namespace {
+
+constexpr int kMaxRows = 8;  // rows of one GEMV launch / prefill chunk
+
+// Decode bookkeeping after the logits: tokens = keys, history row, position advance.
+__global__ void finish_step_kernel(const unsigned long long* keys, int* tokens, int* pos, int* hist,
+                                   int hist_cap, unsigned long long* step, int M) {
+  const int m = threadIdx.x;
+  const unsigned long long s = *step;
+  if (m < M) {
+    const int tok = (int)(keys[m] & 0xffffffffu);
+    tokens[m] = tok;
+    hist[(size_t)(s % hist_cap) * M + m] = tok;
+    pos[m] += 1;
+  }
+  __syncthreads();
+  if (m == 0) *step = s + 1;
+}
+
+__global__ void concat_rows_kernel(const uint16_t* a, long long na, const uint16_t* b, long long nb,
+                                   const uint16_t* c, long long nc, uint16_t* out) {
+  const long long n = na + nb + nc;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x)
+    out[i] = i < na ? a[i] : (i < na + nb ? b[i - na] : c[i - na - nb]);
+}
+
+__global__ void concat_f32_kernel(const float* a, int na, const float* b, int nb, const float* c,
+                                  int nc, float* out) {
+  const int n = na + nb + nc;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    out[i] = i < na ? (a ? a[i] : 0.f) : (i < na + nb ? (b ? b[i - na] : 0.f) : (c ? c[i - na - nb] : 0.f));
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------------------------------------
+// Tensor-parallel plan: q heads split evenly (remainder to the first ranks); each rank keeps the kv
+// heads its q heads use; intermediate split in blocks of 16; vocabulary split evenly.
+// ------------------------------------------------------------------------------------------------
+static void make_plan(const shd_model_config& c, shd_shard_info& s) {
+  const int W = std::max(1, c.tp_world), r = c.tp_rank;
+  auto split = [&](int n, int unit, int& b, int& cnt) {
+    const int blocks = n / unit;
+    const int b0 = (int)((long long)blocks * r / W), b1 = (int)((long long)blocks * (r + 1) / W);
+    b = b0 * unit;
+    cnt = (r == W - 1) ? n - b : (b1 - b0) * unit;
+  };
+  split(c.n_heads, 1, s.q_head_begin, s.q_head_count);
+  const int group = c.n_heads / c.n_kv_heads;
+  if (s.q_head_count > 0) {
+    s.kv_head_begin = s.q_head_begin / group;
+    s.kv_head_count = (s.q_head_begin + s.q_head_count - 1) / group - s.kv_head_begin + 1;
+  } else {
+    s.kv_head_begin = 0;
+    s.kv_head_count = 0;
+  }
+  split(c.intermediate, 16, s.inter_begin, s.inter_count);
+  split(c.vocab, 1, s.vocab_begin, s.vocab_count);
+}
+
+int shd_model::use_stream() {
+  saved_stream = ctx->stream;
+  ctx->stream = stream;
+  return SHD_OK;
+}
+
+void shd_model::restore_stream() { ctx->stream = saved_stream; }
+
+// Order the model stream after the caller's stream (entry) and the caller's after ours (exit).
+int shd_model::enter() {
+  SHD_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
+  SHD_CHECK_CUDA(ctx, cudaEventRecord(ev_in, ctx->stream));
+  SHD_CHECK_CUDA(ctx, cudaStreamWaitEvent(stream, ev_in, 0));
+  use_stream();
+  return SHD_OK;
+}
+
+int shd_model::leave(int rc) {
+  restore_stream();
+  if (cudaEventRecord(ev_out, stream) == cudaSuccess) cudaStreamWaitEvent(ctx->stream, ev_out, 0);
+  return rc;
+}
+
+extern "C" int shd_model_create(shd_ctx* ctx, const shd_model_config* cfg, shd_model** out) {
+  if (!ctx || !cfg || !out) return SHD_ERR_ARG;
+  *out = nullptr;
+  const shd_model_config& c = *cfg;
+  SHD_REQUIRE(ctx, c.hidden > 0 && c.n_layers > 0 && c.n_heads > 0 && c.n_kv_heads > 0 &&
+                       c.intermediate > 0 && c.vocab > 0,
+              "shd_model_create: empty dimension");
+  SHD_REQUIRE(ctx, c.n_heads % c.n_kv_heads == 0, "shd_model_create: n_heads % n_kv_heads != 0");
+  SHD_REQUIRE(ctx, c.head_dim % 32 == 0 && c.head_dim <= 256, "shd_model_create: head_dim must be a multiple of 32, <= 256");
+  SHD_REQUIRE(ctx, c.hidden % 4 == 0, "shd_model_create: hidden % 4 != 0");
+  SHD_REQUIRE(ctx, c.intermediate % 16 == 0, "shd_model_create: intermediate % 16 != 0");
+  SHD_REQUIRE(ctx, c.max_batch >= 1 && c.max_batch <= kMaxRows, "shd_model_create: max_batch must be 1..8");
+  SHD_REQUIRE(ctx, c.max_seq >= 1, "shd_model_create: max_seq < 1");
+  SHD_REQUIRE(ctx, c.tp_world >= 1 && c.tp_rank >= 0 && c.tp_rank < c.tp_world, "shd_model_create: bad tp rank/world");
+  SHD_REQUIRE(ctx, c.tp_world <= c.n_heads, "shd_model_create: more ranks than attention heads");
+  for (int v : {c.variant_decode, c.variant_prefill, c.variant_attn})
+    SHD_REQUIRE(ctx, v >= 0 && v <= 2, "shd_model_create: unknown nonlinear variant");
+  if (c.tp_world > 1) SHD_REQUIRE(ctx, ctx->nccl_comm != nullptr, "shd_model_create: tp_world > 1 needs shd_tp_init first");
+  SHD_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
+
+  shd_model* m = new shd_model();
+  m->ctx = ctx;
+  m->cfg = c;
+  make_plan(c, m->sh);
+  const int d = c.head_dim, h = c.hidden;
+  m->qd = m->sh.q_head_count * d;
+  m->kvd = m->sh.kv_head_count * d;
+  m->I = m->sh.inter_count;
+  m->V = m->sh.vocab_count;
+  m->R = std::max(c.max_batch, kMaxRows);
+  m->T = c.max_seq;
+  m->layers.resize(c.n_layers);
+  m->len.assign(c.max_batch, 0);
+  m->hist_cap = 4096;
+  auto fail = [&](int rc) {
+    shd_model_destroy(m);
+    return rc;
+  };
+  if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&m->ev_in, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&m->ev_out, cudaEventDisableTiming) != cudaSuccess)
+    return fail(shd_fail(ctx, SHD_ERR_CUDA, "shd_model_create: stream/event creation failed"));
+  int rc = shd_build_rope(ctx, d, c.max_seq, c.rope_theta);
+  if (rc) return fail(rc);
+  const size_t R = m->R;
+  const size_t kv_elems = (size_t)c.n_layers * c.max_batch * c.max_seq * std::max(m->kvd, 1);
+  struct A {
+    void** p;
+    size_t bytes;
+  } allocs[] = {
+      {(void**)&m->Hbuf[0], 2 * R * h * 4},  {(void**)&m->Hbuf[1], 2 * R * h * 4},
+      {(void**)&m->Dbuf, 2 * R * h * 4},     {(void**)&m->Xbuf, 2 * R * h * 4},
+      {(void**)&m->Qbuf, R * std::max(m->qd, 1) * 4},
+      {(void**)&m->Abuf, 2 * R * std::max(m->qd, 1) * 4},
+      {(void**)&m->ACTbuf, 2 * R * std::max(m->I, 1) * 4},
+      {(void**)&m->LOGbuf, 2 * (size_t)std::max(m->V, 1) * 4},
+      {(void**)&m->LOGfull, c.tp_world > 1 ? 2 * (size_t)c.vocab * 4 : 16},
+      {(void**)&m->kcache, kv_elems * 4},    {(void**)&m->vcache, kv_elems * 4},
+      {(void**)&m->tokens, R * 4},           {(void**)&m->pos, R * 4},
+      {(void**)&m->seq, R * 4},              {(void**)&m->p_pos, R * 4},
+      {(void**)&m->p_seq, R * 4},            {(void**)&m->p_tokens, R * 4},
+      {(void**)&m->kv_head_of, (size_t)std::max(m->sh.q_head_count, 1) * 4},
+      {(void**)&m->amax, R * 8},             {(void**)&m->step, 8},
+      {(void**)&m->hist, (size_t)m->hist_cap * c.max_batch * 4},
+      {(void**)&m->final_norm, (size_t)h * 4},
+  };
+  for (auto& a : allocs) {
+    cudaError_t e = cudaMalloc(a.p, a.bytes);
+    if (e != cudaSuccess) return fail(shd_cuda_fail(ctx, e, "shd_model_create: cudaMalloc"));
+    m->owned.push_back(*a.p);
+  }
+  for (auto& L : m->layers) {
+    cudaError_t e = cudaMalloc(&L.g1, (size_t)h * 4);
+    if (e == cudaSuccess) {
+      m->owned.push_back(L.g1);
+      e = cudaMalloc(&L.g2, (size_t)h * 4);
+    }
+    if (e != cudaSuccess) return fail(shd_cuda_fail(ctx, e, "shd_model_create: cudaMalloc(norm)"));
+    m->owned.push_back(L.g2);
+  }
+  // sequence-slot and kv-head maps
+  std::vector<int> seqv(R), kvmap(std::max(m->sh.q_head_count, 1));
+  for (size_t i = 0; i < R; ++i) seqv[i] = (int)i;
+  const int group = c.n_heads / c.n_kv_heads;
+  for (int i = 0; i < m->sh.q_head_count; ++i) kvmap[i] = (m->sh.q_head_begin + i) / group - m->sh.kv_head_begin;
+  cudaError_t e = cudaMemcpy(m->seq, seqv.data(), R * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(m->kv_head_of, kvmap.data(), kvmap.size() * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemset(m->step, 0, 8);
+  if (e == cudaSuccess) e = cudaMemset(m->kcache, 0, kv_elems * 4);
+  if (e == cudaSuccess) e = cudaMemset(m->vcache, 0, kv_elems * 4);
+  if (e != cudaSuccess) return fail(shd_cuda_fail(ctx, e, "shd_model_create: init"));
+  // attention scratch for the largest launch (kMaxRows rows)
+  m->nsplit = shd_attn_splits(ctx->num_sms, std::max(m->sh.q_head_count, 1), 1, c.max_seq);
+  m->nsplit_prefill = shd_attn_splits(ctx->num_sms, std::max(m->sh.q_head_count, 1), kMaxRows, c.max_seq);
+  const int ns = std::max(m->nsplit, m->nsplit_prefill);
+  rc = ensure_attn_scratch(ctx, (size_t)R * std::max(m->sh.q_head_count, 1) * ns * (d + 2));
+  if (rc) return fail(rc);
+  SHD_REQUIRE(ctx, (int)R * std::max(m->sh.q_head_count, 1) <= 8192, "shd_model_create: too many heads x rows");
+  *out = m;
+  return SHD_OK;
+}
+
+shd_model::~shd_model() {
+  if (graph) cudaGraphExecDestroy(graph);
+  for (cudaEvent_t ev : prof_events) cudaEventDestroy(ev);
+  for (auto& L : layers) {
+    shd_weight_destroy(L.qkv);
+    shd_weight_destroy(L.o);
+    shd_weight_destroy(L.gateup);
+    shd_weight_destroy(L.down);
+  }
+  shd_weight_destroy(lm_head);
+  for (void* p : owned) cudaFree(p);
+  cudaFree(embed);
+  cudaFree(masks);
+  if (ev_in) cudaEventDestroy(ev_in);
+  if (ev_out) cudaEventDestroy(ev_out);
+  if (stream) cudaStreamDestroy(stream);
+}
+
+extern "C" int shd_model_destroy(shd_model* m) {
+  if (!m) return SHD_OK;
+  cudaSetDevice(m->ctx->device);
+  if (m->stream) cudaStreamSynchronize(m->stream);
+  delete m;
+  return SHD_OK;
+}
+
+extern "C" int shd_model_shard_info(const shd_model* m, shd_shard_info* out) {
+  if (!m || !out) return SHD_ERR_ARG;
+  *out = m->sh;
+  return SHD_OK;
+}
+
+extern "C" int shd_model_seq_len(const shd_model* m, int slot) {
+  if (!m || slot < 0 || slot >= m->cfg.max_batch) return SHD_ERR_ARG;
+  return m->len[slot];
+}
+
+extern "C" int shd_model_set_layer(shd_model* m, int layer, const uint16_t* wq, const uint16_t* wk,
+                                   const uint16_t* wv, const uint16_t* wo, const uint16_t* wg,
+                                   const uint16_t* wu, const uint16_t* wd, const float* bq,
+                                   const float* bk, const float* bv, const float* g1, const float* g2) {
+  if (!m) return SHD_ERR_ARG;
+  shd_ctx* ctx = m->ctx;
+  SHD_REQUIRE(ctx, layer >= 0 && layer < m->cfg.n_layers, "shd_model_set_layer: layer out of range");
+  SHD_REQUIRE(ctx, wq && wk && wv && wo && wg && wu && wd && g1 && g2, "shd_model_set_layer: null weight");
+  SHD_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
+  auto& L = m->layers[layer];
+  const int h = m->cfg.hidden, d = m->cfg.head_dim;
+  const long long nq = (long long)m->qd * h, nk = (long long)m->kvd * h;
+  uint16_t* tmp = nullptr;
+  float* btmp = nullptr;
+  const long long need = std::max(nq + 2 * nk, 2LL * m->I * h);
+  SHD_CHECK_CUDA(ctx, cudaMalloc(&tmp, (size_t)need * 2));
+  cudaError_t e = cudaMalloc(&btmp, (size_t)(m->qd + 2 * m->kvd) * 4);
+  if (e != cudaSuccess) {
+    cudaFree(tmp);
+    return shd_cuda_fail(ctx, e, "cudaMalloc");
+  }
+  int rc = SHD_OK;
+  auto cleanup = [&](int r) {
+    cudaStreamSynchronize(ctx->stream);
+    cudaFree(tmp);
+    cudaFree(btmp);
+    return r;
+  };
+  const int grid = ctx->num_sms * 4;
+  concat_rows_kernel<<<grid, 256, 0, ctx->stream>>>(wq, nq, wk, nk, wv, nk, tmp);
+  concat_f32_kernel<<<8, 256, 0, ctx->stream>>>(bq, m->qd, bk, m->kvd, bv, m->kvd, btmp);
+  if ((e = cudaGetLastError()) != cudaSuccess) return cleanup(shd_cuda_fail(ctx, e, "concat qkv"));
+  shd_weight_destroy(L.qkv);
+  L.qkv = nullptr;
+  const bool has_bias = bq || bk || bv;
+  rc = shd_weight_from_bf16(ctx, tmp, has_bias ? btmp : nullptr, h, m->qd + 2 * m->kvd, SHD_ROWS_QKV, d, &L.qkv);
+  if (rc) return cleanup(rc);
+  cudaStreamSynchronize(ctx->stream);
+  concat_rows_kernel<<<grid, 256, 0, ctx->stream>>>(wg, (long long)m->I * h, wu, (long long)m->I * h, nullptr, 0, tmp);
+  if ((e = cudaGetLastError()) != cudaSuccess) return cleanup(shd_cuda_fail(ctx, e, "concat gate/up"));
+  shd_weight_destroy(L.gateup);
+  L.gateup = nullptr;
+  rc = shd_weight_from_bf16(ctx, tmp, nullptr, h, 2 * m->I, SHD_ROWS_GATEUP, 0, &L.gateup);
+  if (rc) return cleanup(rc);
+  shd_weight_destroy(L.o);
+  L.o = nullptr;
+  rc = shd_weight_from_bf16(ctx, wo, nullptr, m->qd, h, SHD_ROWS_PLAIN, 0, &L.o);
+  if (rc) return cleanup(rc);
+  shd_weight_destroy(L.down);
+  L.down = nullptr;
+  rc = shd_weight_from_bf16(ctx, wd, nullptr, m->I, h, SHD_ROWS_PLAIN, 0, &L.down);
+  if (rc) return cleanup(rc);
+  e = cudaMemcpyAsync(L.g1, g1, (size_t)h * 4, cudaMemcpyDeviceToDevice, ctx->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(L.g2, g2, (size_t)h * 4, cudaMemcpyDeviceToDevice, ctx->stream);
+  if (e != cudaSuccess) return cleanup(shd_cuda_fail(ctx, e, "copy norms"));
+  if (m->graph) {  // weights changed: the captured graph holds old pointers
+    cudaGraphExecDestroy(m->graph);
+    m->graph = nullptr;
+  }
+  return cleanup(SHD_OK);
+}
+
+extern "C" int shd_model_set_embedding(shd_model* m, const uint16_t* table) {
+  if (!m) return SHD_ERR_ARG;
+  shd_ctx* ctx = m->ctx;
+  SHD_REQUIRE(ctx, table, "shd_model_set_embedding: null table");
+  SHD_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
+  const size_t bytes = (size_t)m->cfg.vocab * m->cfg.hidden * 2;
+  if (!m->embed) SHD_CHECK_CUDA(ctx, cudaMalloc(&m->embed, bytes));
+  SHD_CHECK_CUDA(ctx, cudaMemcpyAsync(m->embed, table, bytes, cudaMemcpyDeviceToDevice, ctx->stream));
+  SHD_CHECK_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  return SHD_OK;
+}
+
+extern "C" int shd_model_set_head(shd_model* m, const uint16_t* lm_head, const float* final_norm) {
+  if (!m) return SHD_ERR_ARG;
+  shd_ctx* ctx = m->ctx;
+  SHD_REQUIRE(ctx, lm_head && final_norm, "shd_model_set_head: null pointer");
+  SHD_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
+  shd_weight_destroy(m->lm_head);
+  m->lm_head = nullptr;
+  int rc = shd_weight_from_bf16(ctx, lm_head, nullptr, m->cfg.hidden, m->V, SHD_ROWS_PLAIN, 0, &m->lm_head);
+  if (rc) return rc;
+  SHD_CHECK_CUDA(ctx, cudaMemcpyAsync(m->final_norm, final_norm, (size_t)m->cfg.hidden * 4,
+                                      cudaMemcpyDeviceToDevice, ctx->stream));
+  SHD_CHECK_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  if (m->graph) {
+    cudaGraphExecDestroy(m->graph);
+    m->graph = nullptr;
+  }
+  return SHD_OK;
+}
+
+extern "C" int shd_model_set_masks(shd_model* m, const float* masks, int64_t stride) {
+  if (!m) return SHD_ERR_ARG;
+  shd_ctx* ctx = m->ctx;
+  SHD_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
+  if (m->graph) {
+    cudaGraphExecDestroy(m->graph);
+    m->graph = nullptr;
+  }
+  cudaFree(m->masks);
+  m->masks = nullptr;
+  m->mask_stride = 0;
+  if (!masks) return SHD_OK;
+  const int h = m->cfg.hidden;
+  SHD_REQUIRE(ctx, stride >= 3LL * h + m->cfg.intermediate &&
+                       stride >= (int64_t)h + (int64_t)m->cfg.n_heads * m->cfg.head_dim,
+              "shd_model_set_masks: stride shorter than 3*hidden + intermediate");
+  const size_t bytes = (size_t)m->cfg.n_layers * stride * 4;
+  SHD_CHECK_CUDA(ctx, cudaMalloc(&m->masks, bytes));
+  SHD_CHECK_CUDA(ctx, cudaMemcpyAsync(m->masks, masks, bytes, cudaMemcpyDeviceToDevice, ctx->stream));
+  SHD_CHECK_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  m->mask_stride = stride;
+  return SHD_OK;
+}
+
+extern "C" int shd_model_reset(shd_model* m) {
+  if (!m) return SHD_ERR_ARG;
+  std::fill(m->len.begin(), m->len.end(), 0);
+  m->n_active = 0;
+  return SHD_OK;
+}
+
+// ------------------------------------------------------------------------------------------------
+// Enqueue the layers for M rows (positions pos[m] of slots seq[m]) starting from embedding shares in
+// Hbuf[0] and a zero D. Leaves the final residual in (Hbuf[cur], D) for the head.
+// ------------------------------------------------------------------------------------------------
+int shd_model::enqueue_layers(int M, const int* d_pos, const int* d_seq, int variant, int& cur) {
+  const shd_model_config& c = cfg;
+  const int h = c.hidden, d = c.head_dim;
+  const size_t kv_layer = (size_t)c.max_batch * c.max_seq * kvd;
+  const float* mk = masks;
+  int rc;
+  cur = 0;
+  for (int l = 0; l < c.n_layers; ++l) {
+    const LayerW& Lw = layers[l];
+    const float* lm = mk ? mk + (size_t)l * mask_stride : nullptr;
+    float* Hc = Hbuf[cur];
+    float* Ho = Hbuf[cur ^ 1];
+    // input norm: h = D + H -> Ho, x = reshare(norm(h))
+    NormArgs na{};
+    na.Hc = Hc; na.Hs = Hc + (size_t)M * h; na.Dc = Dbuf; na.Ds = Dbuf + (size_t)M * h;
+    na.Hout_c = Ho; na.Hout_s = Ho + (size_t)M * h; na.ldh = h;
+    na.gamma = Lw.g1; na.eps = c.rms_eps; na.variant = variant;
+    na.mask = lm; na.ldmask = 0;
+    na.Xc = Xbuf; na.Xs = Xbuf + (size_t)M * h; na.ldx = h; na.n = h;
+    if ((rc = launch_norm(ctx, na, M))) return rc;
+    // q/k/v with RoPE and KV-cache write
+    GemvArgs g{};
+    g.Xc = Xbuf; g.Xs = Xbuf + (size_t)M * h; g.ldx = h;
+    g.bias = Lw.qkv->d_bias;
+    g.q_dim = qd; g.kv_dim = kvd; g.head_dim = d;
+    g.rope_cos = ctx->d_rope_cos; g.rope_sin = ctx->d_rope_sin; g.rope_max_seq = ctx->rope_max_seq;
+    g.pos = d_pos; g.seq = d_seq;
+    g.Q = Qbuf; g.ldq = qd;
+    g.Kcache = kcache + (size_t)l * kv_layer; g.Vcache = vcache + (size_t)l * kv_layer;
+    g.kv_seq_stride = (int64_t)c.max_seq * kvd;
+    if ((rc = prof_mark(0, Lw.qkv, true))) return rc;
+    if ((rc = launch_gemv_f32(ctx, Lw.qkv, M, EPI_QKV, g))) return rc;
+    if ((rc = prof_mark(0, Lw.qkv, false))) return rc;
+    // attention -> A shares
+    AttnArgs at{};
+    at.Q = Qbuf; at.ldq = qd;
+    at.Kcache = g.Kcache; at.Vcache = g.Vcache; at.kv_seq_stride = g.kv_seq_stride; at.kvd = kvd;
+    at.kv_head_of = kv_head_of; at.H = sh.q_head_count; at.head_dim = d;
+    at.pos = d_pos; at.seq = d_seq; at.variant = c.variant_attn;
+    at.scale = 1.0f / sqrtf((float)d);
+    at.mask = lm ? lm + h + (size_t)sh.q_head_begin * d : nullptr; at.ldmask = 0;
+    at.Oc = Abuf; at.Os = Abuf + (size_t)M * qd; at.ldo = qd;
+    at.nsplit = (M == 1) ? nsplit : nsplit_prefill;
+    at.partials = ctx->d_attn_part;
+    at.counters = ctx->d_counters + (ctx->n_counters - 8192);
+    at.err = ctx->d_err;
+    if ((rc = launch_attention(ctx, at, M))) return rc;
+    // o projection -> D (partial under TP)
+    GemvArgs go{};
+    go.Xc = Abuf; go.Xs = Abuf + (size_t)M * qd; go.ldx = qd;
+    go.Yc = Dbuf; go.Ys = Dbuf + (size_t)M * h; go.ldy = h;
+    if ((rc = prof_mark(1, Lw.o, true))) return rc;
+    if ((rc = launch_gemv_f32(ctx, Lw.o, M, EPI_STORE, go))) return rc;
+    if ((rc = prof_mark(1, Lw.o, false))) return rc;
+    if ((rc = allreduce_sum(Dbuf, (size_t)2 * M * h))) return rc;
+    // post-attention norm: h = D + Ho -> Hc, x
+    NormArgs nb = na;
+    nb.Hc = Ho; nb.Hs = Ho + (size_t)M * h; nb.Hout_c = Hc; nb.Hout_s = Hc + (size_t)M * h;
+    nb.gamma = Lw.g2; nb.mask = lm ? lm + 2 * (size_t)h : nullptr;
+    if ((rc = launch_norm(ctx, nb, M))) return rc;
+    // gate/up + SwiGLU reshare -> ACT
+    GemvArgs gu{};
+    gu.Xc = Xbuf; gu.Xs = Xbuf + (size_t)M * h; gu.ldx = h;
+    gu.Yc = ACTbuf; gu.Ys = ACTbuf + (size_t)M * I; gu.ldy = I;
+    gu.variant = variant;
+    gu.mask = lm ? lm + 3 * (size_t)h + sh.inter_begin : nullptr; gu.ldmask = 0;
+    if ((rc = prof_mark(2, Lw.gateup, true))) return rc;
+    if ((rc = launch_gemv_f32(ctx, Lw.gateup, M, EPI_GATEUP, gu))) return rc;
+    if ((rc = prof_mark(2, Lw.gateup, false))) return rc;
+    // down -> D
+    GemvArgs gd{};
+    gd.Xc = ACTbuf; gd.Xs = ACTbuf + (size_t)M * I; gd.ldx = I;
+    gd.Yc = Dbuf; gd.Ys = Dbuf + (size_t)M * h; gd.ldy = h;
+    if ((rc = prof_mark(3, Lw.down, true))) return rc;
+    if ((rc = launch_gemv_f32(ctx, Lw.down, M, EPI_STORE, gd))) return rc;
+    if ((rc = prof_mark(3, Lw.down, false))) return rc;
+    if ((rc = allreduce_sum(Dbuf, (size_t)2 * M * h))) return rc;
+    // the residual stream for the next layer is (Hc, D)
+  }
+  return SHD_OK;
+}
+
+// Final norm of row `row` of (Hbuf[cur], D) and the lm_head with argmax into amax[key_row].
+int shd_model::enqueue_head(int M, int row, int cur, int variant, bool want_logits, int key_row) {
+  const int h = cfg.hidden;
+  const float* lm = masks ? masks + (size_t)(cfg.n_layers - 1) * mask_stride : nullptr;
+  float* Hc = Hbuf[cur];
+  NormArgs na{};
+  na.Hc = Hc + (size_t)row * h; na.Hs = Hc + (size_t)M * h + (size_t)row * h;
+  na.Dc = Dbuf + (size_t)row * h; na.Ds = Dbuf + (size_t)M * h + (size_t)row * h;
+  na.ldh = h;
+  na.gamma = final_norm; na.eps = cfg.rms_eps; na.variant = variant;
+  na.mask = lm; na.ldmask = 0;
+  na.Xc = Xbuf; na.Xs = Xbuf + h; na.ldx = h; na.n = h;
+  int rc;
+  if ((rc = launch_norm(ctx, na, 1))) return rc;
+  GemvArgs g{};
+  g.Xc = Xbuf; g.Xs = Xbuf + h; g.ldx = h;
+  g.amax = amax + key_row;
+  g.idx_offset = sh.vocab_begin;
+  if (want_logits) {
+    g.Yc = LOGbuf; g.Ys = LOGbuf + V; g.ldy = V;
+  }
+  return launch_gemv_f32(ctx, lm_head, 1, EPI_LOGITS, g);
+}
+
+// Decode head for all M rows (each its own slot): norm M rows, lm_head on M rows.
+int shd_model::enqueue_head_rows(int M, int cur, int variant) {
+  const int h = cfg.hidden;
+  const float* lm = masks ? masks + (size_t)(cfg.n_layers - 1) * mask_stride : nullptr;
+  float* Hc = Hbuf[cur];
+  NormArgs na{};
+  na.Hc = Hc; na.Hs = Hc + (size_t)M * h; na.Dc = Dbuf; na.Ds = Dbuf + (size_t)M * h; na.ldh = h;
+  na.gamma = final_norm; na.eps = cfg.rms_eps; na.variant = variant;
+  na.mask = lm; na.ldmask = 0;
+  na.Xc = Xbuf; na.Xs = Xbuf + (size_t)M * h; na.ldx = h; na.n = h;
+  int rc;
+  if ((rc = launch_norm(ctx, na, M))) return rc;
+  GemvArgs g{};
+  g.Xc = Xbuf; g.Xs = Xbuf + (size_t)M * h; g.ldx = h;
+  g.amax = amax;
+  g.idx_offset = sh.vocab_begin;
+  if ((rc = prof_mark(4, lm_head, true))) return rc;
+  if ((rc = launch_gemv_f32(ctx, lm_head, M, EPI_LOGITS, g))) return rc;
+  return prof_mark(4, lm_head, false);
+}
+
+int shd_model::check_ready() {
+  SHD_REQUIRE(ctx, embed && lm_head, "model: embedding and head must be set");
+  for (auto& L : layers) SHD_REQUIRE(ctx, L.qkv && L.o && L.gateup && L.down, "model: a layer has no weights");
+  return SHD_OK;
+}
+
+extern "C" int shd_model_prefill(shd_model* m, int slot, const int32_t* tokens_host, int n,
+                                 int32_t* next_token_host) {
+  if (!m) return SHD_ERR_ARG;
+  shd_ctx* ctx = m->ctx;
+  SHD_REQUIRE(ctx, slot >= 0 && slot < m->cfg.max_batch, "shd_model_prefill: slot out of range");
+  SHD_REQUIRE(ctx, tokens_host && n > 0, "shd_model_prefill: empty prompt (the reference rejects it)");
+  SHD_REQUIRE(ctx, m->len[slot] + n <= m->cfg.max_seq, "shd_model_prefill: prompt exceeds max_seq");
+  for (int i = 0; i < n; ++i)
+    SHD_REQUIRE(ctx, tokens_host[i] >= 0 && tokens_host[i] < m->cfg.vocab, "shd_model_prefill: token id out of range");
+  int rc = m->check_ready();
+  if (rc) return rc;
+  if ((rc = m->enter())) return rc;
+  const int h = m->cfg.hidden;
+  std::vector<int> hp(3 * kMaxRows);
+  int cur = 0;
+  for (int p0 = 0; p0 < n && rc == SHD_OK; p0 += kMaxRows) {
+    const int M = std::min(kMaxRows, n - p0);
+    for (int i = 0; i < M; ++i) {
+      hp[i] = tokens_host[p0 + i];
+      hp[kMaxRows + i] = m->len[slot] + p0 + i;
+      hp[2 * kMaxRows + i] = slot;
+    }
+    // the staging vector is reused: finish the previous chunk's copies first
+    if (cudaStreamSynchronize(m->stream) != cudaSuccess) { rc = shd_fail(ctx, SHD_ERR_CUDA, "prefill sync"); break; }
+    cudaError_t e = cudaMemcpyAsync(m->p_tokens, hp.data(), M * 4, cudaMemcpyHostToDevice, m->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(m->p_pos, hp.data() + kMaxRows, M * 4, cudaMemcpyHostToDevice, m->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(m->p_seq, hp.data() + 2 * kMaxRows, M * 4, cudaMemcpyHostToDevice, m->stream);
+    if (e != cudaSuccess) { rc = shd_cuda_fail(ctx, e, "prefill staging"); break; }
+    EmbedArgs ea{};
+    ea.table = m->embed; ea.vocab = m->cfg.vocab; ea.hidden = h; ea.tokens = m->p_tokens;
+    ea.pos = m->p_pos; ea.seed = m->cfg.share_seed; ea.counter_base = (uint64_t)slot << 32;
+    ea.Hc = m->Hbuf[0]; ea.Hs = m->Hbuf[0] + (size_t)M * h; ea.ldh = h;
+    ea.Dc = m->Dbuf; ea.Ds = m->Dbuf + (size_t)M * h; ea.amax = m->amax; ea.err = ctx->d_err;
+    if ((rc = launch_embed(ctx, ea, M))) break;
+    if ((rc = m->enqueue_layers(M, m->p_pos, m->p_seq, m->cfg.variant_prefill, cur))) break;
+    if (p0 + M == n) {
+      if ((rc = m->enqueue_head(M, M - 1, cur, m->cfg.variant_prefill, false, 0))) break;
+      if ((rc = m->allreduce_max_keys(1))) break;
+    }
+  }
+  if (rc == SHD_OK) {
+    unsigned long long key = 0;
+    cudaError_t e = cudaMemcpyAsync(&key, m->amax, 8, cudaMemcpyDeviceToHost, m->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+    if (e != cudaSuccess) rc = shd_cuda_fail(ctx, e, "shd_model_prefill");
+    if (rc == SHD_OK) {
+      const int tok = (int)(key & 0xffffffffu);
+      const int next_pos = m->len[slot] + n;
+      // decode state of the slot: input token and its position
+      e = cudaMemcpyAsync(m->tokens + slot, &tok, 4, cudaMemcpyHostToDevice, m->stream);
+      if (e == cudaSuccess) e = cudaMemcpyAsync(m->pos + slot, &next_pos, 4, cudaMemcpyHostToDevice, m->stream);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+      if (e != cudaSuccess) rc = shd_cuda_fail(ctx, e, "shd_model_prefill: state");
+      m->len[slot] = next_pos;
+      m->n_active = std::max(m->n_active, slot + 1);
+      if (next_token_host) *next_token_host = tok;
+    }
+  }
+  rc = m->leave(rc);
+  if (rc == SHD_OK) rc = shd_sync(ctx);
+  return rc;
+}
+
+// One decode step for slots [0, M): embed the current tokens at pos, all layers, head, tokens.
+int shd_model::enqueue_decode_step(int M) {
+  const int h = cfg.hidden;
+  EmbedArgs ea{};
+  ea.table = embed; ea.vocab = cfg.vocab; ea.hidden = h; ea.tokens = tokens; ea.pos = pos;
+  ea.seed = cfg.share_seed; ea.counter_base = 0;
+  ea.Hc = Hbuf[0]; ea.Hs = Hbuf[0] + (size_t)M * h; ea.ldh = h;
+  ea.Dc = Dbuf; ea.Ds = Dbuf + (size_t)M * h; ea.amax = amax; ea.err = ctx->d_err;
+  ea.slot_counter = 1;
+  int rc;
+  if ((rc = launch_embed(ctx, ea, M))) return rc;
+  int cur = 0;
+  if ((rc = enqueue_layers(M, pos, seq, cfg.variant_decode, cur))) return rc;
+  if ((rc = enqueue_head_rows(M, cur, cfg.variant_decode))) return rc;
+  if ((rc = allreduce_max_keys(M))) return rc;
+  finish_step_kernel<<<1, 32, 0, stream>>>(amax, tokens, pos, hist, hist_cap, step, M);
+  SHD_CHECK_LAUNCH(ctx, "finish_step_kernel");
+  return SHD_OK;
+}
+
+extern "C" int shd_model_decode_async(shd_model* m, int n_steps) {
+  if (!m) return SHD_ERR_ARG;
+  shd_ctx* ctx = m->ctx;
+  SHD_REQUIRE(ctx, n_steps >= 0, "shd_model_decode_async: n_steps < 0");
+  SHD_REQUIRE(ctx, m->n_active > 0, "shd_model_decode_async: no prefilled sequence");
+  const int M = m->n_active;
+  for (int s = 0; s < M; ++s)
+    SHD_REQUIRE(ctx, m->len[s] > 0, "shd_model_decode_async: active slots must all be prefilled");
+  for (int s = 0; s < M; ++s)
+    SHD_REQUIRE(ctx, m->len[s] + n_steps <= m->cfg.max_seq, "shd_model_decode_async: would exceed max_seq");
+  if (n_steps == 0) return SHD_OK;
+  int rc = m->check_ready();
+  if (rc) return rc;
+  if ((rc = m->enter())) return rc;
+  int done = 0;
+  if (!m->graph || m->graph_rows != M) {
+    if (m->graph) {
+      cudaGraphExecDestroy(m->graph);
+      m->graph = nullptr;
+    }
+    // one eager step (sets kernel attributes, real work), then capture the step
+    rc = m->enqueue_decode_step(M);
+    done = 1;
+    if (rc == SHD_OK && m->profiling) {
+      const size_t need = (size_t)2 * (4 * m->cfg.n_layers + 1);
+      while (m->prof_events.size() < need) {
+        cudaEvent_t ev;
+        if (cudaEventCreate(&ev) != cudaSuccess) { rc = shd_fail(ctx, SHD_ERR_CUDA, "cudaEventCreate"); break; }
+        m->prof_events.push_back(ev);
+      }
+    }
+    if (rc == SHD_OK) {
+      cudaGraph_t g = nullptr;
+      cudaError_t e = cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal);
+      if (e == cudaSuccess) {
+        m->graph_launch_mark = ctx->launches;
+        m->prof_active = m->profiling != 0;
+        m->prof_next = 0;
+        m->prof_kind.clear();
+        m->prof_bytes.clear();
+        rc = m->enqueue_decode_step(M);
+        m->prof_active = false;
+        m->prof_count = m->prof_next;
+        e = cudaStreamEndCapture(m->stream, &g);
+        if (rc == SHD_OK && e != cudaSuccess) rc = shd_cuda_fail(ctx, e, "capture decode step");
+      } else {
+        rc = shd_cuda_fail(ctx, e, "cudaStreamBeginCapture");
+      }
+      if (rc == SHD_OK) {
+        e = cudaGraphInstantiate(&m->graph, g, 0);
+        if (e != cudaSuccess) rc = shd_cuda_fail(ctx, e, "cudaGraphInstantiate");
+        m->graph_rows = M;
+        m->graph_launches = ctx->launches - m->graph_launch_mark;
+      }
+      if (g) cudaGraphDestroy(g);
+    }
+  }
+  for (int i = done; i < n_steps && rc == SHD_OK; ++i) {
+    cudaError_t e = cudaGraphLaunch(m->graph, m->stream);
+    if (e != cudaSuccess) rc = shd_cuda_fail(ctx, e, "cudaGraphLaunch");
+  }
+  if (rc == SHD_OK) {
+    for (int s = 0; s < M; ++s) m->len[s] += n_steps;
+    m->steps_done += n_steps;
+  }
+  return m->leave(rc);
+}
+
+extern "C" int shd_model_read_tokens(shd_model* m, int count, int32_t* tokens_host) {
+  if (!m) return SHD_ERR_ARG;
+  shd_ctx* ctx = m->ctx;
+  const int M = m->n_active;
+  SHD_REQUIRE(ctx, count >= 0 && count <= m->hist_cap && count <= m->steps_done,
+              "shd_model_read_tokens: count exceeds the decoded steps kept");
+  SHD_REQUIRE(ctx, tokens_host || count == 0, "shd_model_read_tokens: null output");
+  SHD_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
+  SHD_CHECK_CUDA(ctx, cudaStreamSynchronize(m->stream));
+  std::vector<int> all((size_t)m->hist_cap * M);
+  SHD_CHECK_CUDA(ctx, cudaMemcpy(all.data(), m->hist, all.size() * 4, cudaMemcpyDeviceToHost));
+  for (int i = 0; i < count; ++i) {
+    const long long s = m->steps_done - count + i;
+    std::memcpy(tokens_host + (size_t)i * M, all.data() + (size_t)(s % m->hist_cap) * M, (size_t)M * 4);
+  }
+  return shd_sync(ctx);
+}
+
+extern "C" int shd_model_forward_host(shd_model* m, int slot, const float* hc_host, const float* hs_host,
+                                      float* logits_c_host, float* logits_s_host) {
+  if (!m) return SHD_ERR_ARG;
+  shd_ctx* ctx = m->ctx;
+  SHD_REQUIRE(ctx, slot >= 0 && slot < m->cfg.max_batch, "shd_model_forward_host: slot out of range");
+  SHD_REQUIRE(ctx, hc_host && hs_host && logits_c_host && logits_s_host, "shd_model_forward_host: null buffer");
+  SHD_REQUIRE(ctx, m->len[slot] < m->cfg.max_seq, "shd_model_forward_host: sequence full");
+  int rc = m->check_ready();
+  if (rc) return rc;
+  if ((rc = m->enter())) return rc;
+  const int h = m->cfg.hidden;
+  const int p = m->len[slot];
+  int meta[2] = {p, slot};
+  cudaError_t e = cudaMemcpyAsync(m->Hbuf[0], hc_host, (size_t)h * 4, cudaMemcpyHostToDevice, m->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(m->Hbuf[0] + h, hs_host, (size_t)h * 4, cudaMemcpyHostToDevice, m->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(m->p_pos, &meta[0], 4, cudaMemcpyHostToDevice, m->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(m->p_seq, &meta[1], 4, cudaMemcpyHostToDevice, m->stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(m->Dbuf, 0, (size_t)2 * h * 4, m->stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(m->amax, 0, 8, m->stream);
+  if (e != cudaSuccess) rc = shd_cuda_fail(ctx, e, "shd_model_forward_host: upload");
+  int cur = 0;
+  if (rc == SHD_OK) rc = m->enqueue_layers(1, m->p_pos, m->p_seq, m->cfg.variant_decode, cur);
+  if (rc == SHD_OK) rc = m->enqueue_head(1, 0, cur, m->cfg.variant_decode, true, 0);
+  if (rc == SHD_OK) rc = m->gather_logits(logits_c_host, logits_s_host);
+  if (rc == SHD_OK) {
+    e = cudaStreamSynchronize(m->stream);
+    if (e != cudaSuccess) rc = shd_cuda_fail(ctx, e, "shd_model_forward_host");
+    else m->len[slot] = p + 1;
+  }
+  rc = m->leave(rc);
+  if (rc == SHD_OK) rc = shd_sync(ctx);
+  return rc;
+}
+
+int shd_model::prof_mark(int kind, const shd_weight* w, bool begin) {
+  if (!prof_active) return SHD_OK;
+  if (prof_next + 1 >= prof_events.size()) return SHD_OK;
+  if (begin) {
+    prof_kind.push_back(kind);
+    prof_bytes.push_back((double)w->N * (double)w->K * 2.0);
+    SHD_CHECK_CUDA(ctx, cudaEventRecordWithFlags(prof_events[prof_next], stream, cudaEventRecordExternal));
+  } else {
+    SHD_CHECK_CUDA(ctx, cudaEventRecordWithFlags(prof_events[prof_next + 1], stream, cudaEventRecordExternal));
+    prof_next += 2;
+  }
+  return SHD_OK;
+}
+
+extern "C" int64_t shd_model_step_launches(const shd_model* m) { return m ? m->graph_launches : -1; }
+
+extern "C" int shd_model_set_profiling(shd_model* m, int on) {
+  if (!m) return SHD_ERR_ARG;
+  if ((on != 0) != (m->profiling != 0) && m->graph) {
+    cudaGraphExecDestroy(m->graph);
+    m->graph = nullptr;
+  }
+  m->profiling = on != 0;
+  return SHD_OK;
+}
+
+extern "C" int shd_model_linear_times(shd_model* m, float* ms_out5, double* bytes_out5) {
+  if (!m || !ms_out5 || !bytes_out5) return SHD_ERR_ARG;
+  shd_ctx* ctx = m->ctx;
+  SHD_REQUIRE(ctx, m->prof_count > 0, "shd_model_linear_times: no profiled decode step yet");
+  SHD_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
+  SHD_CHECK_CUDA(ctx, cudaStreamSynchronize(m->stream));
+  for (int k = 0; k < 5; ++k) {
+    ms_out5[k] = 0.f;
+    bytes_out5[k] = 0.0;
+  }
+  for (size_t i = 0; i + 1 < m->prof_count; i += 2) {
+    float ms = 0.f;
+    SHD_CHECK_CUDA(ctx, cudaEventElapsedTime(&ms, m->prof_events[i], m->prof_events[i + 1]));
+    const int k = m->prof_kind[i / 2];
+    ms_out5[k] += ms;
+    bytes_out5[k] += m->prof_bytes[i / 2];
+  }
+  return SHD_OK;
+}

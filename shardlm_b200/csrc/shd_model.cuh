@@ -1,0 +1,76 @@
+// Internal definition of shd_model (the device-resident layer loop).
+#pragma once
+
+#include <vector>
+
+#include "shd_gemv.cuh"
+
+struct LayerW {
+  shd_weight* qkv = nullptr;     // fused q|k|v, SHD_ROWS_QKV
+  shd_weight* o = nullptr;       // [h][q_local]
+  shd_weight* gateup = nullptr;  // fused gate|up, SHD_ROWS_GATEUP
+  shd_weight* down = nullptr;    // [h][inter_local]
+  float* g1 = nullptr;           // input RMSNorm gamma
+  float* g2 = nullptr;           // post-attention RMSNorm gamma
+};
+
+struct shd_model {
+  shd_ctx* ctx = nullptr;
+  shd_model_config cfg{};
+  shd_shard_info sh{};
+  cudaStream_t stream = nullptr, saved_stream = nullptr;
+  cudaEvent_t ev_in = nullptr, ev_out = nullptr;
+  int qd = 0, kvd = 0, I = 0, V = 0;  // local widths
+  int R = 8;                          // activation rows
+  int T = 0;                          // KV capacity per slot
+  std::vector<LayerW> layers;
+  shd_weight* lm_head = nullptr;
+  float* final_norm = nullptr;
+  uint16_t* embed = nullptr;
+  // activations: [2][rows][width], client rows then server rows
+  float* Hbuf[2] = {nullptr, nullptr};
+  float *Dbuf = nullptr, *Xbuf = nullptr, *Qbuf = nullptr, *Abuf = nullptr, *ACTbuf = nullptr;
+  float *LOGbuf = nullptr, *LOGfull = nullptr;
+  float* gather_buf = nullptr;  // TP logit all-gather staging
+  float *kcache = nullptr, *vcache = nullptr;  // [L][slots][T][kvd]
+  int *tokens = nullptr, *pos = nullptr, *seq = nullptr;
+  int *p_tokens = nullptr, *p_pos = nullptr, *p_seq = nullptr;
+  int* kv_head_of = nullptr;
+  unsigned long long* amax = nullptr;
+  unsigned long long* step = nullptr;
+  int* hist = nullptr;
+  int hist_cap = 0;
+  long long steps_done = 0;
+  float* masks = nullptr;
+  int64_t mask_stride = 0;
+  std::vector<void*> owned;
+  std::vector<int> len;
+  int n_active = 0;
+  int nsplit = 1, nsplit_prefill = 1;
+  cudaGraphExec_t graph = nullptr;
+  int graph_rows = 0;
+  int64_t graph_launches = 0, graph_launch_mark = 0;
+  // profiling: CUDA events recorded around each linear launch of the captured step
+  int profiling = 0;
+  bool prof_active = false;
+  std::vector<cudaEvent_t> prof_events;
+  std::vector<int> prof_kind;
+  std::vector<double> prof_bytes;
+  size_t prof_next = 0, prof_count = 0;
+  int prof_mark(int kind, const shd_weight* w, bool begin);
+
+  ~shd_model();
+  int use_stream();
+  void restore_stream();
+  int enter();
+  int leave(int rc);
+  int check_ready();
+  int enqueue_layers(int M, const int* d_pos, const int* d_seq, int variant, int& cur);
+  int enqueue_head(int M, int row, int cur, int variant, bool want_logits, int key_row);
+  int enqueue_head_rows(int M, int cur, int variant);
+  int enqueue_decode_step(int M);
+  // tensor parallel collectives (no-ops at tp_world == 1)
+  int allreduce_sum(float* buf, size_t n);
+  int allreduce_max_keys(int M);
+  int gather_logits(float* lc_host, float* ls_host);
+};

@@ -1,0 +1,79 @@
+// Internal interface of the nonlinear, embedding and attention kernels (used by the model loop).
+#pragma once
+
+#include "shd_common.cuh"
+
+namespace shd {
+
+struct NormArgs {
+  const float* Hc;     // residual stream shares [M][ldh]
+  const float* Hs;
+  const float* Dc;     // sublayer output shares to add first (nullable)
+  const float* Ds;
+  float* Hout_c;       // h = D + H written here when given (nullable)
+  float* Hout_s;
+  int ldh;
+  const float* gamma;
+  float eps;
+  int variant;
+  const float* mask;   // reshare mask [M][ldmask] (nullable -> (y, 0))
+  int ldmask;
+  float* Xc;           // normalized shares out [M][ldx]
+  float* Xs;
+  int ldx;
+  int n;
+};
+
+int launch_norm(shd_ctx* ctx, const NormArgs& a, int M);
+
+struct EmbedArgs {
+  const uint16_t* table;  // bf16 [vocab][hidden]
+  int vocab, hidden;
+  const int32_t* tokens;  // [M] device
+  const int* pos;         // [M] device (nullable -> row index)
+  uint64_t seed;
+  uint64_t counter_base;
+  int slot_counter;       // counter = (row << 32) + pos[row] instead of counter_base + pos[row]
+  float* Hc;
+  float* Hs;
+  int ldh;
+  float* Dc;              // zeroed when given
+  float* Ds;
+  unsigned long long* amax;  // reset to 0 when given
+  int* err;
+};
+
+int launch_embed(shd_ctx* ctx, const EmbedArgs& a, int M);
+int launch_keys_to_tokens(shd_ctx* ctx, const unsigned long long* keys, int* tokens, int M);
+
+struct AttnArgs {
+  const float* Q;          // reconstructed queries [M][ldq], local heads
+  int ldq;
+  const float* Kcache;     // [seq][T][kvd] reconstructed
+  const float* Vcache;
+  int64_t kv_seq_stride;   // floats between sequence slots
+  int kvd;                 // local kv heads * head_dim
+  const int* kv_head_of;   // [H] local kv head of each local q head (device)
+  int H;                   // local q heads
+  int head_dim;
+  const int* pos;          // [M] position of the query row; it attends to [0, pos]
+  const int* seq;          // [M] sequence slot (nullable -> 0)
+  int variant;             // SHD_NL_APPROX/GPU: clamp(-40,40); SHD_NL_MPC: plain exp
+  float scale;
+  const float* mask;       // reshare mask [M][ldo] (nullable)
+  int ldmask;
+  float* Oc;               // attention output shares [M][ldo]
+  float* Os;
+  int ldo;
+  int nsplit;
+  float* partials;         // [M][H][nsplit][head_dim + 2]
+  int* counters;           // [M][H]
+  int* err;
+};
+
+int launch_attention(shd_ctx* ctx, const AttnArgs& a, int M);
+int ensure_attn_scratch(shd_ctx* ctx, size_t floats);
+
+int shd_build_rope(shd_ctx* ctx, int head_dim, int max_seq, float theta);
+
+}  // namespace shd

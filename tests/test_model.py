@@ -1,0 +1,137 @@
+"""Whole-model secret-shared forward pass (libshardlm_cuda layer loop) vs the oracle's restatement of
+the reference layer loop on identical weights and shares.
+
+Token ids: the greedy token at every step must equal the oracle's, except where the oracle's top-2
+logit margin is below the float tolerance (then either index is a correct greedy choice of
+numerically equal logits). Logits: relative to the logit scale, within LOGIT_RTOL.
+"""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_RTOL = 2e-4
+
+
+def _oracle_for(orc, shape, host, max_seq):
+    om = orc.Model(shape.hidden, shape.n_layers, shape.n_heads, shape.n_kv_heads, shape.head_dim,
+                   shape.intermediate, shape.vocab, shape.rope_theta, shape.rms_eps, max_seq)
+    for l, w in enumerate(host["layers"]):
+        om.set_layer(l, w["wq"], w["wk"], w["wv"], w["wo"], w["wg"], w["wu"], w["wd"], w["bq"], w["bk"], w["bv"], w["g1"], w["g2"])
+    om.set_head(host["lm_head_in_out"], host["final_norm"])
+    return om
+
+
+def _oracle_step(orc, om, host, shape, token, pos, seed, variant, slot=0):
+    hc, hs = orc.embed_shares(host["embed"], shape.hidden, token, seed, (slot << 32) + pos)
+    return om.forward(hc, hs, variant=variant, attn_variant=orc.NL_APPROX)
+
+
+def _top2_margin(l):
+    s = np.sort(l.astype(np.float64))
+    return s[-1] - s[-2]
+
+
+def _check_token(gpu_tok, lc, ls, orc):
+    l = lc + ls
+    want = orc.argmax_last(lc, ls)
+    if gpu_tok != want:
+        margin = abs(float(l[gpu_tok]) - float(l[want]))
+        assert margin <= LOGIT_RTOL * np.max(np.abs(l)), f"token {gpu_tok} vs oracle {want}, margin {margin}"
+        return False
+    return True
+
+
+@pytest.mark.parametrize("shape_name,n_layers,prompt,steps", [("tiny", 2, 11, 12), ("qwen2.5-1.5b", 2, 9, 6)])
+def test_prefill_decode_tokens_match_oracle(ctx, orc, shape_name, n_layers, prompt, steps):
+    from shardlm_b200.model import SHAPES, SecureModel
+
+    shape = SHAPES[shape_name].replace(n_layers=n_layers)
+    max_seq = 64
+    m = SecureModel(ctx, shape, max_seq=max_seq, share_seed=123)
+    host = m.load_random_weights(seed=5, host_copy=True)
+    om = _oracle_for(orc, shape, host, max_seq)
+    rng = np.random.default_rng(0)
+    toks = rng.integers(0, shape.vocab, prompt).astype(np.int32)
+    nxt = m.prefill(toks)
+    for p, t in enumerate(toks):
+        _, _, lc, ls = _oracle_step(orc, om, host, shape, int(t), p, 123, orc.NL_GPU)
+    _check_token(nxt, lc, ls, orc)
+    gpu = m.decode(steps)[:, 0]
+    inp = nxt
+    exact = 0
+    for i in range(steps):
+        _, _, lc, ls = _oracle_step(orc, om, host, shape, int(inp), prompt + i, 123, orc.NL_APPROX)
+        exact += _check_token(int(gpu[i]), lc, ls, orc)
+        inp = int(gpu[i])  # teacher-force the GPU's choice so one near-tie cannot cascade
+    assert exact >= steps - 1
+    assert m.seq_len() == prompt + steps
+
+
+def test_forward_host_logits_match_oracle(ctx, orc):
+    """generate_token_gpu semantics: hidden shares in, logit shares out, position by position."""
+    from shardlm_b200.model import TINY, SecureModel
+
+    shape = TINY
+    m = SecureModel(ctx, shape, max_seq=32)
+    host = m.load_random_weights(seed=9, host_copy=True)
+    om = _oracle_for(orc, shape, host, 32)
+    rng = np.random.default_rng(4)
+    for p in range(6):
+        x = rng.standard_normal(shape.hidden).astype(np.float32)
+        hs = rng.uniform(0, 1, shape.hidden).astype(np.float32)
+        hc = (x - hs).astype(np.float32)
+        lc, ls = m.forward_host(hc, hs)
+        _, _, oc, os_ = om.forward(hc, hs, variant=orc.NL_APPROX, attn_variant=orc.NL_APPROX)
+        ref = oc + os_
+        got = lc + ls
+        err = np.max(np.abs(got - ref)) / np.max(np.abs(ref))
+        assert err < LOGIT_RTOL, (p, err)
+        # V3 reshares the final norm as (y, 0): the server logit share is exactly zero
+        assert np.all(ls == 0) and np.all(os_ == 0)
+    assert m.seq_len() == 6
+
+
+def test_mpc_masks_reshare(ctx, orc):
+    """V3-MPC masks: reshares become (y - a, a) with the triple store's a values."""
+    from shardlm_b200._lib import NL_MPC
+    from shardlm_b200.model import TINY, SecureModel
+    from shardlm_b200.sharing import beaver_triples_f32
+
+    shape = TINY
+    m = SecureModel(ctx, shape, max_seq=32, variant_decode=NL_MPC, variant_prefill=NL_MPC, variant_attn=NL_MPC)
+    host = m.load_random_weights(seed=2, host_copy=True)
+    P = 10 * shape.hidden + 20 + 5 * 32  # triples_needed_per_layer(hidden, seq)
+    a = torch.stack([beaver_triples_f32(ctx, P, seed=3, offset=l * P).a for l in range(shape.n_layers)])
+    m.set_masks(a)
+    om = _oracle_for(orc, shape, host, 32)
+    masks = a.cpu().numpy()
+    rng = np.random.default_rng(5)
+    for p in range(4):
+        x = rng.standard_normal(shape.hidden).astype(np.float32)
+        hs = rng.uniform(0, 1, shape.hidden).astype(np.float32)
+        hc = (x - hs).astype(np.float32)
+        lc, ls = m.forward_host(hc, hs)
+        _, _, oc, os_ = om.forward(hc, hs, variant=orc.NL_MPC, attn_variant=orc.NL_MPC, masks=masks)
+        err = np.max(np.abs((lc + ls) - (oc + os_))) / np.max(np.abs(oc + os_))
+        assert err < LOGIT_RTOL, err
+        # with masks, the server logit share is no longer zero
+        assert np.max(np.abs(ls)) > 0
+
+
+def test_model_rejects_bad_requests(ctx):
+    from shardlm_b200._lib import ShdError
+    from shardlm_b200.model import TINY, SecureModel
+
+    m = SecureModel(ctx, TINY, max_seq=8)
+    m.load_random_weights(seed=1)
+    with pytest.raises(ShdError, match="empty prompt"):
+        m.prefill([])
+    with pytest.raises(ShdError, match="out of range"):
+        m.prefill([TINY.vocab])
+    with pytest.raises(ShdError, match="max_seq"):
+        m.prefill(list(range(9)))
+    m.prefill([1, 2, 3])
+    with pytest.raises(ShdError, match="max_seq"):
+        m.decode_async(6)
