@@ -25,6 +25,8 @@ __global__ void attn_decode_kernel(const AttnArgs a) {
   float* red = sc + chunk_max;
   __shared__ int last_flag;
 
+  if (tid == 0) pdl_trigger();
+  pdl_wait();  // positions, queries and the cache come from earlier kernels
   const int p = a.pos[m];
   const int kv_len = p + 1;
   const int sq = a.seq ? a.seq[m] : 0;
@@ -145,8 +147,8 @@ int launch_attention(shd_ctx* ctx, const AttnArgs& a, int M) {
   }
   const int threads = std::max(64, std::min(256, a.head_dim));
   dim3 grid(a.nsplit, a.H, M);
-  attn_decode_kernel<<<grid, threads, smem, ctx->stream>>>(a);
-  SHD_CHECK_LAUNCH(ctx, "attn_decode_kernel");
+  SHD_CHECK_CUDA(ctx, launch_pdl(attn_decode_kernel, grid, dim3(threads), smem, ctx->stream, a));
+  ctx->launches++;
   return SHD_OK;
 }
 

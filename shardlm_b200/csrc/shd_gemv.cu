@@ -11,50 +11,31 @@
 // Tiled weight format: block (t, c) holds rows [32t, 32t+32) x columns [256c, 256c+256) as
 // [32 rows][256 bf16]; within a row, lane l's 16 bytes are columns {4l..4l+3, 128+4l..128+4l+3},
 // so weight and activation shared-memory reads are both conflict-free 16-byte loads.
+//
+// The consumer inner loop uses packed f32x2 FMAs (two adjacent columns per instruction) for up to 4
+// token rows. With the RMSNorm prologue, the activation vector is computed once per CTA into shared
+// memory (reconstruct, normalize, reshare) while the producer already streams weights; otherwise
+// activation chunks travel with each weight block. Kernels are launched with programmatic
+// dependent launch: the producer prefetches weights before the previous kernel has finished.
 #include <algorithm>
 
 #include "shd_gemv.cuh"
 
 namespace shd {
 
-// Dynamic shared memory available per CTA on sm_100 (227 KB) minus room for the tile result and
-// the barriers; the pipeline gets as many stages as fit, at most 12.
-constexpr int kSmemBudget = 232448 - 4608;
-constexpr int stages_for(int stage_bytes) {
-  return (kSmemBudget / stage_bytes) > 12 ? 12 : (kSmemBudget / stage_bytes);
-}
-
-template <int M>
-struct F32Cfg {
-  static constexpr int XB = kChunkBf16 * 4;             // bytes of one (row, share) x chunk
-  static constexpr int STAGE = kBlockBytes + M * 2 * XB;
-  static constexpr int S = stages_for(STAGE);           // pipeline depth
-  static constexpr int V = 4 * 2 * M;                   // accumulators per lane
-  static constexpr int TSUM = kTileRows * 2 * M;        // floats of one tile's result
-  static constexpr size_t SMEM = (size_t)S * STAGE + TSUM * 4 + (2 * S + 2) * 8 + 16;
-};
-
-template <int M>
-struct RingCfg {
-  static constexpr int XB = kChunkI32 * 4;
-  static constexpr int STAGE = kBlockBytes + M * 2 * XB;
-  static constexpr int S = stages_for(STAGE);
-  static constexpr int V = 4 * 2 * M;
-  static constexpr int TSUM = kTileRows * 2 * M;
-  static constexpr size_t SMEM = (size_t)S * STAGE + TSUM * 8 + (2 * S + 2) * 8 + 16;
-};
+constexpr int kSmemLimit = 232448;  // dynamic shared memory per CTA on sm_100
+constexpr int kMaxStages = 12;
+constexpr int kTailBytes = 4608;    // tile result, barriers, flags, reduction scratch
 
 // Stream-K bookkeeping: CTA g owns units [b_g, b_{g+1}), b_g = floor(U g / G).
-__device__ __forceinline__ long long unit_begin(long long U, int G, int g) {
-  return U * g / G;
-}
+__device__ __forceinline__ long long unit_begin(long long U, int G, int g) { return U * g / G; }
 __device__ __forceinline__ int unit_owner(long long U, int G, long long u) {
   return (int)(((u + 1) * (long long)G - 1) / U);
 }
 
-// Reduce V per-lane values over the warp with a reduce-scatter butterfly. Afterwards this lane
-// holds `cnt` fully reduced values with flat indices [base, base+cnt); lanes with any bit of
-// `dup` set hold duplicates and must not write.
+// Reduce V (a power of two) per-lane values over the warp with a reduce-scatter butterfly.
+// Afterwards this lane holds `cnt` fully reduced values with flat indices [base, base+cnt); lanes
+// with any bit of `dup` set hold duplicates and must not write.
 template <typename T, int V>
 __device__ __forceinline__ void warp_reduce_scatter(T (&v)[V], int lane, int& base, int& cnt,
                                                     unsigned& dup) {
@@ -93,57 +74,14 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
 
 struct PipeSmem {
   uint8_t* stages;
+  int stage_bytes;
+  int S;
   uint64_t* full;
   uint64_t* empty;
-  uint64_t* cbar;  // consumer-group barrier (8 warp arrivals)
+  uint64_t* cbar;       // consumer-group barrier (8 warp arrivals)
   volatile int* flags;  // [0] abort, [1] last-arriver flag
+  float* red;           // 16 floats of block-reduction scratch
 };
-
-// Producer: one elected lane streams the weight block and the x chunks of every unit.
-template <int S, int STAGE, int M, int CHUNK, typename XT>
-__device__ void gemv_producer(const PipeSmem& sm, const uint8_t* W, const XT* Xc, const XT* Xs,
-                              int ldx, int K, int nKC, long long u0, long long u1, int* err) {
-  const uint64_t pol_w = l2_policy_evict_first();
-  const uint64_t pol_x = l2_policy_evict_last();
-  int i = 0;
-  long long u = u0;
-  for (; u < u1; ++u, ++i) {
-    const int s = i % S;
-    const uint32_t ph = (uint32_t)(i / S) & 1u;
-    if (i >= S) {
-      if (!mbar_wait_bounded(&sm.empty[s], ph ^ 1u)) {
-        atomicOr(err, SHD_DEVERR_TIMEOUT_EMPTY);
-        sm.flags[0] = 1;
-        break;
-      }
-    }
-    if (sm.flags[0]) break;
-    const int c = (int)(u % nKC);
-    const int rem = min(CHUNK, K - c * CHUNK);
-    const uint32_t xbytes = (uint32_t)rem * 4u;
-    uint8_t* st = sm.stages + (size_t)s * STAGE;
-    mbar_arrive_expect_tx(&sm.full[s], (uint32_t)kBlockBytes + (uint32_t)(M * 2) * xbytes);
-    bulk_g2s(st, W + (size_t)u * kBlockBytes, kBlockBytes, &sm.full[s], pol_w);
-#pragma unroll
-    for (int m = 0; m < M; ++m) {
-      bulk_g2s(st + kBlockBytes + (m * 2 + 0) * (CHUNK * 4), Xc + (size_t)m * ldx + (size_t)c * CHUNK,
-               xbytes, &sm.full[s], pol_x);
-      bulk_g2s(st + kBlockBytes + (m * 2 + 1) * (CHUNK * 4), Xs + (size_t)m * ldx + (size_t)c * CHUNK,
-               xbytes, &sm.full[s], pol_x);
-    }
-  }
-  if (u < u1) {
-    // Aborted: wait (bounded) for the last copy issued into every stage before leaving, so that no
-    // bulk copy lands in shared memory of a CTA that has exited.
-    const int issued = i;
-    for (int k = max(0, issued - S); k < issued; ++k) {
-      const int s = k % S;
-      if (!mbar_wait_bounded(&sm.full[s], (uint32_t)(k / S) & 1u)) {
-        atomicOr(err, SHD_DEVERR_TIMEOUT_DRAIN);
-      }
-    }
-  }
-}
 
 // Consumer-group barrier over the 8 consumer warps, bounded.
 __device__ __forceinline__ bool consumer_sync(const PipeSmem& sm, uint32_t& phase, int lane) {
@@ -152,6 +90,76 @@ __device__ __forceinline__ bool consumer_sync(const PipeSmem& sm, uint32_t& phas
   const bool ok = warp_wait(sm.cbar, phase);
   phase ^= 1u;
   return ok;
+}
+
+// Producer: one elected lane streams the weight block (and, unless the activations are resident,
+// the x chunks) of every unit. Weights for the first S units are requested before waiting on the
+// previous kernel (they do not depend on it); activation copies only after.
+template <int M, int CHUNK, typename XT>
+__device__ void gemv_producer(const PipeSmem& sm, const uint8_t* W, const XT* Xc, const XT* Xs,
+                              int ldx, int K, int nKC, long long u0, long long u1, bool staged_x,
+                              int* err) {
+  const uint64_t pol_w = l2_policy_evict_first();
+  const uint64_t pol_x = l2_policy_evict_last();
+  const int S = sm.S;
+  const long long n = u1 - u0;
+  const int npre = (int)std::min<long long>(S, n);
+  auto xbytes_of = [&](long long u) -> uint32_t {
+    const int c = (int)(u % nKC);
+    return (uint32_t)min(CHUNK, K - c * CHUNK) * 4u;
+  };
+  auto issue_x = [&](int s, long long u) {
+    const int c = (int)(u % nKC);
+    const uint32_t xb = xbytes_of(u);
+    uint8_t* st = sm.stages + (size_t)s * sm.stage_bytes;
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      bulk_g2s(st + kBlockBytes + (m * 2 + 0) * (CHUNK * 4), Xc + (size_t)m * ldx + (size_t)c * CHUNK, xb,
+               &sm.full[s], pol_x);
+      bulk_g2s(st + kBlockBytes + (m * 2 + 1) * (CHUNK * 4), Xs + (size_t)m * ldx + (size_t)c * CHUNK, xb,
+               &sm.full[s], pol_x);
+    }
+  };
+  // phase A: weights of the first npre units (no dependency on earlier kernels)
+  for (int i = 0; i < npre; ++i) {
+    const long long u = u0 + i;
+    const uint32_t tx = (uint32_t)kBlockBytes + (staged_x ? (uint32_t)(M * 2) * xbytes_of(u) : 0u);
+    mbar_arrive_expect_tx(&sm.full[i], tx);
+    bulk_g2s(sm.stages + (size_t)i * sm.stage_bytes, W + (size_t)u * kBlockBytes, kBlockBytes, &sm.full[i], pol_w);
+  }
+  if (staged_x) {
+    pdl_wait();
+    for (int i = 0; i < npre; ++i) issue_x(i, u0 + i);
+  }
+  // phase B: the rest, refilling stages as consumers release them
+  int s = 0;
+  uint32_t ph = 0;  // parity of the empty-barrier phase to wait for
+  long long i = npre;
+  for (; i < n; ++i) {
+    if (!mbar_wait_bounded(&sm.empty[s], ph)) {
+      atomicOr(err, SHD_DEVERR_TIMEOUT_EMPTY);
+      sm.flags[0] = 1;
+      break;
+    }
+    if (sm.flags[0]) break;
+    const long long u = u0 + i;
+    const uint32_t tx = (uint32_t)kBlockBytes + (staged_x ? (uint32_t)(M * 2) * xbytes_of(u) : 0u);
+    mbar_arrive_expect_tx(&sm.full[s], tx);
+    bulk_g2s(sm.stages + (size_t)s * sm.stage_bytes, W + (size_t)u * kBlockBytes, kBlockBytes, &sm.full[s], pol_w);
+    if (staged_x) issue_x(s, u);
+    if (++s == S) {
+      s = 0;
+      ph ^= 1u;
+    }
+  }
+  if (i < n) {
+    // Aborted: wait (bounded) for the last copy issued into every stage before leaving, so that no
+    // bulk copy lands in shared memory of a CTA that has exited.
+    for (long long k = std::max<long long>(0, i - S); k < i; ++k) {
+      const int ks = (int)(k % S);
+      if (!mbar_wait_bounded(&sm.full[ks], (uint32_t)((k / S) & 1))) atomicOr(err, SHD_DEVERR_TIMEOUT_DRAIN);
+    }
+  }
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -312,20 +320,157 @@ __device__ void epilogue_f32(const GemvArgs& a, int t, const float* tsum, int ct
   }
 }
 
+// Partial-tile exchange of stream-K. All consumer threads store this CTA's tile partial; one thread
+// publishes it with a release fence + counter increment; the last contributor reads every
+// contributor's partial (acquire) and sums them in CTA order into tsum. Returns 1 if this CTA must
+// run the epilogue, 0 if another CTA will, -1 on a barrier timeout.
+template <typename T>
+__device__ int split_tile_fixup(const PipeSmem& sm, uint32_t& cphase, T* tsum, T* partials,
+                                int* counters, int tsum_len, long long U, int G, int g, int t,
+                                int nKC, int first_tile, int ctid, int lane) {
+  const int slot = (t == first_tile) ? 0 : 1;
+  T* part = partials + ((size_t)g * 2 + slot) * tsum_len;
+  for (int k = ctid; k < tsum_len; k += kConsumerWarps * 32) part[k] = tsum[k];
+  if (!consumer_sync(sm, cphase, lane)) return -1;
+  const int gf = unit_owner(U, G, (long long)t * nKC);
+  const int gl = unit_owner(U, G, (long long)(t + 1) * nKC - 1);
+  if (ctid == 0) {
+    __threadfence();  // release: the CTA's partial (ordered before by the barrier) before the count
+    const int old = atomicAdd(&counters[t], 1);
+    const int last = (old == gl - gf);
+    if (last) {
+      counters[t] = 0;
+      __threadfence();  // acquire side of the other contributors' releases
+    }
+    sm.flags[1] = last;
+  }
+  if (!consumer_sync(sm, cphase, lane)) return -1;
+  if (!sm.flags[1]) return 0;
+  for (int k = ctid; k < tsum_len; k += kConsumerWarps * 32) {
+    T sum = T(0);
+    for (int gg = gf; gg <= gl; ++gg) {
+      const int ft = (int)(unit_begin(U, G, gg) / nKC);
+      const int sl = (t == ft) ? 0 : 1;
+      const T v = __ldcg(partials + ((size_t)gg * 2 + sl) * tsum_len + k);
+      sum = (gg == gf) ? v : sum + v;
+    }
+    tsum[k] = sum;
+  }
+  if (!consumer_sync(sm, cphase, lane)) return -1;
+  return 1;
+}
+
+// ---- packed f32x2 helpers ----
+__device__ __forceinline__ unsigned long long pack2(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float sum2(unsigned long long v) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+  return lo + hi;
+}
+__device__ __forceinline__ void fma2(unsigned long long& acc, unsigned long long w, unsigned long long x) {
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(w), "l"(x));
+}
+__device__ __forceinline__ unsigned long long bf16pair(uint32_t q) {
+  return pack2(__uint_as_float(q << 16), __uint_as_float(q & 0xffff0000u));
+}
+
+// RMSNorm prologue: x = reshare(RMSNorm(D + H)) for M rows into xres[m][share][KP] (zero padded).
+// Every CTA computes the identical values (same thread mapping, fixed reduction order).
+template <int M>
+__device__ bool norm_prologue(const GemvArgs& a, const PipeSmem& sm, uint32_t& cphase, float* xres,
+                              int KP, int ctid, int lane, int warp, bool write_h) {
+  const int K = a.K;
+  const int K4 = K >> 2;
+  for (int m = 0; m < M; ++m) {
+    const float4* hc = reinterpret_cast<const float4*>(a.nHc + (size_t)m * a.n_ldh);
+    const float4* hs = reinterpret_cast<const float4*>(a.nHs + (size_t)m * a.n_ldh);
+    const float4* dc = a.nDc ? reinterpret_cast<const float4*>(a.nDc + (size_t)m * a.n_ldh) : nullptr;
+    const float4* ds = a.nDs ? reinterpret_cast<const float4*>(a.nDs + (size_t)m * a.n_ldh) : nullptr;
+    float4* oc = (write_h && a.nHout_c) ? reinterpret_cast<float4*>(a.nHout_c + (size_t)m * a.n_ldh) : nullptr;
+    float4* os = (write_h && a.nHout_s) ? reinterpret_cast<float4*>(a.nHout_s + (size_t)m * a.n_ldh) : nullptr;
+    float* xr = xres + (size_t)(m * 2) * KP;
+    float ss = 0.0f;
+    for (int i = ctid; i < K4; i += kConsumerWarps * 32) {
+      float4 c = hc[i], s = hs[i];
+      if (dc) {
+        const float4 e = dc[i], f = ds[i];
+        c = make_float4(__fadd_rn(e.x, c.x), __fadd_rn(e.y, c.y), __fadd_rn(e.z, c.z), __fadd_rn(e.w, c.w));
+        s = make_float4(__fadd_rn(f.x, s.x), __fadd_rn(f.y, s.y), __fadd_rn(f.z, s.z), __fadd_rn(f.w, s.w));
+        if (oc) {
+          oc[i] = c;
+          os[i] = s;
+        }
+      }
+      const float4 x = make_float4(__fadd_rn(c.x, s.x), __fadd_rn(c.y, s.y), __fadd_rn(c.z, s.z), __fadd_rn(c.w, s.w));
+      reinterpret_cast<float4*>(xr)[i] = x;
+      ss = __fmaf_rn(x.x, x.x, ss);
+      ss = __fmaf_rn(x.y, x.y, ss);
+      ss = __fmaf_rn(x.z, x.z, ss);
+      ss = __fmaf_rn(x.w, x.w, ss);
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+    if (lane == 0) sm.red[warp] = ss;
+    if (!consumer_sync(sm, cphase, lane)) return false;
+    float sum_sq = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) sum_sq = __fadd_rn(sum_sq, sm.red[w]);
+    const float mean_sq = __fdiv_rn(sum_sq, (float)K);
+    float inv;
+    if (a.nvariant == SHD_NL_GPU) {
+      inv = rsqrtf(__fadd_rn(mean_sq, a.eps));
+    } else {
+      const float rms = __fsqrt_rn(__fadd_rn(mean_sq, a.eps));
+      if (a.nvariant == SHD_NL_MPC)
+        inv = (rms > 1e-6f && isfinite(rms)) ? __fdiv_rn(1.0f, rms) : 1.0f;
+      else
+        inv = __fdiv_rn(1.0f, rms);
+    }
+    const float* mk = a.nmask ? a.nmask + (size_t)m * a.n_ldmask : nullptr;
+    for (int i = ctid; i < KP; i += kConsumerWarps * 32) {
+      float xc = 0.0f, xs = 0.0f;
+      if (i < K) {
+        float r = __fmul_rn(__fmul_rn(xr[i], inv), a.gamma[i]);
+        if (a.nvariant == SHD_NL_MPC && !isfinite(r)) r = 0.0f;
+        const float mv = mk ? mk[i] : 0.0f;
+        xc = __fsub_rn(r, mv);
+        xs = mv;
+      }
+      xr[i] = xc;
+      xr[KP + i] = xs;
+    }
+    if (!consumer_sync(sm, cphase, lane)) return false;  // red reuse and xres visibility
+  }
+  return true;
+}
+
 // ------------------------------------------------------------------------------------------------
 // f32-share GEMV kernel (bf16 weights)
 // ------------------------------------------------------------------------------------------------
-template <int M, int EPI>
+template <int M, int EPI, bool NORM>
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_f32_kernel(const __grid_constant__ GemvArgs a) {
-  using C = F32Cfg<M>;
+  constexpr bool USE2 = (M <= 4);
+  constexpr int V = 4 * 2 * M;
+  constexpr int VP = (V <= 8) ? 8 : (V <= 16) ? 16 : (V <= 32) ? 32 : 64;
+  constexpr int TSUM = kTileRows * 2 * M;
   extern __shared__ __align__(1024) uint8_t smem[];
+  const int S = a.nstages;
+  const int KP = a.nKC * kChunkBf16;
   PipeSmem sm;
   sm.stages = smem;
-  float* tsum = reinterpret_cast<float*>(smem + (size_t)C::S * C::STAGE);
-  sm.full = reinterpret_cast<uint64_t*>(tsum + C::TSUM);
-  sm.empty = sm.full + C::S;
-  sm.cbar = sm.empty + C::S;
+  sm.S = S;
+  sm.stage_bytes = kBlockBytes + (NORM ? 0 : M * 2 * kChunkBf16 * 4);
+  float* xres = reinterpret_cast<float*>(smem + (size_t)S * sm.stage_bytes);
+  float* tsum = xres + (NORM ? (size_t)M * 2 * KP : 0);
+  sm.full = reinterpret_cast<uint64_t*>(tsum + TSUM);
+  sm.empty = sm.full + S;
+  sm.cbar = sm.empty + S;
   sm.flags = reinterpret_cast<volatile int*>(sm.cbar + 2);
+  sm.red = reinterpret_cast<float*>(sm.cbar + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long U = (long long)a.nT * a.nKC;
@@ -333,7 +478,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_f32_kernel(const __grid_
   const long long u0 = unit_begin(U, G, g), u1 = unit_begin(U, G, g + 1);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < C::S; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(&sm.full[s], 1);
       mbar_init(&sm.empty[s], kConsumerWarps);
     }
@@ -343,138 +488,175 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_f32_kernel(const __grid_
     mbar_fence_init();
   }
   __syncthreads();
+  if (threadIdx.x == 0) pdl_trigger();
 
   if (warp == kConsumerWarps) {
     if (lane == 0)
-      gemv_producer<C::S, C::STAGE, M, kChunkBf16, float>(sm, a.W, a.Xc, a.Xs, a.ldx, a.K, a.nKC,
-                                                          u0, u1, a.err);
+      gemv_producer<M, kChunkBf16, float>(sm, a.W, a.Xc, a.Xs, a.ldx, a.K, a.nKC, u0, u1, !NORM, a.err);
     return;
   }
 
   const int ctid = threadIdx.x;  // 0..255 among consumers
-  const int first_tile = (int)(u0 / a.nKC);
   uint32_t cphase = 0;
-  float acc[C::V];
-#pragma unroll
-  for (int j = 0; j < C::V; ++j) acc[j] = 0.f;
+  pdl_wait();  // activations, positions and scratch come from earlier kernels
+  if constexpr (NORM) {
+    if (!norm_prologue<M>(a, sm, cphase, xres, KP, ctid, lane, warp, g == 0)) {
+      if (lane == 0) atomicOr(a.err, SHD_DEVERR_TIMEOUT_FULL);
+      sm.flags[0] = 1;
+      return;
+    }
+  }
 
-  int i = 0;
-  for (long long u = u0; u < u1; ++u, ++i) {
-    const int s = i % C::S;
-    const uint32_t ph = (uint32_t)(i / C::S) & 1u;
+  const int first_tile = (int)(u0 / a.nKC);
+  unsigned long long acc2[USE2 ? V : 1];
+  float acc[VP];
+#pragma unroll
+  for (int j = 0; j < VP; ++j) acc[j] = 0.f;
+  if constexpr (USE2) {
+#pragma unroll
+    for (int j = 0; j < V; ++j) acc2[j] = 0ull;
+  }
+
+  int t = first_tile, c = (int)(u0 % a.nKC);
+  int s = 0;
+  uint32_t ph = 0;
+  for (long long u = u0; u < u1; ++u) {
     if (!warp_wait(&sm.full[s], ph)) {
       if (lane == 0) atomicOr(a.err, SHD_DEVERR_TIMEOUT_FULL);
       sm.flags[0] = 1;
       return;
     }
-    const int t = (int)(u / a.nKC), c = (int)(u % a.nKC);
-    const uint8_t* st = sm.stages + (size_t)s * C::STAGE;
-    const float* xsm = reinterpret_cast<const float*>(st + kBlockBytes);
-    const bool okA = c * kChunkBf16 + 4 * lane < a.K;
-    const bool okB = c * kChunkBf16 + 128 + 4 * lane < a.K;
+    const uint8_t* st = sm.stages + (size_t)s * sm.stage_bytes;
     const uint4* wv = reinterpret_cast<const uint4*>(st);
-    float wf[4][8];
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const uint4 q = wv[(warp * 4 + r) * 32 + lane];
-      wf[r][0] = bf16lo_to_f32(q.x);
-      wf[r][1] = bf16hi_to_f32(q.x);
-      wf[r][2] = bf16lo_to_f32(q.y);
-      wf[r][3] = bf16hi_to_f32(q.y);
-      wf[r][4] = bf16lo_to_f32(q.z);
-      wf[r][5] = bf16hi_to_f32(q.z);
-      wf[r][6] = bf16lo_to_f32(q.w);
-      wf[r][7] = bf16hi_to_f32(q.w);
+    // activation chunk: resident (zero padded) or staged with the block (masked at the K tail)
+    const float* xbase;
+    int xstride;
+    bool okA = true, okB = true;
+    if constexpr (NORM) {
+      xbase = xres + (size_t)c * kChunkBf16;
+      xstride = KP;
+    } else {
+      xbase = reinterpret_cast<const float*>(st + kBlockBytes);
+      xstride = kChunkBf16;
+      okA = c * kChunkBf16 + 4 * lane < a.K;
+      okB = c * kChunkBf16 + 128 + 4 * lane < a.K;
     }
     const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if constexpr (USE2) {
+      unsigned long long w2[4][4];
 #pragma unroll
-    for (int m = 0; m < M; ++m)
-#pragma unroll
-      for (int sh = 0; sh < 2; ++sh) {
-        const float* xp = xsm + (m * 2 + sh) * kChunkBf16;
-        const float4 xa = okA ? *reinterpret_cast<const float4*>(xp + 4 * lane) : z4;
-        const float4 xb = okB ? *reinterpret_cast<const float4*>(xp + 128 + 4 * lane) : z4;
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          float v = acc[(r * 2 + sh) * M + m];
-          v = fmaf(wf[r][0], xa.x, v);
-          v = fmaf(wf[r][1], xa.y, v);
-          v = fmaf(wf[r][2], xa.z, v);
-          v = fmaf(wf[r][3], xa.w, v);
-          v = fmaf(wf[r][4], xb.x, v);
-          v = fmaf(wf[r][5], xb.y, v);
-          v = fmaf(wf[r][6], xb.z, v);
-          v = fmaf(wf[r][7], xb.w, v);
-          acc[(r * 2 + sh) * M + m] = v;
-        }
+      for (int r = 0; r < 4; ++r) {
+        const uint4 q = wv[(warp * 4 + r) * 32 + lane];
+        w2[r][0] = bf16pair(q.x);
+        w2[r][1] = bf16pair(q.y);
+        w2[r][2] = bf16pair(q.z);
+        w2[r][3] = bf16pair(q.w);
       }
+#pragma unroll
+      for (int m = 0; m < M; ++m)
+#pragma unroll
+        for (int sh = 0; sh < 2; ++sh) {
+          const float* xp = xbase + (size_t)(m * 2 + sh) * xstride;
+          const float4 xa = okA ? *reinterpret_cast<const float4*>(xp + 4 * lane) : z4;
+          const float4 xb = okB ? *reinterpret_cast<const float4*>(xp + 128 + 4 * lane) : z4;
+          const unsigned long long x0 = pack2(xa.x, xa.y), x1 = pack2(xa.z, xa.w);
+          const unsigned long long x2 = pack2(xb.x, xb.y), x3 = pack2(xb.z, xb.w);
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            unsigned long long& A = acc2[(r * 2 + sh) * M + m];
+            fma2(A, w2[r][0], x0);
+            fma2(A, w2[r][1], x1);
+            fma2(A, w2[r][2], x2);
+            fma2(A, w2[r][3], x3);
+          }
+        }
+    } else {
+      float wf[4][8];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const uint4 q = wv[(warp * 4 + r) * 32 + lane];
+        wf[r][0] = bf16lo_to_f32(q.x);
+        wf[r][1] = bf16hi_to_f32(q.x);
+        wf[r][2] = bf16lo_to_f32(q.y);
+        wf[r][3] = bf16hi_to_f32(q.y);
+        wf[r][4] = bf16lo_to_f32(q.z);
+        wf[r][5] = bf16hi_to_f32(q.z);
+        wf[r][6] = bf16lo_to_f32(q.w);
+        wf[r][7] = bf16hi_to_f32(q.w);
+      }
+#pragma unroll
+      for (int m = 0; m < M; ++m)
+#pragma unroll
+        for (int sh = 0; sh < 2; ++sh) {
+          const float* xp = xbase + (size_t)(m * 2 + sh) * xstride;
+          const float4 xa = okA ? *reinterpret_cast<const float4*>(xp + 4 * lane) : z4;
+          const float4 xb = okB ? *reinterpret_cast<const float4*>(xp + 128 + 4 * lane) : z4;
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            float v = acc[(r * 2 + sh) * M + m];
+            v = fmaf(wf[r][0], xa.x, v);
+            v = fmaf(wf[r][1], xa.y, v);
+            v = fmaf(wf[r][2], xa.z, v);
+            v = fmaf(wf[r][3], xa.w, v);
+            v = fmaf(wf[r][4], xb.x, v);
+            v = fmaf(wf[r][5], xb.y, v);
+            v = fmaf(wf[r][6], xb.z, v);
+            v = fmaf(wf[r][7], xb.w, v);
+            acc[(r * 2 + sh) * M + m] = v;
+          }
+        }
+    }
     __syncwarp();
     if (lane == 0) mbar_arrive(&sm.empty[s]);
+    if (++s == S) {
+      s = 0;
+      ph ^= 1u;
+    }
 
-    const bool tile_end = (c == a.nKC - 1) || (u == u1 - 1);
+    const int ct = t, cc = c;
+    if (++c == a.nKC) {
+      c = 0;
+      ++t;
+    }
+    const bool tile_end = (cc == a.nKC - 1) || (u == u1 - 1);
     if (!tile_end) continue;
 
-    // ---- this CTA's contribution to tile t is complete ----
+    // ---- this CTA's contribution to tile ct is complete ----
+    if constexpr (USE2) {
+#pragma unroll
+      for (int j = 0; j < V; ++j) {
+        acc[j] = sum2(acc2[j]);
+        acc2[j] = 0ull;
+      }
+    }
     int base, cnt;
     unsigned dup;
-    warp_reduce_scatter<float, C::V>(acc, lane, base, cnt, dup);
+    warp_reduce_scatter<float, VP>(acc, lane, base, cnt, dup);
     if ((lane & dup) == 0) {
 #pragma unroll
-      for (int j = 0; j < C::V; ++j)
-        if (j < cnt) tsum[warp * C::V + base + j] = acc[j];
+      for (int j = 0; j < VP; ++j)
+        if (j < cnt && base + j < V) tsum[warp * V + base + j] = acc[j];
     }
 #pragma unroll
-    for (int j = 0; j < C::V; ++j) acc[j] = 0.f;
+    for (int j = 0; j < VP; ++j) acc[j] = 0.f;
 
-    const bool full_tile = ((long long)t * a.nKC >= u0) && (c == a.nKC - 1);
+    const bool full_tile = ((long long)ct * a.nKC >= u0) && (cc == a.nKC - 1);
     if (!consumer_sync(sm, cphase, lane)) {
       if (lane == 0) atomicOr(a.err, SHD_DEVERR_TIMEOUT_FULL);
       sm.flags[0] = 1;
       return;
     }
     if (!full_tile) {
-      const int slot = (t == first_tile) ? 0 : 1;
-      float* part = a.partials + ((size_t)g * 2 + slot) * C::TSUM;
-      for (int k = ctid; k < C::TSUM; k += kConsumerWarps * 32) part[k] = tsum[k];
-      __threadfence();
-      if (!consumer_sync(sm, cphase, lane)) {
+      const int r = split_tile_fixup<float>(sm, cphase, tsum, a.partials, a.counters, TSUM, U, G, g, ct,
+                                            a.nKC, first_tile, ctid, lane);
+      if (r < 0) {
         if (lane == 0) atomicOr(a.err, SHD_DEVERR_TIMEOUT_FULL);
         sm.flags[0] = 1;
         return;
       }
-      const int gf = unit_owner(U, G, (long long)t * a.nKC);
-      const int gl = unit_owner(U, G, (long long)(t + 1) * a.nKC - 1);
-      if (ctid == 0) {
-        const int old = atomicAdd(&a.counters[t], 1);
-        const int last = (old == gl - gf);
-        if (last) a.counters[t] = 0;
-        sm.flags[1] = last;
-      }
-      if (!consumer_sync(sm, cphase, lane)) {
-        if (lane == 0) atomicOr(a.err, SHD_DEVERR_TIMEOUT_FULL);
-        sm.flags[0] = 1;
-        return;
-      }
-      const bool last = sm.flags[1] != 0;
-      if (!last) continue;
-      __threadfence();
-      for (int k = ctid; k < C::TSUM; k += kConsumerWarps * 32) {
-        float sum = 0.f;
-        for (int gg = gf; gg <= gl; ++gg) {
-          const int ft = (int)(unit_begin(U, G, gg) / a.nKC);
-          const int sl = (t == ft) ? 0 : 1;
-          sum = (gg == gf) ? __ldcg(a.partials + ((size_t)gg * 2 + sl) * C::TSUM + k)
-                           : __fadd_rn(sum, __ldcg(a.partials + ((size_t)gg * 2 + sl) * C::TSUM + k));
-        }
-        tsum[k] = sum;
-      }
-      if (!consumer_sync(sm, cphase, lane)) {
-        if (lane == 0) atomicOr(a.err, SHD_DEVERR_TIMEOUT_FULL);
-        sm.flags[0] = 1;
-        return;
-      }
+      if (r == 0) continue;
     }
-    epilogue_f32<M, EPI>(a, t, tsum, ctid, a.err);
+    epilogue_f32<M, EPI>(a, ct, tsum, ctid, a.err);
     if (!consumer_sync(sm, cphase, lane)) {
       if (lane == 0) atomicOr(a.err, SHD_DEVERR_TIMEOUT_FULL);
       sm.flags[0] = 1;
@@ -489,15 +671,23 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_f32_kernel(const __grid_
 // ------------------------------------------------------------------------------------------------
 template <int M>
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_ring_kernel(const __grid_constant__ RingArgs a) {
-  using C = RingCfg<M>;
+  constexpr int V = 4 * 2 * M;  // M in {1, 2, 4, 8}: a power of two
+  constexpr int TSUM = kTileRows * 2 * M;
   extern __shared__ __align__(1024) uint8_t smem[];
   PipeSmem sm;
   sm.stages = smem;
-  long long* tsum = reinterpret_cast<long long*>(smem + (size_t)C::S * C::STAGE);
-  sm.full = reinterpret_cast<uint64_t*>(tsum + C::TSUM);
-  sm.empty = sm.full + C::S;
-  sm.cbar = sm.empty + C::S;
+  sm.stage_bytes = kBlockBytes + M * 2 * kChunkI32 * 4;
+  {
+    const int fit = (kSmemLimit - kTailBytes) / sm.stage_bytes;
+    sm.S = fit < kMaxStages ? fit : kMaxStages;
+  }
+  const int S = sm.S;
+  long long* tsum = reinterpret_cast<long long*>(smem + (size_t)S * sm.stage_bytes);
+  sm.full = reinterpret_cast<uint64_t*>(tsum + TSUM);
+  sm.empty = sm.full + S;
+  sm.cbar = sm.empty + S;
   sm.flags = reinterpret_cast<volatile int*>(sm.cbar + 2);
+  sm.red = reinterpret_cast<float*>(sm.cbar + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long U = (long long)a.nT * a.nKC;
@@ -505,7 +695,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_ring_kernel(const __grid
   const long long u0 = unit_begin(U, G, g), u1 = unit_begin(U, G, g + 1);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < C::S; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(&sm.full[s], 1);
       mbar_init(&sm.empty[s], kConsumerWarps);
     }
@@ -515,32 +705,31 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_ring_kernel(const __grid
     mbar_fence_init();
   }
   __syncthreads();
+  if (threadIdx.x == 0) pdl_trigger();
 
   if (warp == kConsumerWarps) {
-    if (lane == 0)
-      gemv_producer<C::S, C::STAGE, M, kChunkI32, int32_t>(sm, a.W, a.Xc, a.Xs, a.ldx, a.K, a.nKC,
-                                                           u0, u1, a.err);
+    if (lane == 0) gemv_producer<M, kChunkI32, int32_t>(sm, a.W, a.Xc, a.Xs, a.ldx, a.K, a.nKC, u0, u1, true, a.err);
     return;
   }
 
   const int ctid = threadIdx.x;
+  pdl_wait();
   const int first_tile = (int)(u0 / a.nKC);
   uint32_t cphase = 0;
-  long long acc[C::V];
+  long long acc[V];
 #pragma unroll
-  for (int j = 0; j < C::V; ++j) acc[j] = 0;
+  for (int j = 0; j < V; ++j) acc[j] = 0;
 
-  int i = 0;
-  for (long long u = u0; u < u1; ++u, ++i) {
-    const int s = i % C::S;
-    const uint32_t ph = (uint32_t)(i / C::S) & 1u;
+  int t = first_tile, c = (int)(u0 % a.nKC);
+  int s = 0;
+  uint32_t ph = 0;
+  for (long long u = u0; u < u1; ++u) {
     if (!warp_wait(&sm.full[s], ph)) {
       if (lane == 0) atomicOr(a.err, SHD_DEVERR_TIMEOUT_FULL);
       sm.flags[0] = 1;
       return;
     }
-    const int t = (int)(u / a.nKC), c = (int)(u % a.nKC);
-    const uint8_t* st = sm.stages + (size_t)s * C::STAGE;
+    const uint8_t* st = sm.stages + (size_t)s * sm.stage_bytes;
     const int32_t* xsm = reinterpret_cast<const int32_t*>(st + kBlockBytes);
     const bool ok = c * kChunkI32 + 4 * lane < a.K;
     const int4* wv = reinterpret_cast<const int4*>(st);
@@ -565,71 +754,49 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_ring_kernel(const __grid
       }
     __syncwarp();
     if (lane == 0) mbar_arrive(&sm.empty[s]);
-
-    const bool tile_end = (c == a.nKC - 1) || (u == u1 - 1);
+    if (++s == S) {
+      s = 0;
+      ph ^= 1u;
+    }
+    const int ct = t, cc = c;
+    if (++c == a.nKC) {
+      c = 0;
+      ++t;
+    }
+    const bool tile_end = (cc == a.nKC - 1) || (u == u1 - 1);
     if (!tile_end) continue;
 
     int base, cnt;
     unsigned dup;
-    warp_reduce_scatter<long long, C::V>(acc, lane, base, cnt, dup);
+    warp_reduce_scatter<long long, V>(acc, lane, base, cnt, dup);
     if ((lane & dup) == 0) {
 #pragma unroll
-      for (int j = 0; j < C::V; ++j)
-        if (j < cnt) tsum[warp * C::V + base + j] = acc[j];
+      for (int j = 0; j < V; ++j)
+        if (j < cnt) tsum[warp * V + base + j] = acc[j];
     }
 #pragma unroll
-    for (int j = 0; j < C::V; ++j) acc[j] = 0;
+    for (int j = 0; j < V; ++j) acc[j] = 0;
 
-    const bool full_tile = ((long long)t * a.nKC >= u0) && (c == a.nKC - 1);
+    const bool full_tile = ((long long)ct * a.nKC >= u0) && (cc == a.nKC - 1);
     if (!consumer_sync(sm, cphase, lane)) {
       if (lane == 0) atomicOr(a.err, SHD_DEVERR_TIMEOUT_FULL);
       sm.flags[0] = 1;
       return;
     }
     if (!full_tile) {
-      const int slot = (t == first_tile) ? 0 : 1;
-      long long* part = a.partials + ((size_t)g * 2 + slot) * C::TSUM;
-      for (int k = ctid; k < C::TSUM; k += kConsumerWarps * 32) part[k] = tsum[k];
-      __threadfence();
-      if (!consumer_sync(sm, cphase, lane)) {
+      const int r = split_tile_fixup<long long>(sm, cphase, tsum, a.partials, a.counters, TSUM, U, G, g, ct,
+                                                a.nKC, first_tile, ctid, lane);
+      if (r < 0) {
         if (lane == 0) atomicOr(a.err, SHD_DEVERR_TIMEOUT_FULL);
         sm.flags[0] = 1;
         return;
       }
-      const int gf = unit_owner(U, G, (long long)t * a.nKC);
-      const int gl = unit_owner(U, G, (long long)(t + 1) * a.nKC - 1);
-      if (ctid == 0) {
-        const int old = atomicAdd(&a.counters[t], 1);
-        const int last = (old == gl - gf);
-        if (last) a.counters[t] = 0;
-        sm.flags[1] = last;
-      }
-      if (!consumer_sync(sm, cphase, lane)) {
-        if (lane == 0) atomicOr(a.err, SHD_DEVERR_TIMEOUT_FULL);
-        sm.flags[0] = 1;
-        return;
-      }
-      if (!sm.flags[1]) continue;
-      __threadfence();
-      for (int k = ctid; k < C::TSUM; k += kConsumerWarps * 32) {
-        long long sum = 0;
-        for (int gg = gf; gg <= gl; ++gg) {
-          const int ft = (int)(unit_begin(U, G, gg) / a.nKC);
-          const int sl = (t == ft) ? 0 : 1;
-          sum += __ldcg(a.partials + ((size_t)gg * 2 + sl) * C::TSUM + k);
-        }
-        tsum[k] = sum;
-      }
-      if (!consumer_sync(sm, cphase, lane)) {
-        if (lane == 0) atomicOr(a.err, SHD_DEVERR_TIMEOUT_FULL);
-        sm.flags[0] = 1;
-        return;
-      }
+      if (r == 0) continue;
     }
     // epilogue: arithmetic shift of the wrapped 64-bit sum, truncation to i32, wrapping bias add
     for (int idx = ctid; idx < kTileRows * M; idx += kConsumerWarps * 32) {
       const int r = idx % kTileRows, m = idx / kTileRows;
-      const int n = t * kTileRows + r;
+      const int n = ct * kTileRows + r;
       if (n >= a.N) continue;
       const int32_t yc = (int32_t)(tsum[(r * 2 + 0) * M + m] >> a.scale);
       int32_t ys = (int32_t)(tsum[(r * 2 + 1) * M + m] >> a.scale);
@@ -648,34 +815,49 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_ring_kernel(const __grid
 // ------------------------------------------------------------------------------------------------
 // Launchers
 // ------------------------------------------------------------------------------------------------
-template <int M, int EPI>
-static int launch_f32_t(shd_ctx* ctx, const shd_weight* w, GemvArgs a) {
-  using C = F32Cfg<M>;
-  static unsigned attr_devices = 0;  // bit d: attribute set on device d
-  if (!(attr_devices & (1u << (ctx->device & 31)))) {
-    SHD_CHECK_CUDA(ctx, cudaFuncSetAttribute(gemv_f32_kernel<M, EPI>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM));
-    attr_devices |= 1u << (ctx->device & 31);
+template <typename Kern>
+static int set_smem_attr(shd_ctx* ctx, Kern kernel, unsigned& devices) {
+  if (!(devices & (1u << (ctx->device & 31)))) {
+    SHD_CHECK_CUDA(ctx, cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
+    devices |= 1u << (ctx->device & 31);
   }
-  const long long U = (long long)w->nT * w->nKC;
-  const int G = (int)std::min<long long>(U, ctx->num_sms);
-  gemv_f32_kernel<M, EPI><<<G, kGemvThreads, C::SMEM, ctx->stream>>>(a);
-  SHD_CHECK_LAUNCH(ctx, "gemv_f32_kernel");
   return SHD_OK;
 }
 
-template <int EPI>
+template <int M, int EPI, bool NORM>
+static int launch_f32_t(shd_ctx* ctx, const shd_weight* w, GemvArgs a) {
+  static unsigned attr_devices = 0;
+  const int rc = set_smem_attr(ctx, gemv_f32_kernel<M, EPI, NORM>, attr_devices);
+  if (rc) return rc;
+  const int stage = kBlockBytes + (NORM ? 0 : M * 2 * kChunkBf16 * 4);
+  const size_t xres = NORM ? (size_t)M * 2 * w->nKC * kChunkBf16 * 4 : 0;
+  const long long avail = (long long)kSmemLimit - kTailBytes - (long long)xres;
+  a.nstages = (int)std::min<long long>(kMaxStages, avail / stage);
+  if (a.nstages < 2) return shd_fail(ctx, SHD_ERR_ARG, "gemv: activation vector too long for the fused norm");
+  const size_t smem = (size_t)a.nstages * stage + xres + kTailBytes;
+  const long long U = (long long)w->nT * w->nKC;
+  const int G = (int)std::min<long long>(U, ctx->num_sms);
+  SHD_CHECK_CUDA(ctx, launch_pdl(gemv_f32_kernel<M, EPI, NORM>, dim3(G), dim3(kGemvThreads), smem, ctx->stream, a));
+  ctx->launches++;
+  return SHD_OK;
+}
+
+template <int EPI, bool NORM>
 static int launch_f32_m(shd_ctx* ctx, const shd_weight* w, int M, GemvArgs a) {
   switch (M) {
-    case 1: return launch_f32_t<1, EPI>(ctx, w, a);
-    case 2: return launch_f32_t<2, EPI>(ctx, w, a);
-    case 4: return launch_f32_t<4, EPI>(ctx, w, a);
-    case 8: return launch_f32_t<8, EPI>(ctx, w, a);
-    default: return shd_fail(ctx, SHD_ERR_ARG, "gemv: M must be 1, 2, 4 or 8 for one launch");
+    case 1: return launch_f32_t<1, EPI, NORM>(ctx, w, a);
+    case 2: return launch_f32_t<2, EPI, NORM>(ctx, w, a);
+    case 3: return launch_f32_t<3, EPI, NORM>(ctx, w, a);
+    case 4: return launch_f32_t<4, EPI, NORM>(ctx, w, a);
+    case 5: return launch_f32_t<5, EPI, NORM>(ctx, w, a);
+    case 6: return launch_f32_t<6, EPI, NORM>(ctx, w, a);
+    case 7: return launch_f32_t<7, EPI, NORM>(ctx, w, a);
+    case 8: return launch_f32_t<8, EPI, NORM>(ctx, w, a);
+    default: return shd_fail(ctx, SHD_ERR_ARG, "gemv: M must be 1..8 for one launch");
   }
 }
 
-int launch_gemv_f32(shd_ctx* ctx, const shd_weight* w, int M, int epi, GemvArgs a) {
+int launch_gemv_f32(shd_ctx* ctx, const shd_weight* w, int M, int epi, GemvArgs a, bool norm) {
   a.W = reinterpret_cast<const uint8_t*>(w->d_tiles);
   a.N = w->N;
   a.K = (w->K + 3) / 4 * 4;  // x extent copied per row (rows padded to 16 bytes)
@@ -684,29 +866,39 @@ int launch_gemv_f32(shd_ctx* ctx, const shd_weight* w, int M, int epi, GemvArgs 
   a.partials = ctx->d_partials;
   a.counters = ctx->d_counters;
   a.err = ctx->d_err;
-  if (w->nT > ctx->n_counters) return shd_fail(ctx, SHD_ERR_ARG, "gemv: too many row tiles");
+  if (w->nT > ctx->n_counters - 8192) return shd_fail(ctx, SHD_ERR_ARG, "gemv: too many row tiles");
+  if (norm) {
+    if (w->K % 4 != 0) return shd_fail(ctx, SHD_ERR_ARG, "gemv: fused norm needs in_features % 4 == 0");
+    a.K = w->K;
+    switch (epi) {
+      case EPI_STORE: return launch_f32_m<EPI_STORE, true>(ctx, w, M, a);
+      case EPI_QKV: return launch_f32_m<EPI_QKV, true>(ctx, w, M, a);
+      case EPI_GATEUP: return launch_f32_m<EPI_GATEUP, true>(ctx, w, M, a);
+      case EPI_LOGITS: return launch_f32_m<EPI_LOGITS, true>(ctx, w, M, a);
+      default: return shd_fail(ctx, SHD_ERR_ARG, "gemv: unknown epilogue");
+    }
+  }
   switch (epi) {
-    case EPI_STORE: return launch_f32_m<EPI_STORE>(ctx, w, M, a);
-    case EPI_QKV: return launch_f32_m<EPI_QKV>(ctx, w, M, a);
-    case EPI_GATEUP: return launch_f32_m<EPI_GATEUP>(ctx, w, M, a);
-    case EPI_LOGITS: return launch_f32_m<EPI_LOGITS>(ctx, w, M, a);
+    case EPI_STORE: return launch_f32_m<EPI_STORE, false>(ctx, w, M, a);
+    case EPI_QKV: return launch_f32_m<EPI_QKV, false>(ctx, w, M, a);
+    case EPI_GATEUP: return launch_f32_m<EPI_GATEUP, false>(ctx, w, M, a);
+    case EPI_LOGITS: return launch_f32_m<EPI_LOGITS, false>(ctx, w, M, a);
     default: return shd_fail(ctx, SHD_ERR_ARG, "gemv: unknown epilogue");
   }
 }
 
 template <int M>
 static int launch_ring_t(shd_ctx* ctx, const shd_weight* w, RingArgs a) {
-  using C = RingCfg<M>;
   static unsigned attr_devices = 0;
-  if (!(attr_devices & (1u << (ctx->device & 31)))) {
-    SHD_CHECK_CUDA(ctx, cudaFuncSetAttribute(gemv_ring_kernel<M>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM));
-    attr_devices |= 1u << (ctx->device & 31);
-  }
+  const int rc = set_smem_attr(ctx, gemv_ring_kernel<M>, attr_devices);
+  if (rc) return rc;
+  const int stage = kBlockBytes + M * 2 * kChunkI32 * 4;
+  const int S = std::min(kMaxStages, (kSmemLimit - kTailBytes) / stage);
+  const size_t smem = (size_t)S * stage + kTailBytes;
   const long long U = (long long)w->nT * w->nKC;
   const int G = (int)std::min<long long>(U, ctx->num_sms);
-  gemv_ring_kernel<M><<<G, kGemvThreads, C::SMEM, ctx->stream>>>(a);
-  SHD_CHECK_LAUNCH(ctx, "gemv_ring_kernel");
+  SHD_CHECK_CUDA(ctx, launch_pdl(gemv_ring_kernel<M>, dim3(G), dim3(kGemvThreads), smem, ctx->stream, a));
+  ctx->launches++;
   return SHD_OK;
 }
 
@@ -719,7 +911,7 @@ int launch_gemv_ring(shd_ctx* ctx, const shd_weight* w, int M, RingArgs a) {
   a.partials = reinterpret_cast<long long*>(ctx->d_partials);
   a.counters = ctx->d_counters;
   a.err = ctx->d_err;
-  if (w->nT > ctx->n_counters) return shd_fail(ctx, SHD_ERR_ARG, "gemv: too many row tiles");
+  if (w->nT > ctx->n_counters - 8192) return shd_fail(ctx, SHD_ERR_ARG, "gemv: too many row tiles");
   switch (M) {
     case 1: return launch_ring_t<1>(ctx, w, a);
     case 2: return launch_ring_t<2>(ctx, w, a);
@@ -741,6 +933,7 @@ using namespace shd;
 __global__ void pad_rows_kernel(const uint32_t* __restrict__ a, const uint32_t* __restrict__ b,
                                 uint32_t* __restrict__ pa, uint32_t* __restrict__ pb, int M, int K,
                                 int K4) {
+  pdl_wait();
   const long long n = (long long)M * K4;
   for (long long v = blockIdx.x * (long long)blockDim.x + threadIdx.x; v < n;
        v += (long long)gridDim.x * blockDim.x) {
@@ -773,8 +966,9 @@ static int stage_padded(shd_ctx* ctx, const void* xc, const void* xs, int M, int
   return SHD_OK;
 }
 
-// Split M into launches of 8, 4, 2, 1 rows.
-static int next_m(int rem) { return rem >= 8 ? 8 : rem >= 4 ? 4 : rem >= 2 ? 2 : 1; }
+// Split M into launches of up to 8 rows (the ring kernel takes 1, 2, 4 or 8).
+static int next_m(int rem) { return rem >= 8 ? 8 : rem; }
+static int next_m_ring(int rem) { return rem >= 8 ? 8 : rem >= 4 ? 4 : rem >= 2 ? 2 : 1; }
 
 extern "C" int shd_linear_dual_f32(shd_ctx* ctx, const shd_weight* w, const float* bias,
                                    const float* xc, const float* xs, float* yc, float* ys, int M,
@@ -837,7 +1031,7 @@ extern "C" int shd_linear_dual_ring(shd_ctx* ctx, const shd_weight* w, const int
     xs = reinterpret_cast<const int32_t*>(ps);
   }
   for (int m0 = 0; m0 < M;) {
-    const int mm = next_m(M - m0);
+    const int mm = next_m_ring(M - m0);
     RingArgs a{};
     a.Xc = xc + (size_t)m0 * ldx;
     a.Xs = xs + (size_t)m0 * ldx;

@@ -72,14 +72,30 @@ struct GemvArgs {
   // EPI_LOGITS
   unsigned long long* amax;  // [M]
   int idx_offset;            // global index of local row 0 (vocabulary-parallel lm_head)
+  // RMSNorm prologue (norm = true at launch): x = reshare(RMSNorm(D + H)) computed per CTA into
+  // shared memory; Xc/Xs are then unused.
+  const float* nHc;  // residual stream shares [M][n_ldh]
+  const float* nHs;
+  const float* nDc;  // sublayer output shares added first (nullable)
+  const float* nDs;
+  float* nHout_c;    // h = D + H written by CTA 0 (nullable)
+  float* nHout_s;
+  int n_ldh;
+  const float* gamma;
+  float eps;
+  int nvariant;
+  const float* nmask;  // reshare mask [M][n_ldmask] (nullable)
+  int n_ldmask;
   // scratch
   float* partials;
   int* counters;
   int* err;
+  int nstages;  // pipeline depth (set by the launcher)
 };
 
-// Launch the f32-share GEMV for M rows with the given epilogue.
-int launch_gemv_f32(shd_ctx* ctx, const shd_weight* w, int M, int epi, GemvArgs a);
+// Launch the f32-share GEMV for M rows with the given epilogue; `norm` selects the fused RMSNorm
+// prologue (x from nHc/nHs/...) instead of staged activations (Xc/Xs).
+int launch_gemv_f32(shd_ctx* ctx, const shd_weight* w, int M, int epi, GemvArgs a, bool norm = false);
 
 struct RingArgs {
   const uint8_t* W;

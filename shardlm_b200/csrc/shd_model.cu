@@ -36,6 +36,8 @@ constexpr int kMaxRows = 8;  // rows of one GEMV launch / prefill chunk
 // Decode bookkeeping after the logits: tokens = keys, history row, position advance.
 __global__ void finish_step_kernel(const unsigned long long* keys, int* tokens, int* pos, int* hist,
                                    int hist_cap, unsigned long long* step, int M) {
+  if (threadIdx.x == 0) pdl_trigger();
+  pdl_wait();  // the argmax keys come from the lm_head kernel
   const int m = threadIdx.x;
   const unsigned long long s = *step;
   if (m < M) {
@@ -155,8 +157,10 @@ extern "C" int shd_model_create(shd_ctx* ctx, const shd_model_config* cfg, shd_m
       cudaEventCreateWithFlags(&m->ev_in, cudaEventDisableTiming) != cudaSuccess ||
       cudaEventCreateWithFlags(&m->ev_out, cudaEventDisableTiming) != cudaSuccess)
     return fail(shd_fail(ctx, SHD_ERR_CUDA, "shd_model_create: stream/event creation failed"));
-  int rc = shd_build_rope(ctx, d, c.max_seq, c.rope_theta);
+  int rc = build_rope_table(ctx, d, c.max_seq, c.rope_theta, &m->rope_cos, &m->rope_sin);
   if (rc) return fail(rc);
+  m->owned.push_back(m->rope_cos);
+  m->owned.push_back(m->rope_sin);
   const size_t R = m->R;
   const size_t kv_elems = (size_t)c.n_layers * c.max_batch * c.max_seq * std::max(m->kvd, 1);
   struct A {
@@ -380,38 +384,53 @@ extern "C" int shd_model_reset(shd_model* m) {
 // Enqueue the layers for M rows (positions pos[m] of slots seq[m]) starting from embedding shares in
 // Hbuf[0] and a zero D. Leaves the final residual in (Hbuf[cur], D) for the head.
 // ------------------------------------------------------------------------------------------------
+// RMSNorm of (D + H) feeding a GEMV: fused into the GEMV prologue when the M normalized rows fit in
+// shared memory next to the weight pipeline, else a separate norm kernel writes Xbuf.
+int shd_model::norm_into(GemvArgs& g, const shd_weight* w, int M, const float* Hc, const float* Hs,
+                         const float* Dc, const float* Ds, float* Oc, float* Os, const float* gamma,
+                         int variant, const float* mask, bool& fused) {
+  const int h = cfg.hidden;
+  fused = (size_t)M * 2 * w->nKC * kChunkBf16 * 4 <= 120 * 1024;
+  if (fused) {
+    g.nHc = Hc; g.nHs = Hs; g.nDc = Dc; g.nDs = Ds; g.nHout_c = Oc; g.nHout_s = Os; g.n_ldh = h;
+    g.gamma = gamma; g.eps = cfg.rms_eps; g.nvariant = variant; g.nmask = mask; g.n_ldmask = 0;
+    return SHD_OK;
+  }
+  NormArgs na{};
+  na.Hc = Hc; na.Hs = Hs; na.Dc = Dc; na.Ds = Ds; na.Hout_c = Oc; na.Hout_s = Os; na.ldh = h;
+  na.gamma = gamma; na.eps = cfg.rms_eps; na.variant = variant; na.mask = mask; na.ldmask = 0;
+  na.Xc = Xbuf; na.Xs = Xbuf + (size_t)M * h; na.ldx = h; na.n = h;
+  g.Xc = Xbuf; g.Xs = Xbuf + (size_t)M * h; g.ldx = h;
+  return launch_norm(ctx, na, M);
+}
+
 int shd_model::enqueue_layers(int M, const int* d_pos, const int* d_seq, int variant, int& cur) {
   const shd_model_config& c = cfg;
   const int h = c.hidden, d = c.head_dim;
   const size_t kv_layer = (size_t)c.max_batch * c.max_seq * kvd;
   const float* mk = masks;
   int rc;
+  bool fused;
   cur = 0;
   for (int l = 0; l < c.n_layers; ++l) {
     const LayerW& Lw = layers[l];
     const float* lm = mk ? mk + (size_t)l * mask_stride : nullptr;
     float* Hc = Hbuf[cur];
     float* Ho = Hbuf[cur ^ 1];
-    // input norm: h = D + H -> Ho, x = reshare(norm(h))
-    NormArgs na{};
-    na.Hc = Hc; na.Hs = Hc + (size_t)M * h; na.Dc = Dbuf; na.Ds = Dbuf + (size_t)M * h;
-    na.Hout_c = Ho; na.Hout_s = Ho + (size_t)M * h; na.ldh = h;
-    na.gamma = Lw.g1; na.eps = c.rms_eps; na.variant = variant;
-    na.mask = lm; na.ldmask = 0;
-    na.Xc = Xbuf; na.Xs = Xbuf + (size_t)M * h; na.ldx = h; na.n = h;
-    if ((rc = launch_norm(ctx, na, M))) return rc;
-    // q/k/v with RoPE and KV-cache write
+    // input norm (h = D + H -> Ho, x = reshare(norm(h))) + q/k/v with RoPE and KV-cache write
     GemvArgs g{};
-    g.Xc = Xbuf; g.Xs = Xbuf + (size_t)M * h; g.ldx = h;
+    if ((rc = norm_into(g, Lw.qkv, M, Hc, Hc + (size_t)M * h, Dbuf, Dbuf + (size_t)M * h, Ho,
+                        Ho + (size_t)M * h, Lw.g1, variant, lm, fused)))
+      return rc;
     g.bias = Lw.qkv->d_bias;
     g.q_dim = qd; g.kv_dim = kvd; g.head_dim = d;
-    g.rope_cos = ctx->d_rope_cos; g.rope_sin = ctx->d_rope_sin; g.rope_max_seq = ctx->rope_max_seq;
+    g.rope_cos = rope_cos; g.rope_sin = rope_sin; g.rope_max_seq = cfg.max_seq;
     g.pos = d_pos; g.seq = d_seq;
     g.Q = Qbuf; g.ldq = qd;
     g.Kcache = kcache + (size_t)l * kv_layer; g.Vcache = vcache + (size_t)l * kv_layer;
     g.kv_seq_stride = (int64_t)c.max_seq * kvd;
     if ((rc = prof_mark(0, Lw.qkv, true))) return rc;
-    if ((rc = launch_gemv_f32(ctx, Lw.qkv, M, EPI_QKV, g))) return rc;
+    if ((rc = launch_gemv_f32(ctx, Lw.qkv, M, EPI_QKV, g, fused))) return rc;
     if ((rc = prof_mark(0, Lw.qkv, false))) return rc;
     // attention -> A shares
     AttnArgs at{};
@@ -435,19 +454,16 @@ int shd_model::enqueue_layers(int M, const int* d_pos, const int* d_seq, int var
     if ((rc = launch_gemv_f32(ctx, Lw.o, M, EPI_STORE, go))) return rc;
     if ((rc = prof_mark(1, Lw.o, false))) return rc;
     if ((rc = allreduce_sum(Dbuf, (size_t)2 * M * h))) return rc;
-    // post-attention norm: h = D + Ho -> Hc, x
-    NormArgs nb = na;
-    nb.Hc = Ho; nb.Hs = Ho + (size_t)M * h; nb.Hout_c = Hc; nb.Hout_s = Hc + (size_t)M * h;
-    nb.gamma = Lw.g2; nb.mask = lm ? lm + 2 * (size_t)h : nullptr;
-    if ((rc = launch_norm(ctx, nb, M))) return rc;
-    // gate/up + SwiGLU reshare -> ACT
+    // post-attention norm (h = D + Ho -> Hc) + gate/up + SwiGLU reshare -> ACT
     GemvArgs gu{};
-    gu.Xc = Xbuf; gu.Xs = Xbuf + (size_t)M * h; gu.ldx = h;
+    if ((rc = norm_into(gu, Lw.gateup, M, Ho, Ho + (size_t)M * h, Dbuf, Dbuf + (size_t)M * h, Hc,
+                        Hc + (size_t)M * h, Lw.g2, variant, lm ? lm + 2 * (size_t)h : nullptr, fused)))
+      return rc;
     gu.Yc = ACTbuf; gu.Ys = ACTbuf + (size_t)M * I; gu.ldy = I;
     gu.variant = variant;
     gu.mask = lm ? lm + 3 * (size_t)h + sh.inter_begin : nullptr; gu.ldmask = 0;
     if ((rc = prof_mark(2, Lw.gateup, true))) return rc;
-    if ((rc = launch_gemv_f32(ctx, Lw.gateup, M, EPI_GATEUP, gu))) return rc;
+    if ((rc = launch_gemv_f32(ctx, Lw.gateup, M, EPI_GATEUP, gu, fused))) return rc;
     if ((rc = prof_mark(2, Lw.gateup, false))) return rc;
     // down -> D
     GemvArgs gd{};
@@ -467,23 +483,18 @@ int shd_model::enqueue_head(int M, int row, int cur, int variant, bool want_logi
   const int h = cfg.hidden;
   const float* lm = masks ? masks + (size_t)(cfg.n_layers - 1) * mask_stride : nullptr;
   float* Hc = Hbuf[cur];
-  NormArgs na{};
-  na.Hc = Hc + (size_t)row * h; na.Hs = Hc + (size_t)M * h + (size_t)row * h;
-  na.Dc = Dbuf + (size_t)row * h; na.Ds = Dbuf + (size_t)M * h + (size_t)row * h;
-  na.ldh = h;
-  na.gamma = final_norm; na.eps = cfg.rms_eps; na.variant = variant;
-  na.mask = lm; na.ldmask = 0;
-  na.Xc = Xbuf; na.Xs = Xbuf + h; na.ldx = h; na.n = h;
-  int rc;
-  if ((rc = launch_norm(ctx, na, 1))) return rc;
   GemvArgs g{};
-  g.Xc = Xbuf; g.Xs = Xbuf + h; g.ldx = h;
+  bool fused;
+  int rc = norm_into(g, lm_head, 1, Hc + (size_t)row * h, Hc + (size_t)M * h + (size_t)row * h,
+                     Dbuf + (size_t)row * h, Dbuf + (size_t)M * h + (size_t)row * h, nullptr, nullptr,
+                     final_norm, variant, lm, fused);
+  if (rc) return rc;
   g.amax = amax + key_row;
   g.idx_offset = sh.vocab_begin;
   if (want_logits) {
     g.Yc = LOGbuf; g.Ys = LOGbuf + V; g.ldy = V;
   }
-  return launch_gemv_f32(ctx, lm_head, 1, EPI_LOGITS, g);
+  return launch_gemv_f32(ctx, lm_head, 1, EPI_LOGITS, g, fused);
 }
 
 // Decode head for all M rows (each its own slot): norm M rows, lm_head on M rows.
@@ -491,19 +502,15 @@ int shd_model::enqueue_head_rows(int M, int cur, int variant) {
   const int h = cfg.hidden;
   const float* lm = masks ? masks + (size_t)(cfg.n_layers - 1) * mask_stride : nullptr;
   float* Hc = Hbuf[cur];
-  NormArgs na{};
-  na.Hc = Hc; na.Hs = Hc + (size_t)M * h; na.Dc = Dbuf; na.Ds = Dbuf + (size_t)M * h; na.ldh = h;
-  na.gamma = final_norm; na.eps = cfg.rms_eps; na.variant = variant;
-  na.mask = lm; na.ldmask = 0;
-  na.Xc = Xbuf; na.Xs = Xbuf + (size_t)M * h; na.ldx = h; na.n = h;
-  int rc;
-  if ((rc = launch_norm(ctx, na, M))) return rc;
   GemvArgs g{};
-  g.Xc = Xbuf; g.Xs = Xbuf + (size_t)M * h; g.ldx = h;
+  bool fused;
+  int rc = norm_into(g, lm_head, M, Hc, Hc + (size_t)M * h, Dbuf, Dbuf + (size_t)M * h, nullptr, nullptr,
+                     final_norm, variant, lm, fused);
+  if (rc) return rc;
   g.amax = amax;
   g.idx_offset = sh.vocab_begin;
   if ((rc = prof_mark(4, lm_head, true))) return rc;
-  if ((rc = launch_gemv_f32(ctx, lm_head, M, EPI_LOGITS, g))) return rc;
+  if ((rc = launch_gemv_f32(ctx, lm_head, M, EPI_LOGITS, g, fused))) return rc;
   return prof_mark(4, lm_head, false);
 }
 
@@ -591,8 +598,9 @@ int shd_model::enqueue_decode_step(int M) {
   if ((rc = enqueue_layers(M, pos, seq, cfg.variant_decode, cur))) return rc;
   if ((rc = enqueue_head_rows(M, cur, cfg.variant_decode))) return rc;
   if ((rc = allreduce_max_keys(M))) return rc;
-  finish_step_kernel<<<1, 32, 0, stream>>>(amax, tokens, pos, hist, hist_cap, step, M);
-  SHD_CHECK_LAUNCH(ctx, "finish_step_kernel");
+  SHD_CHECK_CUDA(ctx, launch_pdl(finish_step_kernel, dim3(1), dim3(32), 0, stream, (const unsigned long long*)amax,
+                                 tokens, pos, hist, hist_cap, step, M));
+  ctx->launches++;
   return SHD_OK;
 }
 

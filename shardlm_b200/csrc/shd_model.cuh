@@ -27,6 +27,7 @@ struct shd_model {
   shd_weight* lm_head = nullptr;
   float* final_norm = nullptr;
   uint16_t* embed = nullptr;
+  float *rope_cos = nullptr, *rope_sin = nullptr;  // RopeFrequencies table [max_seq][head_dim/2]
   // activations: [2][rows][width], client rows then server rows
   float* Hbuf[2] = {nullptr, nullptr};
   float *Dbuf = nullptr, *Xbuf = nullptr, *Qbuf = nullptr, *Abuf = nullptr, *ACTbuf = nullptr;
@@ -65,6 +66,9 @@ struct shd_model {
   int enter();
   int leave(int rc);
   int check_ready();
+  int norm_into(shd::GemvArgs& g, const shd_weight* w, int M, const float* Hc, const float* Hs,
+                const float* Dc, const float* Ds, float* Oc, float* Os, const float* gamma, int variant,
+                const float* mask, bool& fused);
   int enqueue_layers(int M, const int* d_pos, const int* d_seq, int variant, int& cur);
   int enqueue_head(int M, int row, int cur, int variant, bool want_logits, int key_row);
   int enqueue_head_rows(int M, int cur, int variant);

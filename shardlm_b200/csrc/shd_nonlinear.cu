@@ -30,6 +30,8 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 // x = h_c + h_s, y = x * inv_rms * gamma, reshare (y - mask, mask).
 __global__ void norm_reshare_kernel(NormArgs a) {
   __shared__ float red[33];
+  if (threadIdx.x == 0) pdl_trigger();
+  pdl_wait();
   const int m = blockIdx.x;
   const float* hc = a.Hc + (size_t)m * a.ldh;
   const float* hs = a.Hs + (size_t)m * a.ldh;
@@ -84,8 +86,8 @@ __global__ void norm_reshare_kernel(NormArgs a) {
 
 int launch_norm(shd_ctx* ctx, const NormArgs& a, int M) {
   const int threads = a.n >= 4096 ? 1024 : (a.n >= 1024 ? 512 : 128);
-  norm_reshare_kernel<<<M, threads, 0, ctx->stream>>>(a);
-  SHD_CHECK_LAUNCH(ctx, "norm_reshare_kernel");
+  SHD_CHECK_CUDA(ctx, launch_pdl(norm_reshare_kernel, dim3(M), dim3(threads), 0, ctx->stream, a));
+  ctx->launches++;
   return SHD_OK;
 }
 
@@ -155,6 +157,8 @@ __global__ void rope_shares_kernel(float* xc, float* xs, int M, int n_heads, int
 // Embedding shares: server share s_k = unit(word(seed, 7, counter * hidden + k)), client e - s.
 // Also (optionally) zeroes the sublayer-output rows D and resets the argmax keys for a new step.
 __global__ void embed_shares_kernel(EmbedArgs a) {
+  if (threadIdx.x == 0) pdl_trigger();
+  pdl_wait();  // tokens and positions come from the previous step
   const int m = blockIdx.y;
   const int tok = a.tokens[m];
   if (tok < 0 || tok >= a.vocab) {
@@ -178,8 +182,8 @@ __global__ void embed_shares_kernel(EmbedArgs a) {
 
 int launch_embed(shd_ctx* ctx, const EmbedArgs& a, int M) {
   dim3 grid((a.hidden + 255) / 256, M);
-  embed_shares_kernel<<<grid, 256, 0, ctx->stream>>>(a);
-  SHD_CHECK_LAUNCH(ctx, "embed_shares_kernel");
+  SHD_CHECK_CUDA(ctx, launch_pdl(embed_shares_kernel, grid, dim3(256), 0, ctx->stream, a));
+  ctx->launches++;
   return SHD_OK;
 }
 
@@ -244,10 +248,8 @@ static int ew_grid(shd_ctx* ctx, long long n) {
 
 // RopeFrequencies::new (crates/v2/sharing/src/secure_attention.rs:42-63) on the host with libm's
 // powf/cosf/sinf, exactly as the reference computes its table, then uploaded.
-int shd::shd_build_rope(shd_ctx* ctx, int head_dim, int max_seq, float theta) {
-  if (ctx->d_rope_cos && ctx->rope_head_dim == head_dim && ctx->rope_max_seq >= max_seq &&
-      ctx->rope_theta == theta)
-    return SHD_OK;
+int shd::build_rope_table(shd_ctx* ctx, int head_dim, int max_seq, float theta, float** cos_out,
+                          float** sin_out) {
   const int half = head_dim / 2;
   std::vector<float> inv(half), c((size_t)max_seq * half), s((size_t)max_seq * half);
   for (int i = 0; i < half; ++i) inv[i] = 1.0f / powf(theta, (float)(2 * i) / (float)head_dim);
@@ -256,14 +258,30 @@ int shd::shd_build_rope(shd_ctx* ctx, int head_dim, int max_seq, float theta) {
       c[(size_t)p * half + i] = cosf((float)p * inv[i]);
       s[(size_t)p * half + i] = sinf((float)p * inv[i]);
     }
+  float *dc = nullptr, *ds = nullptr;
+  cudaError_t e = cudaMalloc(&dc, c.size() * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&ds, s.size() * 4);
+  if (e == cudaSuccess) e = cudaMemcpy(dc, c.data(), c.size() * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(ds, s.data(), s.size() * 4, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    cudaFree(dc);
+    cudaFree(ds);
+    return shd_cuda_fail(ctx, e, "RoPE table");
+  }
+  *cos_out = dc;
+  *sin_out = ds;
+  return SHD_OK;
+}
+
+// The context's table serves shd_rope_shares; it is replaced on every call.
+int shd::shd_build_rope(shd_ctx* ctx, int head_dim, int max_seq, float theta) {
   SHD_CHECK_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
   cudaFree(ctx->d_rope_cos);
   cudaFree(ctx->d_rope_sin);
   ctx->d_rope_cos = ctx->d_rope_sin = nullptr;
-  SHD_CHECK_CUDA(ctx, cudaMalloc(&ctx->d_rope_cos, c.size() * 4));
-  SHD_CHECK_CUDA(ctx, cudaMalloc(&ctx->d_rope_sin, s.size() * 4));
-  SHD_CHECK_CUDA(ctx, cudaMemcpy(ctx->d_rope_cos, c.data(), c.size() * 4, cudaMemcpyHostToDevice));
-  SHD_CHECK_CUDA(ctx, cudaMemcpy(ctx->d_rope_sin, s.data(), s.size() * 4, cudaMemcpyHostToDevice));
+  ctx->rope_head_dim = ctx->rope_max_seq = 0;
+  const int rc = build_rope_table(ctx, head_dim, max_seq, theta, &ctx->d_rope_cos, &ctx->d_rope_sin);
+  if (rc) return rc;
   ctx->rope_head_dim = head_dim;
   ctx->rope_max_seq = max_seq;
   ctx->rope_theta = theta;

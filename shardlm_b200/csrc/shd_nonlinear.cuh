@@ -75,5 +75,8 @@ int launch_attention(shd_ctx* ctx, const AttnArgs& a, int M);
 int ensure_attn_scratch(shd_ctx* ctx, size_t floats);
 
 int shd_build_rope(shd_ctx* ctx, int head_dim, int max_seq, float theta);
+// RopeFrequencies::new table ([max_seq][head_dim/2] cos and sin) in new device allocations.
+int build_rope_table(shd_ctx* ctx, int head_dim, int max_seq, float theta, float** cos_out,
+                     float** sin_out);
 
 }  // namespace shd

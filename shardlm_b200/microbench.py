@@ -1,0 +1,123 @@
+"""Kernel microbenchmarks (CUDA events on the launching stream).
+
+  python -m shardlm_b200.microbench linear [--model qwen2.5-7b] [--kind all|qkv|o|gateup|down|lm_head]
+                                           [--rows 1] [--iters 20]
+  python -m shardlm_b200.microbench beaver [--n 9699328] [--iters 20]
+  python -m shardlm_b200.microbench ring   [--copies 16] [--iters 20]
+
+Each weight kind is instantiated in enough copies to exceed the 126 MB L2, and launches rotate over
+the copies, so every launch streams its weights from HBM.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import numpy as np
+import torch
+
+from .model import SHAPES
+from .runtime import Context, Weight, ptr
+from .sharing import GpuSecureLinear
+
+L2_BYTES = 126 * 2**20
+
+
+def _time(fn, iters: int) -> float:
+    for _ in range(3):
+        fn(0)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(iters):
+        fn(i)
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def linear(args, ctx: Context):
+    sh = SHAPES[args.model]
+    h, d = sh.hidden, sh.head_dim
+    kinds = {"qkv": (sh.n_heads * d + 2 * sh.n_kv_heads * d, h), "o": (h, sh.n_heads * d),
+             "gateup": (2 * sh.intermediate, h), "down": (h, sh.intermediate), "lm_head": (sh.vocab, h)}
+    todo = list(kinds) if args.kind == "all" else [args.kind]
+    out = {}
+    for k in todo:
+        N, K = kinds[k]
+        copies = max(1, -(-2 * L2_BYTES // (N * K * 2)))
+        lins = []
+        for c in range(copies):
+            w = (torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16)
+            lins.append(GpuSecureLinear(ctx, Weight.from_bf16_out_in(ctx, w), None))
+            del w
+        M = args.rows
+        xc, xs = torch.randn(M, K, device="cuda"), torch.rand(M, K, device="cuda")
+        yc, ys = torch.empty(M, N, device="cuda"), torch.empty(M, N, device="cuda")
+
+        def run(i):
+            ctx.call("shd_linear_dual_f32", lins[i % copies].weight.handle, None, ptr(xc), ptr(xs),
+                     ptr(yc), ptr(ys), M, None, None)
+
+        ms = _time(run, args.iters)
+        ctx.sync()
+        out[k] = {"N": N, "K": K, "rows": M, "us": round(ms * 1e3, 2), "GBps": round(N * K * 2 / ms / 1e6, 1)}
+        del lins
+        torch.cuda.empty_cache()
+    print(json.dumps(out))
+
+
+def beaver(args, ctx: Context):
+    from .sharing import beaver_triples_f32, secure_multiply_batch
+
+    n = args.n
+    x = [torch.randn(n, device="cuda") for _ in range(4)]
+    t = beaver_triples_f32(ctx, n, seed=1)
+    res = secure_multiply_batch(ctx, *x, t, return_opened=True)
+
+    def run(i):
+        secure_multiply_batch(ctx, *x, t, return_opened=True)
+
+    ms = _time(run, args.iters)
+    ctx.sync()
+    del res
+    print(json.dumps({"beaver_f32": {"n": n, "us": round(ms * 1e3, 2), "GBps": round(56 * n / ms / 1e6, 1)}}))
+
+
+def ring(args, ctx: Context):
+    from .sharing import LinearServer
+
+    rng = np.random.default_rng(0)
+    servers = [LinearServer(rng.integers(-2**20, 2**20, 1536 * 1536, dtype=np.int64).astype(np.int32), None,
+                            1536, 1536, 16, ctx) for _ in range(args.copies)]
+    xc = torch.randint(-2**31, 2**31 - 1, (1, 1536), device="cuda", dtype=torch.int64).to(torch.int32)
+    xs = torch.randint(-2**31, 2**31 - 1, (1, 1536), device="cuda", dtype=torch.int64).to(torch.int32)
+    yc = torch.empty(1, 1536, device="cuda", dtype=torch.int32)
+    ys = torch.empty(1, 1536, device="cuda", dtype=torch.int32)
+
+    def run(i):
+        s = servers[i % args.copies]
+        ctx.call("shd_linear_dual_ring", s.weight.handle, None, ptr(xc), ptr(xs), ptr(yc), ptr(ys), 1, 16)
+
+    ms = _time(run, args.iters)
+    ctx.sync()
+    b = 1536 * 1536 * 4
+    print(json.dumps({"ring_linear_1536": {"us": round(ms * 1e3, 2), "GBps": round(b / ms / 1e6, 1)}}))
+
+
+def main():
+    p = argparse.ArgumentParser()
+    p.add_argument("what", choices=["linear", "beaver", "ring"])
+    p.add_argument("--model", default="qwen2.5-7b")
+    p.add_argument("--kind", default="all")
+    p.add_argument("--rows", type=int, default=1)
+    p.add_argument("--iters", type=int, default=20)
+    p.add_argument("--n", type=int, default=512 * 18944)
+    p.add_argument("--copies", type=int, default=16)
+    args = p.parse_args()
+    ctx = Context(0)
+    {"linear": linear, "beaver": beaver, "ring": ring}[args.what](args, ctx)
+
+
+if __name__ == "__main__":
+    main()

@@ -10,8 +10,21 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-def _dev(ctx, a):
-    return ctx.to_device(np.ascontiguousarray(a, np.float32))
+_LIVE = []
+
+
+@pytest.fixture(autouse=True)
+def _release_staged():
+    yield
+    torch.cuda.synchronize()
+    _LIVE.clear()
+
+
+def _dev(ctx, a, dtype=np.float32):
+    # The raw address goes to the library; keep the tensor alive until the kernels that read it ran.
+    t = ctx.to_device(np.ascontiguousarray(a, dtype))
+    _LIVE.append(t)
+    return t
 
 
 def _call(ctx, name, *args):
@@ -136,7 +149,7 @@ def test_embed_shares_bit_exact(ctx, orc):
     toks = np.array([0, 999, 17, 17], np.int32)
     hc, hs = ctx.empty(4, h), ctx.empty(4, h)
     counter = (3 << 32) + 100
-    _call(ctx, "shd_embed_shares", ptr(table), V, h, ptr(ctx.to_device(toks)), 4, 77, counter, ptr(hc), ptr(hs))
+    _call(ctx, "shd_embed_shares", ptr(table), V, h, ptr(_dev(ctx, toks, np.int32)), 4, 77, counter, ptr(hc), ptr(hs))
     tab = table.view(torch.int16).cpu().numpy().view(np.uint16)
     for m in range(4):
         ec, es = orc.embed_shares(tab, h, toks[m], 77, counter + m)
