@@ -17,9 +17,9 @@ int shd_cuda_fail(shd_ctx* ctx, cudaError_t e, const char* what) {
   return shd_fail(ctx, SHD_ERR_CUDA, m);
 }
 
-// Split-K partial storage: 2 slots per CTA, a tile of 32 rows x 2 shares x 8 token rows, 8 bytes
-// per value (the ring kernel accumulates in 64 bits).
-static size_t partial_floats_for(int sms) { return (size_t)sms * 2 * (kTileRows * 2 * 8) * 2; }
+// Split-K partial storage: up to two CTAs per SM, 2 slots per CTA, a tile of 32 rows x 2 shares x
+// 8 token rows, 8 bytes per value (the ring kernel accumulates in 64 bits).
+static size_t partial_floats_for(int sms) { return (size_t)2 * sms * 2 * (kTileRows * 2 * 8) * 2; }
 
 extern "C" int shd_init(int device, shd_ctx** out) {
   if (!out) return SHD_ERR_ARG;

