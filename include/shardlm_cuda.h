@@ -290,11 +290,12 @@ int shd_model_seq_len(const shd_model* m, int slot);
 /* Kernels launched by one captured decode step (0 before the first decode). */
 int64_t shd_model_step_launches(const shd_model* m);
 /* Profiling: when on, the captured decode step records CUDA events around every share-wise linear
- * launch; shd_model_linear_times then returns, for the most recent step, the summed device time
- * (ms) and the summed weight bytes of the launches of each kind: [0] qkv, [1] o, [2] gate/up,
- * [3] down, [4] lm_head. Turning it on or off re-captures the graph at the next decode. */
+ * and attention launch; shd_model_linear_times then returns, for the most recent step, the summed
+ * device time (ms) and the summed weight bytes of the launches of each kind: [0] qkv, [1] o,
+ * [2] gate/up, [3] down, [4] lm_head, [5] attention (bytes 0). Turning it on or off re-captures
+ * the graph at the next decode. */
 int shd_model_set_profiling(shd_model* m, int on);
-int shd_model_linear_times(shd_model* m, float* ms_out5, double* bytes_out5);
+int shd_model_linear_times(shd_model* m, float* ms_out6, double* bytes_out6);
 
 #ifdef __cplusplus
 }

@@ -2,180 +2,276 @@
 // crates/v2/sharing/src/secure_nonlinear.rs:287-333, and compute_mpc_attention_on_shares,
 // crates/v2/server/src/routes/secure_inference_mpc.rs:568-663), followed by the reshare.
 //
-// Split-K flash decode: CTA (split, head, row) scores its slice of positions (one warp per
-// position, lanes over head_dim), forms exp(s - local max) and the weighted V sum, and writes a
-// partial (max, sum, acc[head_dim]). The last CTA of a (row, head) to arrive combines the splits in
-// split order -- deterministic -- and writes (out - mask, mask).
+// Cluster flash decode. A cluster of 8 CTAs serves one (query row, head group), a group being up to
+// 4 query heads that share one kv head, so each K/V row is read once for the group. CTA r of the
+// cluster takes the r-th eighth of the positions and walks it in tiles of 32: the tile's K and V
+// rows are staged in shared memory with coalesced 16-byte loads; warps split head_dim and lanes
+// split the 32 positions for the scores; an online softmax (running max, sum) is kept per head and
+// the weighted V sum lives in registers. The 8 partial results are gathered into CTA 0 through
+// distributed shared memory and combined in rank order, so the result does not depend on timing.
+//
+// Against the reference's two-pass softmax (max over all scores, clamp(s - max, -40, 40), exp, sum,
+// divide, weighted sum) the online form differs only in rounding and in applying the -40 clamp
+// relative to a running instead of the global maximum (weights below e^-40 of the largest, i.e.
+// contributions under 4.3e-18 of the total).
+#include <cooperative_groups.h>
+
 #include <algorithm>
 #include <cmath>
+#include <cstring>
 #include <vector>
 
 #include "shd_nonlinear.cuh"
 
+namespace cg = cooperative_groups;
+
 namespace shd {
 
-__global__ void attn_decode_kernel(const AttnArgs a) {
-  extern __shared__ float sm[];  // q[head_dim] | scores[chunk_max] | red[34]
-  const int hd = a.head_dim;
-  const int sp = blockIdx.x, h = blockIdx.y, m = blockIdx.z;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
-  const int chunk_max = (int)((a.kv_seq_stride / a.kvd + a.nsplit - 1) / a.nsplit);
-  float* q = sm;
-  float* sc = sm + hd;
-  float* red = sc + chunk_max;
-  __shared__ int last_flag;
+constexpr int kAttnCluster = 8;   // CTAs per (row, group)
+constexpr int kAttnTile = 32;     // positions per tile
+constexpr int kAttnThreads = 256;
+constexpr int kAttnGroup = 4;     // query heads per group (kAttnGroupMax bounds the scratch)
 
+template <int HD>
+struct AttnSmem {
+  static constexpr int KS = HD + 4;  // padded row stride (conflict-free column reads)
+  float k[kAttnTile][KS];
+  float v[kAttnTile][HD];
+  float q[kAttnGroup][HD];
+  float spart[kAttnThreads / 32][kAttnGroup][kAttnTile];  // per-warp partial dots
+  float p[kAttnGroup][kAttnTile];                         // tile weights
+  float m[kAttnGroup], l[kAttnGroup], alpha[kAttnGroup];
+  float gather[kAttnCluster][kAttnGroup][HD + 2];         // CTA 0: partials of the cluster
+};
+
+template <int HD>
+__global__ void __launch_bounds__(kAttnThreads) attn_cluster_kernel(const AttnArgs a) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  AttnSmem<HD>& S = *reinterpret_cast<AttnSmem<HD>*>(smem_raw);
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int gi = blockIdx.y, m = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int NW = kAttnThreads / 32;  // 8 warps
+  constexpr int DW = HD / NW;            // dims per warp in the score phase (16 or 8)
   if (tid == 0) pdl_trigger();
   pdl_wait();  // positions, queries and the cache come from earlier kernels
-  const int p = a.pos[m];
-  const int kv_len = p + 1;
+
+  const int4 grp = a.groups[gi];
+  const int kvh = grp.x, qh0 = grp.y, G = grp.z;
+  const int kv_len = a.pos[m] + 1;
   const int sq = a.seq ? a.seq[m] : 0;
-  const int kvh = a.kv_head_of[h];
-  const int chunk = (kv_len + a.nsplit - 1) / a.nsplit;
-  const int t0 = min(sp * chunk, kv_len), t1 = min(t0 + chunk, kv_len);
-  const float* K = a.Kcache + (size_t)sq * a.kv_seq_stride + (size_t)kvh * hd;
-  const float* V = a.Vcache + (size_t)sq * a.kv_seq_stride + (size_t)kvh * hd;
+  const int per = (kv_len + kAttnCluster - 1) / kAttnCluster;
+  const int t0 = min(rank * per, kv_len), t1 = min(t0 + per, kv_len);
+  const float* K = a.Kcache + (size_t)sq * a.kv_seq_stride + (size_t)kvh * HD;
+  const float* V = a.Vcache + (size_t)sq * a.kv_seq_stride + (size_t)kvh * HD;
   const bool mpc = a.variant == SHD_NL_MPC;
 
-  for (int d = tid; d < hd; d += blockDim.x) q[d] = a.Q[(size_t)m * a.ldq + (size_t)h * hd + d];
-  __syncthreads();
-
-  // scores: one warp per position, lanes stride head_dim; score = (q.k) * scale
-  for (int t = t0 + warp; t < t1; t += nw) {
-    const float* kr = K + (size_t)t * a.kvd;
-    float s = 0.0f;
-    for (int d = lane; d < hd; d += 32) s = __fmaf_rn(q[d], kr[d], s);
+  for (int i = tid; i < kAttnGroup * HD; i += kAttnThreads) {
+    const int g = i / HD, d = i % HD;
+    S.q[g][d] = (g < G) ? a.Q[(size_t)m * a.ldq + (size_t)(qh0 + g) * HD + d] : 0.0f;
+  }
+  if (tid < kAttnGroup) {
+    S.m[tid] = -INFINITY;
+    S.l[tid] = 0.0f;
+  }
+  // PV mapping: thread -> dim d, heads g0 and g0 + 2 (kAttnThreads = 2 * HD for HD = 128)
+  constexpr int GPT = kAttnGroup * HD / kAttnThreads;  // heads per thread: 2 (HD 128) or 1 (HD 64)
+  float acc[GPT];
 #pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
-    if (lane == 0) sc[t - t0] = __fmul_rn(s, a.scale);
-  }
+  for (int j = 0; j < GPT; ++j) acc[j] = 0.0f;
+  const int pd = tid % HD, pg0 = tid / HD;  // head of acc[j] = pg0 + j * (kAttnThreads / HD)
   __syncthreads();
 
-  // local max
-  float mx = -INFINITY;
-  for (int t = t0 + tid; t < t1; t += blockDim.x) mx = fmaxf(mx, sc[t - t0]);
+  float qreg[kAttnGroup][DW];  // this warp's slice of the queries
 #pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  if (lane == 0) red[warp] = mx;
-  __syncthreads();
-  mx = -INFINITY;
-  for (int w = 0; w < nw; ++w) mx = fmaxf(mx, red[w]);
-  __syncthreads();
-
-  // weights and their sum (fixed tree)
-  float l = 0.0f;
-  for (int t = t0 + tid; t < t1; t += blockDim.x) {
-    float x = __fsub_rn(sc[t - t0], mx);
-    if (!mpc) x = fminf(fmaxf(x, -40.0f), 40.0f);
-    const float e = expf(x);
-    sc[t - t0] = e;
-    l = __fadd_rn(l, e);
-  }
+  for (int g = 0; g < kAttnGroup; ++g)
 #pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) l = __fadd_rn(l, __shfl_xor_sync(0xffffffffu, l, o));
-  if (lane == 0) red[warp] = l;
-  __syncthreads();
-  l = 0.0f;
-  for (int w = 0; w < nw; ++w) l = __fadd_rn(l, red[w]);
+    for (int j = 0; j < DW; ++j) qreg[g][j] = S.q[g][warp * DW + j];
 
-  // weighted V sum, one thread per dimension
-  float* part = a.partials + (((size_t)m * a.H + h) * a.nsplit + sp) * (hd + 2);
-  for (int d = tid; d < hd; d += blockDim.x) {
-    float acc = 0.0f;
-    for (int t = t0; t < t1; ++t) acc = __fmaf_rn(sc[t - t0], V[(size_t)t * a.kvd + d], acc);
-    part[2 + d] = acc;
-  }
-  if (tid == 0) {
-    part[0] = (t0 < t1) ? mx : -INFINITY;
-    part[1] = l;
-  }
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    const int old = atomicAdd(&a.counters[m * a.H + h], 1);
-    last_flag = (old == a.nsplit - 1);
-    if (last_flag) a.counters[m * a.H + h] = 0;
-  }
-  __syncthreads();
-  if (!last_flag) return;
-  __threadfence();
-
-  const float* base = a.partials + ((size_t)m * a.H + h) * a.nsplit * (hd + 2);
-  float M = -INFINITY;
-  for (int s = 0; s < a.nsplit; ++s) M = fmaxf(M, __ldcg(base + (size_t)s * (hd + 2)));
-  float L = 0.0f;
-  for (int s = 0; s < a.nsplit; ++s) {
-    const float ms = __ldcg(base + (size_t)s * (hd + 2));
-    if (ms == -INFINITY) continue;
-    L = __fadd_rn(L, __fmul_rn(__ldcg(base + (size_t)s * (hd + 2) + 1), expf(__fsub_rn(ms, M))));
-  }
-  const bool uniform = mpc && !(L > 1e-10f && isfinite(L));
-  for (int d = tid; d < hd; d += blockDim.x) {
-    float out;
-    if (uniform) {
-      // compute_mpc_attention_on_shares: 1/seq_len weights when the sum is not usable
-      float acc = 0.0f;
-      for (int t = 0; t < kv_len; ++t) acc = __fmaf_rn(__fdiv_rn(1.0f, (float)kv_len), V[(size_t)t * a.kvd + d], acc);
-      out = acc;
-    } else {
-      float acc = 0.0f;
-      for (int s = 0; s < a.nsplit; ++s) {
-        const float ms = __ldcg(base + (size_t)s * (hd + 2));
-        if (ms == -INFINITY) continue;
-        acc = __fadd_rn(acc, __fmul_rn(__ldcg(base + (size_t)s * (hd + 2) + 2 + d), expf(__fsub_rn(ms, M))));
+  for (int tb = t0; tb < t1; tb += kAttnTile) {
+    const int nt = min(kAttnTile, t1 - tb);
+    // stage K and V rows of the tile
+    for (int i = tid; i < kAttnTile * (HD / 4); i += kAttnThreads) {
+      const int r = i / (HD / 4), c4 = i % (HD / 4);
+      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+      if (r < nt) {
+        kv = *reinterpret_cast<const float4*>(K + (size_t)(tb + r) * a.kvd + 4 * c4);
+        vv = *reinterpret_cast<const float4*>(V + (size_t)(tb + r) * a.kvd + 4 * c4);
       }
-      out = __fdiv_rn(acc, L);
+      *reinterpret_cast<float4*>(&S.k[r][4 * c4]) = kv;
+      *reinterpret_cast<float4*>(&S.v[r][4 * c4]) = vv;
     }
-    const size_t o = (size_t)m * a.ldo + (size_t)h * hd + d;
-    const float mk = a.mask ? a.mask[(size_t)m * a.ldmask + (size_t)h * hd + d] : 0.0f;
+    __syncthreads();
+    // partial dots: warp = dim slice, lane = position
+    {
+      float part[kAttnGroup];
+#pragma unroll
+      for (int g = 0; g < kAttnGroup; ++g) part[g] = 0.0f;
+#pragma unroll
+      for (int j = 0; j < DW; j += 4) {
+        const float4 kk = *reinterpret_cast<const float4*>(&S.k[lane][warp * DW + j]);
+#pragma unroll
+        for (int g = 0; g < kAttnGroup; ++g) {
+          part[g] = __fmaf_rn(qreg[g][j + 0], kk.x, part[g]);
+          part[g] = __fmaf_rn(qreg[g][j + 1], kk.y, part[g]);
+          part[g] = __fmaf_rn(qreg[g][j + 2], kk.z, part[g]);
+          part[g] = __fmaf_rn(qreg[g][j + 3], kk.w, part[g]);
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < kAttnGroup; ++g) S.spart[warp][g][lane] = part[g];
+    }
+    __syncthreads();
+    // scores and online softmax: warp g (< G) owns head g, lane = position
+    if (warp < G) {
+      const int g = warp;
+      float s = 0.0f;
+#pragma unroll
+      for (int w = 0; w < NW; ++w) s = __fadd_rn(s, S.spart[w][g][lane]);
+      s = (lane < nt) ? __fmul_rn(s, a.scale) : -INFINITY;
+      float tmax = s;
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
+      const float mold = S.m[g];
+      const float mnew = fmaxf(mold, tmax);
+      float x = __fsub_rn(s, mnew);
+      if (!mpc) x = fminf(fmaxf(x, -40.0f), 40.0f);
+      const float pe = (lane < nt) ? expf(x) : 0.0f;
+      float tsum = pe;
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) tsum = __fadd_rn(tsum, __shfl_xor_sync(0xffffffffu, tsum, o));
+      S.p[g][lane] = pe;
+      __syncwarp();
+      if (lane == 0) {
+        const float al = (mold == -INFINITY) ? 0.0f : expf(__fsub_rn(mold, mnew));
+        S.alpha[g] = al;
+        S.l[g] = __fmaf_rn(S.l[g], al, tsum);
+        S.m[g] = mnew;
+      }
+    }
+    __syncthreads();
+    // weighted V: thread -> (head, dim)
+#pragma unroll
+    for (int j = 0; j < GPT; ++j) {
+      const int g = pg0 + j * (kAttnThreads / HD);
+      if (g < G) {
+        float v = __fmul_rn(acc[j], S.alpha[g]);
+        for (int r = 0; r < nt; ++r) v = __fmaf_rn(S.p[g][r], S.v[r][pd], v);
+        acc[j] = v;
+      }
+    }
+    __syncthreads();  // the tile buffers are reused
+  }
+
+  // gather the cluster's partials into CTA 0 (distributed shared memory), then combine in rank order
+  AttnSmem<HD>* root = cluster.map_shared_rank(&S, 0);
+#pragma unroll
+  for (int j = 0; j < GPT; ++j) {
+    const int g = pg0 + j * (kAttnThreads / HD);
+    if (g < G) root->gather[rank][g][2 + pd] = acc[j];
+  }
+  if (tid < G) {
+    root->gather[rank][tid][0] = S.m[tid];
+    root->gather[rank][tid][1] = S.l[tid];
+  }
+  cluster.sync();
+  if (rank != 0) return;
+
+#pragma unroll
+  for (int j = 0; j < GPT; ++j) {
+    const int g = pg0 + j * (kAttnThreads / HD);
+    if (g >= G) continue;
+    float Mx = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < kAttnCluster; ++r) Mx = fmaxf(Mx, S.gather[r][g][0]);
+    float L = 0.0f, out = 0.0f;
+#pragma unroll
+    for (int r = 0; r < kAttnCluster; ++r) {
+      const float mr = S.gather[r][g][0];
+      if (mr == -INFINITY) continue;
+      const float w = expf(__fsub_rn(mr, Mx));
+      L = __fmaf_rn(S.gather[r][g][1], w, L);
+      out = __fmaf_rn(S.gather[r][g][2 + pd], w, out);
+    }
+    if (mpc && !(L > 1e-10f && isfinite(L))) {
+      // compute_mpc_attention_on_shares: weights 1/seq_len when the sum is not usable
+      float u = 0.0f;
+      for (int tt = 0; tt < kv_len; ++tt) u = __fmaf_rn(__fdiv_rn(1.0f, (float)kv_len), V[(size_t)tt * a.kvd + pd], u);
+      out = u;
+    } else {
+      out = __fdiv_rn(out, L);
+    }
+    const int h = qh0 + g;
+    const size_t o = (size_t)m * a.ldo + (size_t)h * HD + pd;
+    const float mk = a.mask ? a.mask[(size_t)m * a.ldmask + (size_t)h * HD + pd] : 0.0f;
     a.Oc[o] = __fsub_rn(out, mk);
     a.Os[o] = mk;
   }
 }
 
-int ensure_attn_scratch(shd_ctx* ctx, size_t floats);
-
-int launch_attention(shd_ctx* ctx, const AttnArgs& a, int M) {
-  const int T = (int)(a.kv_seq_stride / a.kvd);
-  const int chunk_max = (T + a.nsplit - 1) / a.nsplit;
-  const size_t smem = (size_t)(a.head_dim + chunk_max + 34) * 4;
-  if (smem > 200 * 1024) return shd_fail(ctx, SHD_ERR_ARG, "attention: too few splits for this cache length");
+template <int HD>
+static int launch_attn_t(shd_ctx* ctx, const AttnArgs& a, int M) {
   static unsigned attr_devices = 0;
-  if (smem > 48 * 1024 && !(attr_devices & (1u << (ctx->device & 31)))) {
-    SHD_CHECK_CUDA(ctx, cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+  const size_t smem = sizeof(AttnSmem<HD>);
+  if (!(attr_devices & (1u << (ctx->device & 31)))) {
+    SHD_CHECK_CUDA(ctx, cudaFuncSetAttribute(attn_cluster_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attr_devices |= 1u << (ctx->device & 31);
   }
-  const int threads = std::max(64, std::min(256, a.head_dim));
-  dim3 grid(a.nsplit, a.H, M);
-  SHD_CHECK_CUDA(ctx, launch_pdl(attn_decode_kernel, grid, dim3(threads), smem, ctx->stream, a));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kAttnCluster, a.n_groups, M);
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = ctx->stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kAttnCluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  SHD_CHECK_CUDA(ctx, cudaLaunchKernelEx(&cfg, attn_cluster_kernel<HD>, a));
   ctx->launches++;
   return SHD_OK;
 }
+
+int launch_attention(shd_ctx* ctx, const AttnArgs& a, int M) {
+  if (a.head_dim == 128) return launch_attn_t<128>(ctx, a, M);
+  if (a.head_dim == 64) return launch_attn_t<64>(ctx, a, M);
+  return shd_fail(ctx, SHD_ERR_UNSUPPORTED, "attention: head_dim must be 64 or 128");
+}
+
+// Consecutive local q heads with the same kv head, cut into near-equal groups of <= 4.
+std::vector<int4> attn_groups(int q_begin, int q_count, int kv_begin, int group) {
+  std::vector<int4> out;
+  int i = 0;
+  while (i < q_count) {
+    const int kv = (q_begin + i) / group;
+    int n = 0;
+    while (i + n < q_count && (q_begin + i + n) / group == kv) ++n;
+    const int parts = (n + kAttnGroup - 1) / kAttnGroup;
+    int done = 0;
+    for (int p = 0; p < parts; ++p) {
+      const int cnt = (n - done) / (parts - p);
+      out.push_back(make_int4(kv - kv_begin, i + done, cnt, 0));
+      done += cnt;
+    }
+    i += n;
+  }
+  return out;
+}
+
+size_t attn_partial_floats(int, int, int, int) { return 0; }
 
 }  // namespace shd
 
 using namespace shd;
 
-// Scratch for split partials and (row, head) counters, grown outside any stream capture.
-int shd::ensure_attn_scratch(shd_ctx* ctx, size_t floats) {
-  if (floats <= ctx->attn_part_floats) return SHD_OK;
-  SHD_CHECK_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
-  cudaFree(ctx->d_attn_part);
-  ctx->d_attn_part = nullptr;
-  ctx->attn_part_floats = 0;
-  SHD_CHECK_CUDA(ctx, cudaMalloc(&ctx->d_attn_part, floats * 4));
-  ctx->attn_part_floats = floats;
-  return SHD_OK;
-}
+int shd::ensure_attn_scratch(shd_ctx*, size_t) { return SHD_OK; }
 
-// Choose the split count: enough CTAs to cover the SMs twice, chunks of at least 16 positions.
-int shd_attn_splits(int num_sms, int H, int M, int max_len) {
-  int ns = (2 * num_sms + H * M - 1) / (H * M);
-  ns = std::max(1, std::min(ns, 64));
-  ns = std::min(ns, std::max(1, (max_len + 15) / 16));
-  while ((max_len + ns - 1) / ns > 16384) ++ns;
-  return ns;
-}
+int shd_attn_splits(int, int, int, int) { return kAttnCluster; }
 
 extern "C" int shd_attn_decode(shd_ctx* ctx, const float* q, const float* k_cache,
                                const float* v_cache, int kv_capacity, int H, int Hkv, int head_dim,
@@ -184,26 +280,22 @@ extern "C" int shd_attn_decode(shd_ctx* ctx, const float* q, const float* k_cach
   if (!ctx) return SHD_ERR_ARG;
   SHD_REQUIRE(ctx, q && k_cache && v_cache && pos_host && out_c && out_s, "shd_attn_decode: null pointer");
   SHD_REQUIRE(ctx, H > 0 && Hkv > 0 && H % Hkv == 0, "shd_attn_decode: num_heads must be a multiple of num_kv_heads");
-  SHD_REQUIRE(ctx, head_dim > 0 && head_dim % 32 == 0 && head_dim <= 256, "shd_attn_decode: head_dim must be a multiple of 32, <= 256");
+  SHD_REQUIRE(ctx, head_dim == 64 || head_dim == 128, "shd_attn_decode: head_dim must be 64 or 128");
   SHD_REQUIRE(ctx, variant >= 0 && variant <= 2, "shd_attn_decode: unknown variant");
   SHD_REQUIRE(ctx, M > 0 && kv_capacity > 0, "shd_attn_decode: bad shape");
-  int maxp = 0;
-  for (int i = 0; i < M; ++i) {
+  for (int i = 0; i < M; ++i)
     SHD_REQUIRE(ctx, pos_host[i] >= 0 && pos_host[i] < kv_capacity, "shd_attn_decode: position outside the cache");
-    maxp = std::max(maxp, (int)pos_host[i]);
-  }
   SHD_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
-  const int ns = shd_attn_splits(ctx->num_sms, H, M, maxp + 1);
-  const size_t part = (size_t)M * H * ns * (head_dim + 2);
-  int rc = ensure_attn_scratch(ctx, part);
-  if (rc) return rc;
-  // small per-call staging: positions and the q-head -> kv-head map
+  const std::vector<int4> groups = attn_groups(0, H, 0, H / Hkv);
+  const int ng = (int)groups.size();
+  // per-call staging of groups and positions
   int* d_meta = nullptr;
-  SHD_CHECK_CUDA(ctx, cudaMallocAsync(&d_meta, (size_t)(M + H) * 4, ctx->stream));
-  std::vector<int> meta(M + H);
-  for (int i = 0; i < M; ++i) meta[i] = pos_host[i];
-  for (int h = 0; h < H; ++h) meta[M + h] = h / (H / Hkv);
-  SHD_CHECK_CUDA(ctx, cudaMemcpyAsync(d_meta, meta.data(), meta.size() * 4, cudaMemcpyHostToDevice, ctx->stream));
+  const size_t meta_bytes = (size_t)ng * 16 + (size_t)M * 4;
+  SHD_CHECK_CUDA(ctx, cudaMallocAsync(&d_meta, meta_bytes, ctx->stream));
+  std::vector<int> meta(meta_bytes / 4);
+  std::memcpy(meta.data(), groups.data(), (size_t)ng * 16);
+  for (int i = 0; i < M; ++i) meta[4 * ng + i] = pos_host[i];
+  SHD_CHECK_CUDA(ctx, cudaMemcpyAsync(d_meta, meta.data(), meta_bytes, cudaMemcpyHostToDevice, ctx->stream));
   AttnArgs a{};
   a.Q = q;
   a.ldq = H * head_dim;
@@ -211,10 +303,10 @@ extern "C" int shd_attn_decode(shd_ctx* ctx, const float* q, const float* k_cach
   a.Vcache = v_cache;
   a.kvd = Hkv * head_dim;
   a.kv_seq_stride = (int64_t)kv_capacity * a.kvd;
-  a.kv_head_of = d_meta + M;
-  a.H = H;
+  a.groups = reinterpret_cast<const int4*>(d_meta);
+  a.n_groups = ng;
   a.head_dim = head_dim;
-  a.pos = d_meta;
+  a.pos = d_meta + 4 * ng;
   a.seq = nullptr;
   a.variant = variant;
   a.scale = 1.0f / sqrtf((float)head_dim);
@@ -223,14 +315,11 @@ extern "C" int shd_attn_decode(shd_ctx* ctx, const float* q, const float* k_cach
   a.Oc = out_c;
   a.Os = out_s;
   a.ldo = H * head_dim;
-  a.nsplit = ns;
-  a.partials = ctx->d_attn_part;
-  a.counters = ctx->d_counters + (ctx->n_counters - 8192);
+  a.nsplit = kAttnCluster;
   a.err = ctx->d_err;
-  SHD_REQUIRE(ctx, M * H <= 8192, "shd_attn_decode: too many (row, head) pairs");
-  rc = launch_attention(ctx, a, M);
+  int rc = launch_attention(ctx, a, M);
   cudaFreeAsync(d_meta, ctx->stream);
-  // the host vector must outlive the async copy
+  // the host staging vector must outlive the async copy
   cudaError_t e = cudaStreamSynchronize(ctx->stream);
   if (e != cudaSuccess) return shd_cuda_fail(ctx, e, "shd_attn_decode");
   return rc;

@@ -27,7 +27,7 @@
 
 using namespace shd;
 
-int shd_attn_splits(int num_sms, int H, int M, int max_len);
+int shd_attn_splits(int num_sms, int n_groups, int M, int max_len);
 
 namespace {
 
@@ -123,7 +123,7 @@ extern "C" int shd_model_create(shd_ctx* ctx, const shd_model_config* cfg, shd_m
                        c.intermediate > 0 && c.vocab > 0,
               "shd_model_create: empty dimension");
   SHD_REQUIRE(ctx, c.n_heads % c.n_kv_heads == 0, "shd_model_create: n_heads % n_kv_heads != 0");
-  SHD_REQUIRE(ctx, c.head_dim % 32 == 0 && c.head_dim <= 256, "shd_model_create: head_dim must be a multiple of 32, <= 256");
+  SHD_REQUIRE(ctx, c.head_dim == 64 || c.head_dim == 128, "shd_model_create: head_dim must be 64 or 128");
   SHD_REQUIRE(ctx, c.hidden % 4 == 0, "shd_model_create: hidden % 4 != 0");
   SHD_REQUIRE(ctx, c.intermediate % 16 == 0, "shd_model_create: intermediate % 16 != 0");
   SHD_REQUIRE(ctx, c.max_batch >= 1 && c.max_batch <= kMaxRows, "shd_model_create: max_batch must be 1..8");
@@ -178,7 +178,6 @@ extern "C" int shd_model_create(shd_ctx* ctx, const shd_model_config* cfg, shd_m
       {(void**)&m->tokens, R * 4},           {(void**)&m->pos, R * 4},
       {(void**)&m->seq, R * 4},              {(void**)&m->p_pos, R * 4},
       {(void**)&m->p_seq, R * 4},            {(void**)&m->p_tokens, R * 4},
-      {(void**)&m->kv_head_of, (size_t)std::max(m->sh.q_head_count, 1) * 4},
       {(void**)&m->amax, R * 8},             {(void**)&m->step, 8},
       {(void**)&m->hist, (size_t)m->hist_cap * c.max_batch * 4},
       {(void**)&m->final_norm, (size_t)h * 4},
@@ -197,24 +196,29 @@ extern "C" int shd_model_create(shd_ctx* ctx, const shd_model_config* cfg, shd_m
     if (e != cudaSuccess) return fail(shd_cuda_fail(ctx, e, "shd_model_create: cudaMalloc(norm)"));
     m->owned.push_back(L.g2);
   }
-  // sequence-slot and kv-head maps
-  std::vector<int> seqv(R), kvmap(std::max(m->sh.q_head_count, 1));
+  // sequence-slot map and attention head groups (q heads sharing a kv head, <= 8 per group)
+  std::vector<int> seqv(R);
   for (size_t i = 0; i < R; ++i) seqv[i] = (int)i;
   const int group = c.n_heads / c.n_kv_heads;
-  for (int i = 0; i < m->sh.q_head_count; ++i) kvmap[i] = (m->sh.q_head_begin + i) / group - m->sh.kv_head_begin;
+  const std::vector<int4> groups = attn_groups(m->sh.q_head_begin, m->sh.q_head_count, m->sh.kv_head_begin, group);
+  m->n_groups = (int)groups.size();
   cudaError_t e = cudaMemcpy(m->seq, seqv.data(), R * 4, cudaMemcpyHostToDevice);
-  if (e == cudaSuccess) e = cudaMemcpy(m->kv_head_of, kvmap.data(), kvmap.size() * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMalloc(&m->attn_groups_dev, groups.size() * sizeof(int4) + 16);
+  if (e == cudaSuccess) {
+    m->owned.push_back(m->attn_groups_dev);
+    e = cudaMemcpy(m->attn_groups_dev, groups.data(), groups.size() * sizeof(int4), cudaMemcpyHostToDevice);
+  }
   if (e == cudaSuccess) e = cudaMemset(m->step, 0, 8);
   if (e == cudaSuccess) e = cudaMemset(m->kcache, 0, kv_elems * 4);
   if (e == cudaSuccess) e = cudaMemset(m->vcache, 0, kv_elems * 4);
   if (e != cudaSuccess) return fail(shd_cuda_fail(ctx, e, "shd_model_create: init"));
   // attention scratch for the largest launch (kMaxRows rows)
-  m->nsplit = shd_attn_splits(ctx->num_sms, std::max(m->sh.q_head_count, 1), 1, c.max_seq);
-  m->nsplit_prefill = shd_attn_splits(ctx->num_sms, std::max(m->sh.q_head_count, 1), kMaxRows, c.max_seq);
+  m->nsplit = shd_attn_splits(ctx->num_sms, std::max(m->n_groups, 1), c.max_batch, c.max_seq);
+  m->nsplit_prefill = shd_attn_splits(ctx->num_sms, std::max(m->n_groups, 1), kMaxRows, c.max_seq);
   const int ns = std::max(m->nsplit, m->nsplit_prefill);
-  rc = ensure_attn_scratch(ctx, (size_t)R * std::max(m->sh.q_head_count, 1) * ns * (d + 2));
+  rc = ensure_attn_scratch(ctx, attn_partial_floats((int)R, std::max(m->n_groups, 1), ns, d));
   if (rc) return fail(rc);
-  SHD_REQUIRE(ctx, (int)R * std::max(m->sh.q_head_count, 1) <= 8192, "shd_model_create: too many heads x rows");
+  SHD_REQUIRE(ctx, (int)R * std::max(m->n_groups, 1) <= 8192, "shd_model_create: too many head groups x rows");
   *out = m;
   return SHD_OK;
 }
@@ -436,16 +440,18 @@ int shd_model::enqueue_layers(int M, const int* d_pos, const int* d_seq, int var
     AttnArgs at{};
     at.Q = Qbuf; at.ldq = qd;
     at.Kcache = g.Kcache; at.Vcache = g.Vcache; at.kv_seq_stride = g.kv_seq_stride; at.kvd = kvd;
-    at.kv_head_of = kv_head_of; at.H = sh.q_head_count; at.head_dim = d;
+    at.groups = attn_groups_dev; at.n_groups = n_groups; at.head_dim = d;
     at.pos = d_pos; at.seq = d_seq; at.variant = c.variant_attn;
     at.scale = 1.0f / sqrtf((float)d);
     at.mask = lm ? lm + h + (size_t)sh.q_head_begin * d : nullptr; at.ldmask = 0;
     at.Oc = Abuf; at.Os = Abuf + (size_t)M * qd; at.ldo = qd;
-    at.nsplit = (M == 1) ? nsplit : nsplit_prefill;
+    at.nsplit = (M <= cfg.max_batch) ? nsplit : nsplit_prefill;
     at.partials = ctx->d_attn_part;
     at.counters = ctx->d_counters + (ctx->n_counters - 8192);
     at.err = ctx->d_err;
+    if ((rc = prof_mark(5, nullptr, true))) return rc;
     if ((rc = launch_attention(ctx, at, M))) return rc;
+    if ((rc = prof_mark(5, nullptr, false))) return rc;
     // o projection -> D (partial under TP)
     GemvArgs go{};
     go.Xc = Abuf; go.Xs = Abuf + (size_t)M * qd; go.ldx = qd;
@@ -628,7 +634,7 @@ extern "C" int shd_model_decode_async(shd_model* m, int n_steps) {
     rc = m->enqueue_decode_step(M);
     done = 1;
     if (rc == SHD_OK && m->profiling) {
-      const size_t need = (size_t)2 * (4 * m->cfg.n_layers + 1);
+      const size_t need = (size_t)2 * (5 * m->cfg.n_layers + 1);
       while (m->prof_events.size() < need) {
         cudaEvent_t ev;
         if (cudaEventCreate(&ev) != cudaSuccess) { rc = shd_fail(ctx, SHD_ERR_CUDA, "cudaEventCreate"); break; }
@@ -729,7 +735,7 @@ int shd_model::prof_mark(int kind, const shd_weight* w, bool begin) {
   if (prof_next + 1 >= prof_events.size()) return SHD_OK;
   if (begin) {
     prof_kind.push_back(kind);
-    prof_bytes.push_back((double)w->N * (double)w->K * 2.0);
+    prof_bytes.push_back(w ? (double)w->N * (double)w->K * 2.0 : 0.0);
     SHD_CHECK_CUDA(ctx, cudaEventRecordWithFlags(prof_events[prof_next], stream, cudaEventRecordExternal));
   } else {
     SHD_CHECK_CUDA(ctx, cudaEventRecordWithFlags(prof_events[prof_next + 1], stream, cudaEventRecordExternal));
@@ -750,22 +756,22 @@ extern "C" int shd_model_set_profiling(shd_model* m, int on) {
   return SHD_OK;
 }
 
-extern "C" int shd_model_linear_times(shd_model* m, float* ms_out5, double* bytes_out5) {
-  if (!m || !ms_out5 || !bytes_out5) return SHD_ERR_ARG;
+extern "C" int shd_model_linear_times(shd_model* m, float* ms_out6, double* bytes_out6) {
+  if (!m || !ms_out6 || !bytes_out6) return SHD_ERR_ARG;
   shd_ctx* ctx = m->ctx;
   SHD_REQUIRE(ctx, m->prof_count > 0, "shd_model_linear_times: no profiled decode step yet");
   SHD_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
   SHD_CHECK_CUDA(ctx, cudaStreamSynchronize(m->stream));
-  for (int k = 0; k < 5; ++k) {
-    ms_out5[k] = 0.f;
-    bytes_out5[k] = 0.0;
+  for (int k = 0; k < 6; ++k) {
+    ms_out6[k] = 0.f;
+    bytes_out6[k] = 0.0;
   }
   for (size_t i = 0; i + 1 < m->prof_count; i += 2) {
     float ms = 0.f;
     SHD_CHECK_CUDA(ctx, cudaEventElapsedTime(&ms, m->prof_events[i], m->prof_events[i + 1]));
     const int k = m->prof_kind[i / 2];
-    ms_out5[k] += ms;
-    bytes_out5[k] += m->prof_bytes[i / 2];
+    ms_out6[k] += ms;
+    bytes_out6[k] += m->prof_bytes[i / 2];
   }
   return SHD_OK;
 }

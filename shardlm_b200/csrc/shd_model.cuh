@@ -36,7 +36,8 @@ struct shd_model {
   float *kcache = nullptr, *vcache = nullptr;  // [L][slots][T][kvd]
   int *tokens = nullptr, *pos = nullptr, *seq = nullptr;
   int *p_tokens = nullptr, *p_pos = nullptr, *p_seq = nullptr;
-  int* kv_head_of = nullptr;
+  int4* attn_groups_dev = nullptr;  // attention head groups (kv head, first q head, count)
+  int n_groups = 0;
   unsigned long long* amax = nullptr;
   unsigned long long* step = nullptr;
   int* hist = nullptr;

@@ -1,6 +1,8 @@
 // Internal interface of the nonlinear, embedding and attention kernels (used by the model loop).
 #pragma once
 
+#include <vector>
+
 #include "shd_common.cuh"
 
 namespace shd {
@@ -46,6 +48,8 @@ struct EmbedArgs {
 int launch_embed(shd_ctx* ctx, const EmbedArgs& a, int M);
 int launch_keys_to_tokens(shd_ctx* ctx, const unsigned long long* keys, int* tokens, int M);
 
+constexpr int kAttnGroupMax = 8;  // q heads handled together (sharing one kv head)
+
 struct AttnArgs {
   const float* Q;          // reconstructed queries [M][ldq], local heads
   int ldq;
@@ -53,9 +57,9 @@ struct AttnArgs {
   const float* Vcache;
   int64_t kv_seq_stride;   // floats between sequence slots
   int kvd;                 // local kv heads * head_dim
-  const int* kv_head_of;   // [H] local kv head of each local q head (device)
-  int H;                   // local q heads
-  int head_dim;
+  const int4* groups;      // [n_groups] (local kv head, first local q head, q head count <= 8, 0)
+  int n_groups;
+  int head_dim;            // 64 or 128
   const int* pos;          // [M] position of the query row; it attends to [0, pos]
   const int* seq;          // [M] sequence slot (nullable -> 0)
   int variant;             // SHD_NL_APPROX/GPU: clamp(-40,40); SHD_NL_MPC: plain exp
@@ -66,13 +70,17 @@ struct AttnArgs {
   float* Os;
   int ldo;
   int nsplit;
-  float* partials;         // [M][H][nsplit][head_dim + 2]
-  int* counters;           // [M][H]
+  float* partials;         // [M][n_groups][nsplit][kAttnGroupMax][head_dim + 2]
+  int* counters;           // [M][n_groups]
   int* err;
 };
 
 int launch_attention(shd_ctx* ctx, const AttnArgs& a, int M);
 int ensure_attn_scratch(shd_ctx* ctx, size_t floats);
+// Groups of at most kAttnGroupMax consecutive local q heads sharing one kv head. Local q heads are
+// [q_begin, q_begin + q_count) of the model, local kv heads start at kv_begin; group = H / Hkv.
+std::vector<int4> attn_groups(int q_begin, int q_count, int kv_begin, int group);
+size_t attn_partial_floats(int M, int n_groups, int nsplit, int head_dim);
 
 int shd_build_rope(shd_ctx* ctx, int head_dim, int max_seq, float theta);
 // RopeFrequencies::new table ([max_seq][head_dim/2] cos and sin) in new device allocations.
