@@ -110,6 +110,20 @@ int shd_linear_dual_f32(shd_ctx* ctx, const shd_weight* w, const float* bias, co
                         const float* xs, float* yc, float* ys, int M, const float* residual_c,
                         const float* residual_s);
 
+/* Allocation-free form of shd_linear_dual_f32 (no counterpart in the reference). For callers that
+ * cannot allocate device memory while they run a layer -- a host framework that owns and freezes the
+ * GPU's memory up front, or a request path that must not allocate. Same computation and arguments
+ * (weight from an earlier shd_weight_* call; stream = the caller's cudaStream_t, NULL = legacy
+ * default stream), but the split-K scratch is a static device array of about 1.3 MB that every GPU
+ * loading the library keeps until exit; nothing is allocated or freed. Limits: out_features <=
+ * 262144, in_features % 4 == 0 and 16-byte aligned rows (SHD_ERR_ARG otherwise). The first call on
+ * a device looks up the array's device address; make it before any stream capture. All calls share
+ * the array (its tile counters are cleared at the start of each call): calls that overlap on the GPU
+ * race. Device-side timeouts are not reported by this entry point. */
+int shd_linear_dual_f32_noalloc(const shd_weight* w, const float* bias, const float* xc,
+                                const float* xs, float* yc, float* ys, int M,
+                                const float* residual_c, const float* residual_s, void* stream);
+
 /* LinearServer::handle_request / multiply_vector (crates/sharing/src/linear.rs:204-274), bit-exact:
  *   acc_j = sum_i (i64)x_i * (i64)W_ij (wrapping), y_j = (i32)(acc_j >> scale),
  *   ys_j = ys_j wrapping_add bias_j (bias from the weight, or `bias` when non-null).

@@ -53,6 +53,7 @@ SIGNATURES: dict[str, tuple] = {
     "shd_weight_device_bytes": (I64, [P]),
     "shd_linear_dual_f32": (I32, [P, P, P, P, P, P, P, I32, P, P]),
     "shd_linear_dual_ring": (I32, [P, P, P, P, P, P, P, I32, I32]),
+    "shd_linear_dual_f32_noalloc": (I32, [P, P, P, P, P, P, I32, P, P, P]),
     "shd_reconstruct_f32": (I32, [P, P, P, P, I64]),
     "shd_reshare_f32": (I32, [P, P, P, P, P, I64]),
     "shd_add_shares": (I32, [P, P, P, P, P, P, P, I64]),
