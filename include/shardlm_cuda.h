@@ -268,6 +268,13 @@ typedef struct shd_shard_info {
 int shd_model_create(shd_ctx* ctx, const shd_model_config* cfg, shd_model** out);
 int shd_model_destroy(shd_model* m);
 int shd_model_shard_info(const shd_model* m, shd_shard_info* out);
+/* The same slice computed on the host for any (tp_rank, tp_world) of `cfg`, without a device or a
+ * context (no counterpart in the reference, whose TP refuses head counts that do not divide,
+ * crates/v2/core/src/parallel.rs:89-98). Query heads and vocab rows split evenly (the last rank
+ * takes the remainder), the intermediate dimension in blocks of 16; kv heads are those the local
+ * query heads read, so a kv head shared by two ranks is replicated on both. SHD_ERR_ARG on a
+ * config shd_model_create would refuse for its shape or rank. */
+int shd_tp_plan(const shd_model_config* cfg, shd_shard_info* out);
 /* Layer weights of this rank's shard, DEVICE bf16 in [out][in] (safetensors) layout; copied.
  * wq [q_count*d][h], wk/wv [kv_count*d][h], wo [h][q_count*d], wg/wu [inter_count][h],
  * wd [h][inter_count]; biases f32 (nullable); norms f32 [h]. */

@@ -77,6 +77,7 @@ SIGNATURES: dict[str, tuple] = {
     "shd_model_create": (I32, [P, P, PP]),
     "shd_model_destroy": (I32, [P]),
     "shd_model_shard_info": (I32, [P, P]),
+    "shd_tp_plan": (I32, [P, P]),
     "shd_model_set_layer": (I32, [P, I32] + [P] * 12),
     "shd_model_set_embedding": (I32, [P, P]),
     "shd_model_set_head": (I32, [P, P, P]),

@@ -382,12 +382,21 @@ __device__ __forceinline__ unsigned long long bf16pair(uint32_t q) {
 }
 
 // RMSNorm prologue: x = reshare(RMSNorm(D + H)) for M rows into xres[m][share][KP] (zero padded).
-// Every CTA computes the identical values (same thread mapping, fixed reduction order).
+// Every CTA computes the identical values (same thread mapping, fixed reduction order). Each thread
+// owns float4 groups i = ctid + 256 j; the loads of a block of kNormGroups groups (and of gamma and
+// the mask) are all issued before any is used, so a CTA waits on L2 about twice per row instead of
+// once per group.
+constexpr int kNormGroups = 4;
+
 template <int M>
 __device__ bool norm_prologue(const GemvArgs& a, const PipeSmem& sm, uint32_t& cphase, float* xres,
                               int KP, int ctid, int lane, int warp, bool write_h) {
+  constexpr int NJ = kNormGroups;
+  constexpr int STEP = kConsumerWarps * 32;
   const int K = a.K;
-  const int K4 = K >> 2;
+  const int K4 = K >> 2, KP4 = KP >> 2;
+  const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  const bool g_vec = (reinterpret_cast<uintptr_t>(a.gamma) & 15) == 0;
   for (int m = 0; m < M; ++m) {
     const float4* hc = reinterpret_cast<const float4*>(a.nHc + (size_t)m * a.n_ldh);
     const float4* hs = reinterpret_cast<const float4*>(a.nHs + (size_t)m * a.n_ldh);
@@ -396,24 +405,50 @@ __device__ bool norm_prologue(const GemvArgs& a, const PipeSmem& sm, uint32_t& c
     float4* oc = (write_h && a.nHout_c) ? reinterpret_cast<float4*>(a.nHout_c + (size_t)m * a.n_ldh) : nullptr;
     float4* os = (write_h && a.nHout_s) ? reinterpret_cast<float4*>(a.nHout_s + (size_t)m * a.n_ldh) : nullptr;
     float* xr = xres + (size_t)(m * 2) * KP;
+    float4* xr4 = reinterpret_cast<float4*>(xr);
     float ss = 0.0f;
-    for (int i = ctid; i < K4; i += kConsumerWarps * 32) {
-      float4 c = hc[i], s = hs[i];
+    for (int b = 0; b < K4; b += NJ * STEP) {
+      float4 c[NJ], s[NJ];
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) {
+        const int i = b + ctid + j * STEP;
+        c[j] = (i < K4) ? hc[i] : z4;
+        s[j] = (i < K4) ? hs[i] : z4;
+      }
       if (dc) {
-        const float4 e = dc[i], f = ds[i];
-        c = make_float4(__fadd_rn(e.x, c.x), __fadd_rn(e.y, c.y), __fadd_rn(e.z, c.z), __fadd_rn(e.w, c.w));
-        s = make_float4(__fadd_rn(f.x, s.x), __fadd_rn(f.y, s.y), __fadd_rn(f.z, s.z), __fadd_rn(f.w, s.w));
-        if (oc) {
-          oc[i] = c;
-          os[i] = s;
+        float4 e[NJ], f[NJ];
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+          const int i = b + ctid + j * STEP;
+          e[j] = (i < K4) ? dc[i] : z4;
+          f[j] = (i < K4) ? ds[i] : z4;
+        }
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+          const int i = b + ctid + j * STEP;
+          c[j] = make_float4(__fadd_rn(e[j].x, c[j].x), __fadd_rn(e[j].y, c[j].y), __fadd_rn(e[j].z, c[j].z),
+                             __fadd_rn(e[j].w, c[j].w));
+          s[j] = make_float4(__fadd_rn(f[j].x, s[j].x), __fadd_rn(f[j].y, s[j].y), __fadd_rn(f[j].z, s[j].z),
+                             __fadd_rn(f[j].w, s[j].w));
+          if (oc && i < K4) {
+            oc[i] = c[j];
+            os[i] = s[j];
+          }
         }
       }
-      const float4 x = make_float4(__fadd_rn(c.x, s.x), __fadd_rn(c.y, s.y), __fadd_rn(c.z, s.z), __fadd_rn(c.w, s.w));
-      reinterpret_cast<float4*>(xr)[i] = x;
-      ss = __fmaf_rn(x.x, x.x, ss);
-      ss = __fmaf_rn(x.y, x.y, ss);
-      ss = __fmaf_rn(x.z, x.z, ss);
-      ss = __fmaf_rn(x.w, x.w, ss);
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) {
+        const int i = b + ctid + j * STEP;
+        if (i < K4) {
+          const float4 x = make_float4(__fadd_rn(c[j].x, s[j].x), __fadd_rn(c[j].y, s[j].y),
+                                       __fadd_rn(c[j].z, s[j].z), __fadd_rn(c[j].w, s[j].w));
+          xr4[i] = x;
+          ss = __fmaf_rn(x.x, x.x, ss);
+          ss = __fmaf_rn(x.y, x.y, ss);
+          ss = __fmaf_rn(x.z, x.z, ss);
+          ss = __fmaf_rn(x.w, x.w, ss);
+        }
+      }
     }
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
@@ -434,17 +469,46 @@ __device__ bool norm_prologue(const GemvArgs& a, const PipeSmem& sm, uint32_t& c
         inv = __fdiv_rn(1.0f, rms);
     }
     const float* mk = a.nmask ? a.nmask + (size_t)m * a.n_ldmask : nullptr;
-    for (int i = ctid; i < KP; i += kConsumerWarps * 32) {
-      float xc = 0.0f, xs = 0.0f;
-      if (i < K) {
-        float r = __fmul_rn(__fmul_rn(xr[i], inv), a.gamma[i]);
-        if (a.nvariant == SHD_NL_MPC && !isfinite(r)) r = 0.0f;
-        const float mv = mk ? mk[i] : 0.0f;
-        xc = __fsub_rn(r, mv);
-        xs = mv;
+    const bool m_vec = (reinterpret_cast<uintptr_t>(mk) & 15) == 0;
+    for (int b = 0; b < KP4; b += NJ * STEP) {
+      float4 gv[NJ], mv[NJ];
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) {
+        const int i = b + ctid + j * STEP;
+        gv[j] = z4;
+        mv[j] = z4;
+        if (i < K4) {
+          gv[j] = g_vec ? reinterpret_cast<const float4*>(a.gamma)[i]
+                        : make_float4(a.gamma[4 * i], a.gamma[4 * i + 1], a.gamma[4 * i + 2], a.gamma[4 * i + 3]);
+          if (mk)
+            mv[j] = m_vec ? reinterpret_cast<const float4*>(mk)[i]
+                          : make_float4(mk[4 * i], mk[4 * i + 1], mk[4 * i + 2], mk[4 * i + 3]);
+        }
       }
-      xr[i] = xc;
-      xr[KP + i] = xs;
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) {
+        const int i = b + ctid + j * STEP;
+        if (i >= KP4) continue;
+        float4 xc = z4, xs = z4;
+        if (i < K4) {
+          const float4 x = xr4[i];
+          float r0 = __fmul_rn(__fmul_rn(x.x, inv), gv[j].x);
+          float r1 = __fmul_rn(__fmul_rn(x.y, inv), gv[j].y);
+          float r2 = __fmul_rn(__fmul_rn(x.z, inv), gv[j].z);
+          float r3 = __fmul_rn(__fmul_rn(x.w, inv), gv[j].w);
+          if (a.nvariant == SHD_NL_MPC) {
+            if (!isfinite(r0)) r0 = 0.0f;
+            if (!isfinite(r1)) r1 = 0.0f;
+            if (!isfinite(r2)) r2 = 0.0f;
+            if (!isfinite(r3)) r3 = 0.0f;
+          }
+          xc = make_float4(__fsub_rn(r0, mv[j].x), __fsub_rn(r1, mv[j].y), __fsub_rn(r2, mv[j].z),
+                           __fsub_rn(r3, mv[j].w));
+          xs = mv[j];
+        }
+        xr4[i] = xc;
+        reinterpret_cast<float4*>(xr + KP)[i] = xs;
+      }
     }
     if (!consumer_sync(sm, cphase, lane)) return false;  // red reuse and xres visibility
   }

@@ -255,6 +255,17 @@ extern "C" int shd_model_shard_info(const shd_model* m, shd_shard_info* out) {
   return SHD_OK;
 }
 
+extern "C" int shd_tp_plan(const shd_model_config* cfg, shd_shard_info* out) {
+  if (!cfg || !out) return SHD_ERR_ARG;
+  const shd_model_config& c = *cfg;
+  if (c.n_heads <= 0 || c.n_kv_heads <= 0 || c.intermediate <= 0 || c.vocab <= 0 ||
+      c.n_heads % c.n_kv_heads != 0 || c.intermediate % 16 != 0 || c.tp_world < 1 ||
+      c.tp_rank < 0 || c.tp_rank >= c.tp_world || c.tp_world > c.n_heads)
+    return SHD_ERR_ARG;
+  make_plan(c, *out);
+  return SHD_OK;
+}
+
 extern "C" int shd_model_seq_len(const shd_model* m, int slot) {
   if (!m || slot < 0 || slot >= m->cfg.max_batch) return SHD_ERR_ARG;
   return m->len[slot];

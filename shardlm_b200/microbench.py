@@ -4,7 +4,9 @@
                                            [--rows 1] [--iters 20]
   python -m shardlm_b200.microbench beaver [--n 9699328] [--iters 20]
   python -m shardlm_b200.microbench ring   [--copies 16] [--iters 20]
+  python -m shardlm_b200.microbench attn   [--model qwen2.5-7b] [--kv-len 577] [--iters 20]
 
+--graph times a captured CUDA graph of the launches instead of host-issued launches.
 Each weight kind is instantiated in enough copies to exceed the 126 MB L2, and launches rotate over
 the copies, so every launch streams its weights from HBM.
 """
@@ -23,14 +25,28 @@ from .sharing import GpuSecureLinear
 L2_BYTES = 126 * 2**20
 
 
+GRAPH = False  # --graph: time a CUDA graph of `iters` back-to-back launches (no host launch cost)
+
+
 def _time(fn, iters: int) -> float:
     for _ in range(3):
         fn(0)
     torch.cuda.synchronize()
+    g = None
+    if GRAPH:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(iters):
+                fn(i)
+        g.replay()
+        torch.cuda.synchronize()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
-    for i in range(iters):
-        fn(i)
+    if g is not None:
+        g.replay()
+    else:
+        for i in range(iters):
+            fn(i)
     e.record()
     torch.cuda.synchronize()
     return s.elapsed_time(e) / iters
@@ -105,18 +121,45 @@ def ring(args, ctx: Context):
     print(json.dumps({"ring_linear_1536": {"us": round(ms * 1e3, 2), "GBps": round(b / ms / 1e6, 1)}}))
 
 
+def attn(args, ctx: Context):
+    """Decode attention over reconstructed caches (one query row at position kv_len - 1)."""
+    sh = SHAPES[args.model]
+    H, Hkv, d, L = sh.n_heads, sh.n_kv_heads, sh.head_dim, args.kv_len
+    cap = L + 16
+    copies = max(1, -(-2 * L2_BYTES // (2 * cap * Hkv * d * 4)))
+    ks = [torch.randn(cap, Hkv * d, device="cuda") for _ in range(copies)]
+    vs = [torch.randn(cap, Hkv * d, device="cuda") for _ in range(copies)]
+    q = torch.randn(H * d, device="cuda")
+    oc, os_ = torch.empty(H * d, device="cuda"), torch.empty(H * d, device="cuda")
+    pos = np.array([L - 1], np.int32)
+
+    def run(i):
+        ctx.call("shd_attn_decode", ptr(q), ptr(ks[i % copies]), ptr(vs[i % copies]), cap, H, Hkv, d,
+                 pos.ctypes.data, 1, 0, None, ptr(oc), ptr(os_))
+
+    ms = _time(run, args.iters)
+    ctx.sync()
+    kv_bytes = 2 * L * Hkv * d * 4
+    print(json.dumps({"attn": {"H": H, "Hkv": Hkv, "kv_len": L, "us": round(ms * 1e3, 2),
+                               "GBps": round(kv_bytes / ms / 1e6, 1)}}))
+
+
 def main():
     p = argparse.ArgumentParser()
-    p.add_argument("what", choices=["linear", "beaver", "ring"])
+    p.add_argument("what", choices=["linear", "beaver", "ring", "attn"])
+    p.add_argument("--kv-len", type=int, default=577)
     p.add_argument("--model", default="qwen2.5-7b")
     p.add_argument("--kind", default="all")
     p.add_argument("--rows", type=int, default=1)
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--n", type=int, default=512 * 18944)
     p.add_argument("--copies", type=int, default=16)
+    p.add_argument("--graph", action="store_true")
     args = p.parse_args()
+    global GRAPH
+    GRAPH = args.graph
     ctx = Context(0)
-    {"linear": linear, "beaver": beaver, "ring": ring}[args.what](args, ctx)
+    {"linear": linear, "beaver": beaver, "ring": ring, "attn": attn}[args.what](args, ctx)
 
 
 if __name__ == "__main__":
