@@ -37,6 +37,8 @@ def parse():
     p.add_argument("--e2e-steps", type=int, default=24)
     p.add_argument("--cpu-sample-steps", type=int, default=2)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--engine", type=int, default=0, choices=[0, 1],
+                   help="decode engine: 0 = one kernel per operation (default), 1 = one persistent kernel per step")
     return p.parse_args()
 
 
@@ -208,6 +210,7 @@ def run_ours(args, shape):
     prof_steps = 3
     max_seq = args.prompt + args.warmup + args.steps + prof_steps + e2e_steps + 8
     model = SecureModel(ctx, shape, max_seq=max_seq, max_batch=B, share_seed=0x5EED, tp_rank=rank, tp_world=world)
+    model.set_engine(args.engine)
     model.load_random_weights(seed=0)
     rng = np.random.default_rng(0)  # seeded uniform prompt token ids
     for b in range(B):

@@ -314,9 +314,23 @@ int64_t shd_model_step_launches(const shd_model* m);
  * and attention launch; shd_model_linear_times then returns, for the most recent step, the summed
  * device time (ms) and the summed weight bytes of the launches of each kind: [0] qkv, [1] o,
  * [2] gate/up, [3] down, [4] lm_head, [5] attention (bytes 0). Turning it on or off re-captures
- * the graph at the next decode. */
+ * the graph at the next decode. With the persistent step kernel (shd_model_set_engine) the times
+ * are, per kind, the summed spans from the first CTA starting a job of that kind to the last one
+ * finishing it (%globaltimer inside the kernel), averaged over the decode steps run since
+ * profiling was turned on. */
 int shd_model_set_profiling(shd_model* m, int on);
 int shd_model_linear_times(shd_model* m, float* ms_out6, double* bytes_out6);
+/* Decode engine (no counterpart in the reference, whose decode is host-driven). 0 (default): one
+ * kernel per operation, chained by programmatic dependent launch in a captured graph (always used
+ * under tensor parallelism, for prefill and for shd_model_forward_host). 1: on a single GPU
+ * (tp_world == 1) each decode step is ONE persistent kernel (one or two CTAs per SM, all resident)
+ * running the embedding, every layer, the head and the token update as a job list with grid
+ * barriers between jobs, its weight stream running ahead across them; same results within the f32
+ * tolerance. On B200 the per-job barriers currently cost more than the overlap gains (7B decode
+ * ~260 vs ~330 tok/s), hence the default. Switching re-captures the graph at the next decode. */
+int shd_model_set_engine(shd_model* m, int engine);
+/* 1 when the last decode used the persistent step kernel, else 0. */
+int shd_model_engine(const shd_model* m);
 
 #ifdef __cplusplus
 }

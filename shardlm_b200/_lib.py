@@ -91,6 +91,8 @@ SIGNATURES: dict[str, tuple] = {
     "shd_model_step_launches": (I64, [P]),
     "shd_model_set_profiling": (I32, [P, I32]),
     "shd_model_linear_times": (I32, [P, P, P]),
+    "shd_model_set_engine": (I32, [P, I32]),
+    "shd_model_engine": (I32, [P]),
 }
 
 

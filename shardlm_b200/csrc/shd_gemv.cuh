@@ -96,6 +96,9 @@ struct GemvArgs {
 // Launch the f32-share GEMV for M rows with the given epilogue; `norm` selects the fused RMSNorm
 // prologue (x from nHc/nHs/...) instead of staged activations (Xc/Xs).
 int launch_gemv_f32(shd_ctx* ctx, const shd_weight* w, int M, int epi, GemvArgs a, bool norm = false);
+// Fill the weight, shape and scratch fields of `a` for `w` (what launch_gemv_f32 adds before a
+// launch); the persistent step kernel records jobs with it.
+int gemv_prepare(shd_ctx* ctx, const shd_weight* w, GemvArgs& a, bool norm);
 
 struct RingArgs {
   const uint8_t* W;

@@ -225,6 +225,7 @@ extern "C" int shd_model_create(shd_ctx* ctx, const shd_model_config* cfg, shd_m
 
 shd_model::~shd_model() {
   if (graph) cudaGraphExecDestroy(graph);
+  shd::step_plan_free(step_plan);
   for (cudaEvent_t ev : prof_events) cudaEventDestroy(ev);
   for (auto& L : layers) {
     shd_weight_destroy(L.qkv);
@@ -416,7 +417,68 @@ int shd_model::norm_into(GemvArgs& g, const shd_weight* w, int M, const float* H
   na.gamma = gamma; na.eps = cfg.rms_eps; na.variant = variant; na.mask = mask; na.ldmask = 0;
   na.Xc = Xbuf; na.Xs = Xbuf + (size_t)M * h; na.ldx = h; na.n = h;
   g.Xc = Xbuf; g.Xs = Xbuf + (size_t)M * h; g.ldx = h;
-  return launch_norm(ctx, na, M);
+  return op_norm(na, M);
+}
+
+int shd_model::op_gemv(const shd_weight* w, int M, int epi, const GemvArgs& g, bool norm, int kind) {
+  if (!rec) return launch_gemv_f32(ctx, w, M, epi, g, norm);
+  StepJob j{};
+  j.type = JOB_GEMV;
+  j.epi = epi;
+  j.norm = norm ? 1 : 0;
+  j.kind = kind;
+  j.bytes = (double)w->N * (double)w->K * 2.0;
+  j.g = g;
+  const int rc = gemv_prepare(ctx, w, j.g, norm);
+  if (rc) return rc;
+  rec->push_back(j);
+  return SHD_OK;
+}
+
+int shd_model::op_attn(const AttnArgs& at, int M) {
+  if (!rec) return launch_attention(ctx, at, M);
+  StepJob j{};
+  j.type = JOB_ATTN;
+  j.kind = KIND_ATTN;
+  j.at = at;
+  rec->push_back(j);
+  return SHD_OK;
+}
+
+int shd_model::op_norm(const NormArgs& na, int M) {
+  if (!rec) return launch_norm(ctx, na, M);
+  StepJob j{};
+  j.type = JOB_NORM;
+  j.kind = KIND_OTHER;
+  j.na = na;
+  rec->push_back(j);
+  return SHD_OK;
+}
+
+int shd_model::op_embed(const EmbedArgs& ea, int M) {
+  if (!rec) return launch_embed(ctx, ea, M);
+  StepJob j{};
+  j.type = JOB_EMBED;
+  j.kind = KIND_OTHER;
+  j.ea = ea;
+  rec->push_back(j);
+  return SHD_OK;
+}
+
+// Record the decode step of M rows as a job list and upload it for the persistent kernel.
+// SHD_ERR_UNSUPPORTED leaves the per-kernel path in use.
+int shd_model::build_step(int M) {
+  std::vector<StepJob> jobs;
+  rec = &jobs;
+  int rc = enqueue_decode_step(M);
+  rec = nullptr;
+  if (rc) return rc;
+  rc = shd::step_plan_build(ctx, step_plan, jobs, M);
+  if (rc == SHD_ERR_UNSUPPORTED) {
+    ctx->last_error.clear();
+    return SHD_OK;
+  }
+  return rc;
 }
 
 int shd_model::enqueue_layers(int M, const int* d_pos, const int* d_seq, int variant, int& cur) {
@@ -445,7 +507,7 @@ int shd_model::enqueue_layers(int M, const int* d_pos, const int* d_seq, int var
     g.Kcache = kcache + (size_t)l * kv_layer; g.Vcache = vcache + (size_t)l * kv_layer;
     g.kv_seq_stride = (int64_t)c.max_seq * kvd;
     if ((rc = prof_mark(0, Lw.qkv, true))) return rc;
-    if ((rc = launch_gemv_f32(ctx, Lw.qkv, M, EPI_QKV, g, fused))) return rc;
+    if ((rc = op_gemv(Lw.qkv, M, EPI_QKV, g, fused, KIND_QKV))) return rc;
     if ((rc = prof_mark(0, Lw.qkv, false))) return rc;
     // attention -> A shares
     AttnArgs at{};
@@ -461,14 +523,14 @@ int shd_model::enqueue_layers(int M, const int* d_pos, const int* d_seq, int var
     at.counters = ctx->d_counters + (ctx->n_counters - 8192);
     at.err = ctx->d_err;
     if ((rc = prof_mark(5, nullptr, true))) return rc;
-    if ((rc = launch_attention(ctx, at, M))) return rc;
+    if ((rc = op_attn(at, M))) return rc;
     if ((rc = prof_mark(5, nullptr, false))) return rc;
     // o projection -> D (partial under TP)
     GemvArgs go{};
     go.Xc = Abuf; go.Xs = Abuf + (size_t)M * qd; go.ldx = qd;
     go.Yc = Dbuf; go.Ys = Dbuf + (size_t)M * h; go.ldy = h;
     if ((rc = prof_mark(1, Lw.o, true))) return rc;
-    if ((rc = launch_gemv_f32(ctx, Lw.o, M, EPI_STORE, go))) return rc;
+    if ((rc = op_gemv(Lw.o, M, EPI_STORE, go, false, KIND_O))) return rc;
     if ((rc = prof_mark(1, Lw.o, false))) return rc;
     if ((rc = allreduce_sum(Dbuf, (size_t)2 * M * h))) return rc;
     // post-attention norm (h = D + Ho -> Hc) + gate/up + SwiGLU reshare -> ACT
@@ -480,14 +542,14 @@ int shd_model::enqueue_layers(int M, const int* d_pos, const int* d_seq, int var
     gu.variant = variant;
     gu.mask = lm ? lm + 3 * (size_t)h + sh.inter_begin : nullptr; gu.ldmask = 0;
     if ((rc = prof_mark(2, Lw.gateup, true))) return rc;
-    if ((rc = launch_gemv_f32(ctx, Lw.gateup, M, EPI_GATEUP, gu, fused))) return rc;
+    if ((rc = op_gemv(Lw.gateup, M, EPI_GATEUP, gu, fused, KIND_GATEUP))) return rc;
     if ((rc = prof_mark(2, Lw.gateup, false))) return rc;
     // down -> D
     GemvArgs gd{};
     gd.Xc = ACTbuf; gd.Xs = ACTbuf + (size_t)M * I; gd.ldx = I;
     gd.Yc = Dbuf; gd.Ys = Dbuf + (size_t)M * h; gd.ldy = h;
     if ((rc = prof_mark(3, Lw.down, true))) return rc;
-    if ((rc = launch_gemv_f32(ctx, Lw.down, M, EPI_STORE, gd))) return rc;
+    if ((rc = op_gemv(Lw.down, M, EPI_STORE, gd, false, KIND_DOWN))) return rc;
     if ((rc = prof_mark(3, Lw.down, false))) return rc;
     if ((rc = allreduce_sum(Dbuf, (size_t)2 * M * h))) return rc;
     // the residual stream for the next layer is (Hc, D)
@@ -527,7 +589,7 @@ int shd_model::enqueue_head_rows(int M, int cur, int variant) {
   g.amax = amax;
   g.idx_offset = sh.vocab_begin;
   if ((rc = prof_mark(4, lm_head, true))) return rc;
-  if ((rc = launch_gemv_f32(ctx, lm_head, M, EPI_LOGITS, g, fused))) return rc;
+  if ((rc = op_gemv(lm_head, M, EPI_LOGITS, g, fused, KIND_HEAD))) return rc;
   return prof_mark(4, lm_head, false);
 }
 
@@ -610,10 +672,13 @@ int shd_model::enqueue_decode_step(int M) {
   ea.Dc = Dbuf; ea.Ds = Dbuf + (size_t)M * h; ea.amax = amax; ea.err = ctx->d_err;
   ea.slot_counter = 1;
   int rc;
-  if ((rc = launch_embed(ctx, ea, M))) return rc;
+  if (!rec && step_usable(M))
+    return shd::step_launch(ctx, step_plan, stream, amax, tokens, pos, hist, hist_cap, step, profiling != 0);
+  if ((rc = op_embed(ea, M))) return rc;
   int cur = 0;
   if ((rc = enqueue_layers(M, pos, seq, cfg.variant_decode, cur))) return rc;
   if ((rc = enqueue_head_rows(M, cur, cfg.variant_decode))) return rc;
+  if (rec) return SHD_OK;  // the step kernel does the token update itself
   if ((rc = allreduce_max_keys(M))) return rc;
   SHD_CHECK_CUDA(ctx, launch_pdl(finish_step_kernel, dim3(1), dim3(32), 0, stream, (const unsigned long long*)amax,
                                  tokens, pos, hist, hist_cap, step, M));
@@ -641,8 +706,10 @@ extern "C" int shd_model_decode_async(shd_model* m, int n_steps) {
       cudaGraphExecDestroy(m->graph);
       m->graph = nullptr;
     }
-    // one eager step (sets kernel attributes, real work), then capture the step
-    rc = m->enqueue_decode_step(M);
+    // the persistent step for this batch size (single GPU), then one eager step (sets kernel
+    // attributes, real work), then capture the step
+    if (m->engine == 1 && ctx->tp_world <= 1 && m->step_plan.M != M) rc = m->build_step(M);
+    if (rc == SHD_OK) rc = m->enqueue_decode_step(M);
     done = 1;
     if (rc == SHD_OK && m->profiling) {
       const size_t need = (size_t)2 * (5 * m->cfg.n_layers + 1);
@@ -742,7 +809,7 @@ extern "C" int shd_model_forward_host(shd_model* m, int slot, const float* hc_ho
 }
 
 int shd_model::prof_mark(int kind, const shd_weight* w, bool begin) {
-  if (!prof_active) return SHD_OK;
+  if (!prof_active || rec) return SHD_OK;
   if (prof_next + 1 >= prof_events.size()) return SHD_OK;
   if (begin) {
     prof_kind.push_back(kind);
@@ -764,15 +831,41 @@ extern "C" int shd_model_set_profiling(shd_model* m, int on) {
     m->graph = nullptr;
   }
   m->profiling = on != 0;
+  if (m->profiling && m->step_plan.d_prof) {
+    SHD_CHECK_CUDA(m->ctx, cudaSetDevice(m->ctx->device));
+    const int rc = shd::step_prof_reset(m->ctx, m->step_plan, m->stream);
+    if (rc) return rc;
+    SHD_CHECK_CUDA(m->ctx, cudaStreamSynchronize(m->stream));
+  }
   return SHD_OK;
+}
+
+extern "C" int shd_model_set_engine(shd_model* m, int engine) {
+  if (!m) return SHD_ERR_ARG;
+  SHD_REQUIRE(m->ctx, engine == 0 || engine == 1, "shd_model_set_engine: engine must be 0 or 1");
+  if (engine != m->engine) {
+    if (m->graph) {
+      cudaGraphExecDestroy(m->graph);
+      m->graph = nullptr;
+    }
+    shd::step_plan_free(m->step_plan);
+    m->engine = engine;
+  }
+  return SHD_OK;
+}
+
+extern "C" int shd_model_engine(const shd_model* m) {
+  if (!m) return SHD_ERR_ARG;
+  return (m->engine == 1 && m->step_plan.M > 0) ? 1 : 0;
 }
 
 extern "C" int shd_model_linear_times(shd_model* m, float* ms_out6, double* bytes_out6) {
   if (!m || !ms_out6 || !bytes_out6) return SHD_ERR_ARG;
   shd_ctx* ctx = m->ctx;
-  SHD_REQUIRE(ctx, m->prof_count > 0, "shd_model_linear_times: no profiled decode step yet");
   SHD_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
   SHD_CHECK_CUDA(ctx, cudaStreamSynchronize(m->stream));
+  if (m->step_usable(m->graph_rows)) return shd::step_prof_read(ctx, m->step_plan, ms_out6, bytes_out6);
+  SHD_REQUIRE(ctx, m->prof_count > 0, "shd_model_linear_times: no profiled decode step yet");
   for (int k = 0; k < 6; ++k) {
     ms_out6[k] = 0.f;
     bytes_out6[k] = 0.0;

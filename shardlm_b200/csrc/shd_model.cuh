@@ -4,6 +4,7 @@
 #include <vector>
 
 #include "shd_gemv.cuh"
+#include "shd_step.cuh"
 
 struct LayerW {
   shd_weight* qkv = nullptr;     // fused q|k|v, SHD_ROWS_QKV
@@ -60,6 +61,17 @@ struct shd_model {
   std::vector<double> prof_bytes;
   size_t prof_next = 0, prof_count = 0;
   int prof_mark(int kind, const shd_weight* w, bool begin);
+  // persistent decode step (one kernel per token; single-GPU models)
+  int engine = 0;                           // 0: one kernel per operation, 1: persistent step kernel
+  shd::StepPlan step_plan;                  // plan for step_plan.M rows (0: none)
+  std::vector<shd::StepJob>* rec = nullptr;  // when set, the enqueue functions record jobs
+  bool step_usable(int M) const { return engine == 1 && ctx->tp_world <= 1 && step_plan.M == M; }
+  int build_step(int M);
+  // launch (or record) one operation of the layer loop
+  int op_gemv(const shd_weight* w, int M, int epi, const shd::GemvArgs& g, bool norm, int kind);
+  int op_attn(const shd::AttnArgs& at, int M);
+  int op_norm(const shd::NormArgs& na, int M);
+  int op_embed(const shd::EmbedArgs& ea, int M);
 
   ~shd_model();
   int use_stream();

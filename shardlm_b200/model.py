@@ -177,6 +177,16 @@ class SecureModel:
     def reset(self) -> None:
         check(lib().shd_model_reset(self.handle), self.ctx.ptr)
 
+    def set_engine(self, engine: int) -> None:
+        """Decode engine: 0 = one kernel per operation (default), 1 = one persistent kernel per step
+        (single GPU)."""
+        check(lib().shd_model_set_engine(self.handle, engine), self.ctx.ptr)
+
+    @property
+    def engine(self) -> int:
+        """1 when the last decode ran the persistent step kernel."""
+        return int(lib().shd_model_engine(self.handle))
+
     def prefill(self, tokens, slot: int = 0) -> int:
         t = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
         out = C.c_int32()

@@ -43,13 +43,17 @@ def _check_token(gpu_tok, lc, ls, orc):
     return True
 
 
-@pytest.mark.parametrize("shape_name,n_layers,prompt,steps", [("tiny", 2, 11, 12), ("qwen2.5-1.5b", 2, 9, 6)])
-def test_prefill_decode_tokens_match_oracle(ctx, orc, shape_name, n_layers, prompt, steps):
+@pytest.mark.parametrize("engine", [1, 0])
+@pytest.mark.parametrize("shape_name,n_layers,prompt,steps,max_seq",
+                         [("tiny", 2, 11, 12, 64), ("qwen2.5-1.5b", 2, 9, 6, 64), ("tiny", 1, 2450, 3, 2460)])
+def test_prefill_decode_tokens_match_oracle(ctx, orc, shape_name, n_layers, prompt, steps, max_seq, engine):
+    """engine 1: the persistent step kernel; engine 0: one kernel per operation. The long prompt
+    gives every attention split of the step kernel several 32-position tiles."""
     from shardlm_b200.model import SHAPES, SecureModel
 
     shape = SHAPES[shape_name].replace(n_layers=n_layers)
-    max_seq = 64
     m = SecureModel(ctx, shape, max_seq=max_seq, share_seed=123)
+    m.set_engine(engine)
     host = m.load_random_weights(seed=5, host_copy=True)
     om = _oracle_for(orc, shape, host, max_seq)
     rng = np.random.default_rng(0)
@@ -67,6 +71,7 @@ def test_prefill_decode_tokens_match_oracle(ctx, orc, shape_name, n_layers, prom
         inp = int(gpu[i])  # teacher-force the GPU's choice so one near-tie cannot cascade
     assert exact >= steps - 1
     assert m.seq_len() == prompt + steps
+    assert m.engine == engine
 
 
 def test_forward_host_logits_match_oracle(ctx, orc):
@@ -118,6 +123,50 @@ def test_mpc_masks_reshare(ctx, orc):
         assert err < LOGIT_RTOL, err
         # with masks, the server logit share is no longer zero
         assert np.max(np.abs(ls)) > 0
+
+
+@pytest.mark.parametrize("variant", ["approx", "mpc"])
+def test_batched_decode_engines_agree_with_oracle(ctx, orc, variant):
+    """Three slots decoded together (M = 3 rows per step) by both engines, each checked against the
+    oracle slot by slot (teacher-forced on the GPU's tokens)."""
+    from shardlm_b200._lib import NL_APPROX, NL_GPU, NL_MPC
+    from shardlm_b200.model import TINY, SecureModel
+    from shardlm_b200.sharing import beaver_triples_f32
+
+    shape = TINY.replace(n_layers=2)
+    nl = NL_MPC if variant == "mpc" else NL_APPROX
+    nl_pre = NL_MPC if variant == "mpc" else NL_GPU
+    prompts = [np.array(p, np.int32) for p in ([5, 17, 300], [9, 2, 44, 11, 7], [999])]
+    steps = 5
+    results = {}
+    for engine in (1, 0):
+        m = SecureModel(ctx, shape, max_seq=32, max_batch=3, share_seed=77, variant_decode=nl,
+                        variant_prefill=nl_pre, variant_attn=nl)
+        m.set_engine(engine)
+        host = m.load_random_weights(seed=12, host_copy=True)
+        masks = None
+        if variant == "mpc":
+            P = 10 * shape.hidden + 20 + 5 * 32
+            a = torch.stack([beaver_triples_f32(ctx, P, seed=8, offset=l * P).a for l in range(shape.n_layers)])
+            m.set_masks(a)
+            masks = a.cpu().numpy()
+        first = [m.prefill(p, slot=b) for b, p in enumerate(prompts)]
+        toks = m.decode(steps, n_active=3)
+        assert m.engine == engine
+        results[engine] = toks
+        om = [_oracle_for(orc, shape, host, 32) for _ in prompts]
+        for b, p in enumerate(prompts):
+            for i, t in enumerate(p):
+                hc, hs = orc.embed_shares(host["embed"], shape.hidden, int(t), 77, (b << 32) + i)
+                om[b].forward(hc, hs, variant=nl_pre, attn_variant=nl, masks=masks)
+            inp = first[b]
+            for i in range(steps):
+                hc, hs = orc.embed_shares(host["embed"], shape.hidden, int(inp), 77, (b << 32) + len(p) + i)
+                _, _, lc, ls = om[b].forward(hc, hs, variant=nl, attn_variant=nl, masks=masks)
+                _check_token(int(toks[i, b]), lc, ls, orc)
+                inp = int(toks[i, b])
+    # both engines compute the same shares up to float reassociation: the tokens agree
+    assert np.mean(results[0] == results[1]) >= 0.9
 
 
 def test_model_rejects_bad_requests(ctx):
