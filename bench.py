@@ -23,6 +23,10 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "secret-shared decode tok/s (Qwen2.5-7B shape)"
+# DRAM bytes per algorithmic (weight) byte of the dual-share GEMV launches of a 7B decode step, from
+# ncu captures of each projection (q/k/v 1.002, o 1.003, gate/up 1.014, down 1.026; lm_head taken as
+# 1.0), weighted by their bytes per step.
+TRAFFIC_PER_ALGORITHMIC_BYTE = 1.0151
 
 
 def parse():
@@ -319,7 +323,11 @@ def run_ours(args, shape):
             "roofline": {"bound": "hbm", "kernel": "gemv_f32_kernel (dual-share linear, all launches of one step)",
                          "achieved": round(achieved, 1) if achieved else None, "peak": peak,
                          "peak_source": src, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4) if achieved else None, "traffic": None,
+                         "frac": round(achieved / peak, 4) if achieved else None,
+                         "traffic": round(TRAFFIC_PER_ALGORITHMIC_BYTE * lin_bytes / n_lin),
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch of "
+                                           "each 7B projection (profiles/gemv_dual_share_7b.md), weighted "
+                                           "over one step: 1.0151 x the algorithmic bytes",
                          "algorithmic_bytes_per_launch": round(lin_bytes / n_lin),
                          "avg_launch_us": round(lin_ms * 1e3 / n_lin, 2),
                          "per_kind_GBps": {k: round(by5[i] / (ms5[i] * 1e-3) / 1e9, 1) if ms5[i] > 0 else None
