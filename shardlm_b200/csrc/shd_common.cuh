@@ -44,6 +44,9 @@ struct shd_ctx {
   // split partials of the decode attention kernel
   float* d_attn_part = nullptr;
   size_t attn_part_floats = 0;
+  // bf16 activation planes of the tensor-core linear
+  void* d_tc_planes = nullptr;
+  size_t tc_planes_elems = 0;
   // NCCL (tensor parallelism), loaded at run time
   void* nccl_comm = nullptr;
   int tp_rank = 0, tp_world = 1;

@@ -4,6 +4,7 @@
 #include <vector>
 
 #include "shd_gemv.cuh"
+#include "shd_tc.cuh"
 
 using namespace shd;
 
@@ -66,6 +67,7 @@ extern "C" int shd_destroy(shd_ctx* ctx) {
   cudaFree(ctx->d_rope_sin);
   cudaFree(ctx->d_xpad);
   cudaFree(ctx->d_attn_part);
+  cudaFree(ctx->d_tc_planes);
   delete ctx;
   return SHD_OK;
 }
@@ -330,6 +332,7 @@ extern "C" int shd_weight_destroy(shd_weight* w) {
   cudaFree(w->d_tiles);
   cudaFree(w->d_bias);
   cudaFree(w->d_bias_i32);
+  shd::free_weight_map(w);
   delete w;
   return SHD_OK;
 }

@@ -21,6 +21,7 @@
 
 #include "shd_gemv.cuh"
 #include "shd_gemv_dev.cuh"
+#include "shd_tc.cuh"
 
 namespace shd {
 
@@ -30,6 +31,7 @@ constexpr int kSmemLimit = 232448;  // dynamic shared memory per CTA on sm_100
 constexpr int kMaxStages = 6;
 constexpr int kSmemPerCta2 = 115712;  // dynamic shared memory per CTA at two CTAs per SM
 constexpr int kTailBytes = 4608;    // tile result, barriers, flags, reduction scratch
+constexpr int kGemvMaxRowsPerLaunch = 8;  // more rows go to the tensor-core linear
 
 template <int M, int CHUNK, typename XT>
 __device__ void gemv_producer(const PipeSmem& sm, const uint8_t* W, const XT* Xc, const XT* Xs,
@@ -586,6 +588,21 @@ extern "C" int shd_linear_dual_f32(shd_ctx* ctx, const shd_weight* w, const floa
     if (rc) return rc;
     xc = reinterpret_cast<const float*>(pc);
     xs = reinterpret_cast<const float*>(ps);
+  }
+  if (M > kGemvMaxRowsPerLaunch) {
+    // many rows: the tensor-core path (one pass over the weights for all rows)
+    GemvArgs a{};
+    a.Xc = xc;
+    a.Xs = xs;
+    a.ldx = ldx;
+    a.bias = bias ? bias : w->d_bias;
+    a.Rc = residual_c;
+    a.Rs = residual_s;
+    a.ldr = w->N;
+    a.Yc = yc;
+    a.Ys = ys;
+    a.ldy = w->N;
+    return launch_linear_tc(ctx, w, M, EPI_STORE, a);
   }
   for (int m0 = 0; m0 < M;) {
     const int mm = next_m(M - m0);

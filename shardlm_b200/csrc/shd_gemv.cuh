@@ -35,6 +35,7 @@ struct shd_weight {
   float* d_bias = nullptr;  // f32 bias in tile row order (nT*32), nullable
   int32_t* d_bias_i32 = nullptr;
   int64_t bytes = 0;
+  void* tmap = nullptr;     // host copy of the TMA tensor map of the blocks (tensor-core path)
 };
 
 namespace shd {

@@ -1,0 +1,557 @@
+// Tensor-core dual-share linear for many rows (prefill chunks, batched decode): tcgen05 on sm_100a.
+//
+// The shares are f32 and the weights exact bf16 (the reference's f32 weights are bf16 upcasts,
+// crates/v2/server/src/secure_weights.rs:432-440). Every f32 share value splits exactly into three
+// bf16 terms, x = x0 + x1 + x2 (x0 = bf16(x), x1 = bf16(x - x0), x2 = x - x0 - x1: 8 + 8 + 8
+// significand bits, the exponent range of bf16 is that of f32), and a bf16 x bf16 product is exact in
+// f32. So Y = X W^T is computed as sum_i X_i W^T on the bf16 tensor cores with f32 accumulation in
+// tensor memory: the only rounding is that of the f32 accumulation, as in an f32 GEMM.
+//
+// Kernel (one CTA per SM, persistent over output tiles of 128 weight rows x NT token rows):
+//  * warp 4 (one lane) loads per 64-wide K block the weight tile with one 4-D TMA copy straight out
+//    of the 16 KB tiled weight blocks (128 rows = 4 consecutive 32-row tiles, 64 of the 256 columns
+//    of one chunk, 128-byte swizzle) and the six activation planes (client/server x three bf16
+//    terms) with one 3-D TMA copy, into an S-stage mbarrier ring;
+//  * warp 5 allocates tensor memory (two accumulator buffers, each [client | server] x NT f32
+//    columns) and one lane issues tcgen05.mma (M = 128, N = NT, K = 16, bf16 x bf16 -> f32): per
+//    16-wide K step, three MMAs per share accumulate the three terms; tcgen05.commit frees the ring
+//    stage and, after the last K block, hands the accumulator to the epilogue;
+//  * warps 0-3 (tensor memory lanes 0-127 = the tile's 128 weight rows) read the accumulators with
+//    tcgen05.ld and apply the epilogue of the layer (store + bias + residual, q/k/v with RoPE and the
+//    KV-cache write, gate/up with SwiGLU and reshare), one thread per weight row.
+//
+// The weight blocks keep the GEMV layout, whose 256 columns of a chunk are stored permuted (lane l
+// of a row holds columns 4l..4l+3 and 128+4l..128+4l+3); the split kernel writes the activation
+// planes in the same permuted column order, so the MMA's K sum pairs the right terms.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <mutex>
+
+#include "shd_gemv_dev.cuh"
+#include "shd_tc.cuh"
+
+namespace shd {
+namespace {
+
+constexpr int kTcBM = 128;          // weight rows per tile
+constexpr int kTcBK = 64;           // K per ring stage (one 128-byte swizzle row of bf16)
+constexpr int kTcThreads = 192;     // warps 0-3 epilogue, 4 TMA, 5 MMA
+constexpr int kTcSmemLimit = 232448 - 1024;
+constexpr int kTcABytes = kTcBM * kTcBK * 2;  // 16 KB
+
+// ---------------------------------------------------------------------------------------------
+// PTX wrappers
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                            uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2], %7;" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                            uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16 (bf16 inputs, f32 accumulate).
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on `bar` once all tcgen05 operations issued so far by this thread have completed.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// 32 lanes x 8 consecutive f32 columns.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, 8-row atoms 1024 bytes apart.
+__device__ __forceinline__ uint64_t smem_desc_sw128(const void* p) {
+  const uint64_t addr = smem_u32(p);
+  return ((addr & 0x3FFFFull) >> 4) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// Instruction descriptor: D f32, A and B bf16, both K-major, M = 128, N = nt.
+__host__ __device__ constexpr uint32_t idesc_bf16_f32(int nt) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(nt >> 3) << 17) | ((uint32_t)(kTcBM >> 4) << 24);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Kernel
+// ---------------------------------------------------------------------------------------------
+struct TcArgs {
+  GemvArgs g;    // epilogue parameters (as for the GEMV epilogues) and N, K, nT, nKC, err
+  int epi;
+  int M;         // token rows
+  int n_tok;     // token tiles (ceil(M / NT))
+  int n_row;     // weight row tiles of 128 (ceil(nT / 4))
+  int n_kb;      // K blocks of 64
+  int nstages;
+};
+
+template <int NT>
+struct TcSmem {
+  static constexpr int kBBytes = 6 * NT * kTcBK * 2;
+  static constexpr int kStage = kTcABytes + kBBytes;
+};
+
+__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag) {
+  if (mbar_wait_bounded(bar, parity)) return true;
+  atomicOr(err, SHD_DEVERR_TIMEOUT_FULL);
+  *abort_flag = 1;
+  return false;
+}
+
+// Epilogue for one accumulator buffer: this thread owns weight row `r` of the tile (tile-order row
+// index n = row0 + r) and the tile's token columns.
+template <int NT>
+__device__ void tc_epilogue(const TcArgs& ta, uint32_t tacc, int row0, int tok0, int warp, int lane) {
+  const GemvArgs& a = ta.g;
+  const int r = warp * 32 + lane;
+  const int n = row0 + r;  // row in tile order
+  const uint32_t tl = tacc + ((uint32_t)(warp * 32) << 16);
+  const int ntok = min(NT, ta.M - tok0);
+  for (int c0 = 0; c0 < NT; c0 += 8) {
+    float vc[8], vs[8];
+    tmem_ld8(tl + c0, vc);
+    tmem_ld8(tl + NT + c0, vs);
+    tmem_wait_ld();
+    if (c0 >= ntok) continue;  // padding columns (the loads above are warp-collective)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int m = tok0 + c0 + j;
+      const bool live = (c0 + j < ntok);
+      float yc = vc[j], ys = vs[j];
+      if (ta.epi == EPI_STORE) {
+        if (live && n < a.N) {
+          if (a.bias) ys = __fadd_rn(ys, a.bias[n]);
+          if (a.Rc) {
+            yc = __fadd_rn(yc, __ldcg(a.Rc + (size_t)m * a.ldr + n));
+            ys = __fadd_rn(ys, __ldcg(a.Rs + (size_t)m * a.ldr + n));
+          }
+          a.Yc[(size_t)m * a.ldy + n] = yc;
+          a.Ys[(size_t)m * a.ldy + n] = ys;
+        }
+      } else if (ta.epi == EPI_QKV) {
+        // rows 2p, 2p+1 of the tile order are a RoPE pair: exchange with the neighbour lane
+        if (a.bias && n < a.N) ys = __fadd_rn(ys, a.bias[n]);
+        const float oc = __shfl_xor_sync(0xffffffffu, yc, 1);
+        const float os = __shfl_xor_sync(0xffffffffu, ys, 1);
+        if (!live || n >= a.N) continue;
+        const int np = n & ~1;  // first row of the pair
+        const bool second = (n & 1) != 0;
+        const float x0c = second ? oc : yc, x1c = second ? yc : oc;
+        const float x0s = second ? os : ys, x1s = second ? ys : os;
+        const int hd = a.head_dim, half = hd >> 1;
+        const int head = np / hd;
+        const int p = (np % hd) >> 1;
+        const int n0 = head * hd + p, n1 = n0 + half;
+        const int pos = a.pos ? a.pos[m] : 0;
+        float oc_, os_;
+        if (n0 < a.q_dim + a.kv_dim) {
+          if (pos < 0 || pos >= a.rope_max_seq) {
+            atomicOr(a.err, SHD_DEVERR_ARG);
+            continue;
+          }
+          // RopeFrequencies::apply_to_share (secure_attention.rs:84-121), no fused multiply-add
+          const float cs = a.rope_cos[(size_t)pos * half + p];
+          const float sn = a.rope_sin[(size_t)pos * half + p];
+          if (!second) {
+            oc_ = __fsub_rn(__fmul_rn(x0c, cs), __fmul_rn(x1c, sn));
+            os_ = __fsub_rn(__fmul_rn(x0s, cs), __fmul_rn(x1s, sn));
+          } else {
+            oc_ = __fadd_rn(__fmul_rn(x0c, sn), __fmul_rn(x1c, cs));
+            os_ = __fadd_rn(__fmul_rn(x0s, sn), __fmul_rn(x1s, cs));
+          }
+        } else {
+          oc_ = second ? x1c : x0c;
+          os_ = second ? x1s : x0s;
+        }
+        const int nn = second ? n1 : n0;
+        if (a.Yc) {
+          a.Yc[(size_t)m * a.ldy + nn] = oc_;
+          a.Ys[(size_t)m * a.ldy + nn] = os_;
+        }
+        const float v = __fadd_rn(oc_, os_);
+        if (n0 < a.q_dim) {
+          if (a.Q) a.Q[(size_t)m * a.ldq + nn] = v;
+        } else {
+          const bool isk = n0 < a.q_dim + a.kv_dim;
+          float* cache = isk ? a.Kcache : a.Vcache;
+          const int off = isk ? (nn - a.q_dim) : (nn - a.q_dim - a.kv_dim);
+          if (cache) {
+            const int sq = a.seq ? a.seq[m] : 0;
+            cache[(size_t)sq * a.kv_seq_stride + (size_t)pos * a.kv_dim + off] = v;
+          }
+        }
+      } else {  // EPI_GATEUP: lanes 0-15 gate rows, 16-31 the matching up rows of the 32-row tile
+        const float uc = __shfl_xor_sync(0xffffffffu, yc, 16);
+        const float us = __shfl_xor_sync(0xffffffffu, ys, 16);
+        if (!live || lane >= 16) continue;
+        const int I = a.N >> 1;
+        const int i = (n >> 5) * 16 + lane;
+        if (i >= I) continue;
+        const float gv = __fadd_rn(yc, ys);
+        const float uv = __fadd_rn(uc, us);
+        const float y = swiglu_variant(gv, uv, a.variant);
+        const float mk = a.mask ? a.mask[(size_t)m * a.ldmask + i] : 0.0f;
+        a.Yc[(size_t)m * a.ldy + i] = __fsub_rn(y, mk);
+        a.Ys[(size_t)m * a.ldy + i] = mk;
+      }
+    }
+  }
+}
+
+template <int NT>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tc_linear_kernel(const __grid_constant__ TcArgs ta, const __grid_constant__ CUtensorMap map_w,
+                     const __grid_constant__ CUtensorMap map_x) {
+  using L = TcSmem<NT>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte alignment for the swizzled operand tiles
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int S = ta.nstages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * L::kStage);
+  uint64_t* empty = full + S;
+  uint64_t* acc_full = empty + S;   // [2] MMA -> epilogue
+  uint64_t* acc_empty = acc_full + 2;  // [2] epilogue -> MMA
+  uint64_t* done = acc_empty + 2;
+  uint32_t* tmem_base = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr uint32_t kCols = (4 * NT < 32) ? 32 : (4 * NT);  // two buffers of [client | server] x NT
+  const int tiles = ta.n_row * ta.n_tok;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 5) tmem_alloc(tmem_base, kCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_base;
+  pdl_wait();  // activation planes and epilogue inputs come from earlier kernels
+
+  if (warp == 4) {
+    if (lane == 0) {
+      const uint64_t pol_w = l2_policy_evict_first();
+      const uint64_t pol_x = l2_policy_evict_last();
+      int s = 0;
+      uint32_t ph = 0;
+      long long n = 0;
+      for (int t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x) {
+        const int rt = t / ta.n_tok, tt = t % ta.n_tok;
+        for (int kb = 0; kb < ta.n_kb; ++kb, ++n) {
+          if (n >= S && !tc_wait(&empty[s], ph ^ 1u, ta.g.err, abort_flag)) break;
+          uint8_t* st = smem + (size_t)s * L::kStage;
+          mbar_arrive_expect_tx(&full[s], (uint32_t)L::kStage);
+          // weights: columns (kb % 4) * 64 of chunk kb / 4, rows of 32-row tiles 4 rt .. 4 rt + 3
+          tma_load_4d(st, &map_w, (kb & 3) * kTcBK, 0, kb >> 2, rt * 4, &full[s], pol_w);
+          // activation planes: K block kb, token rows tt * NT .., all six planes
+          tma_load_3d(st + kTcABytes, &map_x, kb * kTcBK, tt * NT, 0, &full[s], pol_x);
+          if (++s == S) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(NT);
+      int s = 0;
+      uint32_t ph = 0;
+      int it = 0;
+      for (int t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x, ++it) {
+        const int buf = it & 1;
+        const uint32_t use = (uint32_t)(it >> 1);  // uses of this buffer so far
+        if (use > 0 && !tc_wait(&acc_empty[buf], (use - 1) & 1u, ta.g.err, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t dacc = tbase + (uint32_t)(buf * 2 * NT);
+        bool ok = true;
+        for (int kb = 0; kb < ta.n_kb; ++kb) {
+          if (!tc_wait(&full[s], ph, ta.g.err, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          uint8_t* st = smem + (size_t)s * L::kStage;
+          const uint64_t ad = smem_desc_sw128(st);
+#pragma unroll
+          for (int k = 0; k < kTcBK / 16; ++k) {
+#pragma unroll
+            for (int sh = 0; sh < 2; ++sh)
+#pragma unroll
+              for (int q = 0; q < 3; ++q) {
+                const uint64_t bd = smem_desc_sw128(st + kTcABytes + (size_t)(sh * 3 + q) * NT * kTcBK * 2);
+                tc_mma(dacc + (uint32_t)(sh * NT), ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc,
+                       (kb > 0 || k > 0 || q > 0) ? 1u : 0u);
+              }
+          }
+          tc_commit(&empty[s]);  // the stage is free once these MMAs have read it
+          if (++s == S) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&acc_full[buf]);
+      }
+      // every MMA issued has completed before the accumulators are released
+      tc_commit(done);
+      if (!mbar_wait_bounded(done, 0)) atomicOr(ta.g.err, SHD_DEVERR_TIMEOUT_DRAIN);
+    }
+  } else {
+    // epilogue warps 0-3: tensor memory lanes 32 w .. 32 w + 31
+    int it = 0;
+    for (int t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x, ++it) {
+      const int buf = it & 1;
+      const uint32_t use = (uint32_t)(it >> 1);
+      if (!warp_wait(&acc_full[buf], use & 1u)) {
+        if (lane == 0) atomicOr(ta.g.err, SHD_DEVERR_TIMEOUT_FULL);
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int rt = t / ta.n_tok, tt = t % ta.n_tok;
+      tc_epilogue<NT>(ta, tbase + (uint32_t)(buf * 2 * NT), rt * kTcBM, tt * NT, warp, lane);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
+  }
+  // the producer's copies in flight must land before the CTA leaves
+  if (warp == 4 && lane == 0 && *abort_flag) {
+    for (int s = 0; s < S; ++s) mbar_wait_bounded(&full[s], 0);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 5) tmem_dealloc(tbase, kCols);
+}
+
+// Split f32 shares into the six bf16 planes [share * 3 + term][Mp][KP], columns permuted as in the
+// weight blocks (physical j of chunk c <- logical column c*256 + 4 (j/8) + (j%8 < 4 ? j%8 : 124 + j%8)),
+// zero beyond K and beyond M.
+__global__ void split_planes_kernel(const float* __restrict__ xc, const float* __restrict__ xs, int ldx, int M,
+                                    int K, int Mp, int KP, uint16_t* __restrict__ out) {
+  const size_t plane = (size_t)Mp * KP;
+  const long long total = (long long)Mp * KP;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int m = (int)(idx / KP), j = (int)(idx % KP);
+    const int c = j >> 8, jj = j & 255;
+    const int l = jj >> 3, i = jj & 7;
+    const int col = c * 256 + (i < 4 ? 4 * l + i : 128 + 4 * l + (i - 4));
+    float v[2] = {0.f, 0.f};
+    if (m < M && col < K) {
+      v[0] = xc[(size_t)m * ldx + col];
+      v[1] = xs[(size_t)m * ldx + col];
+    }
+#pragma unroll
+    for (int sh = 0; sh < 2; ++sh) {
+      const __nv_bfloat16 b0 = __float2bfloat16_rn(v[sh]);
+      const float r1 = __fsub_rn(v[sh], __bfloat162float(b0));
+      const __nv_bfloat16 b1 = __float2bfloat16_rn(r1);
+      const float r2 = __fsub_rn(r1, __bfloat162float(b1));
+      const __nv_bfloat16 b2 = __float2bfloat16_rn(r2);
+      out[(size_t)(sh * 3 + 0) * plane + idx] = __bfloat16_as_ushort(b0);
+      out[(size_t)(sh * 3 + 1) * plane + idx] = __bfloat16_as_ushort(b1);
+      out[(size_t)(sh * 3 + 2) * plane + idx] = __bfloat16_as_ushort(b2);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// Weight tensor map: dims (innermost first) 256 columns, 32 rows, nKC chunks, nT tiles of the
+// 16 KB-block layout; box 64 x 32 x 1 x 4 = a 128-row x 64-column tile.
+int weight_map(shd_ctx* ctx, const shd_weight* w, CUtensorMap* map) {
+  auto enc = encode_fn();
+  if (!enc) return shd_fail(ctx, SHD_ERR_UNSUPPORTED, "tensor-core linear: cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[4] = {256, 32, (cuuint64_t)w->nKC, (cuuint64_t)w->nT};
+  const cuuint64_t strides[3] = {512, (cuuint64_t)kBlockBytes, (cuuint64_t)w->nKC * kBlockBytes};
+  const cuuint32_t box[4] = {kTcBK, 32, 1, 4};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, w->d_tiles, dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return shd_fail(ctx, SHD_ERR_CUDA, "tensor-core linear: weight tensor map");
+  return SHD_OK;
+}
+
+// Activation-plane tensor map: dims KP, Mp, 6 planes; box 64 x NT x 6.
+int planes_map(shd_ctx* ctx, const uint16_t* planes, int Mp, int KP, int nt, CUtensorMap* map) {
+  auto enc = encode_fn();
+  if (!enc) return shd_fail(ctx, SHD_ERR_UNSUPPORTED, "tensor-core linear: cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[3] = {(cuuint64_t)KP, (cuuint64_t)Mp, 6};
+  const cuuint64_t strides[2] = {(cuuint64_t)KP * 2, (cuuint64_t)Mp * KP * 2};
+  const cuuint32_t box[3] = {kTcBK, (cuuint32_t)nt, 6};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<uint16_t*>(planes), dims, strides,
+                         box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return shd_fail(ctx, SHD_ERR_CUDA, "tensor-core linear: activation tensor map");
+  return SHD_OK;
+}
+
+int ensure_planes(shd_ctx* ctx, size_t elems) {
+  if (ctx->tc_planes_elems >= elems) return SHD_OK;
+  if (ctx->d_tc_planes) cudaFree(ctx->d_tc_planes);
+  ctx->d_tc_planes = nullptr;
+  ctx->tc_planes_elems = 0;
+  SHD_CHECK_CUDA(ctx, cudaMalloc(&ctx->d_tc_planes, elems * 2));
+  ctx->tc_planes_elems = elems;
+  return SHD_OK;
+}
+
+template <int NT>
+int launch_tc_t(shd_ctx* ctx, const TcArgs& ta, const CUtensorMap& mw, const CUtensorMap& mx) {
+  static unsigned attr_devices = 0;
+  const int S = std::min(8, (kTcSmemLimit - 1024 - 256) / TcSmem<NT>::kStage);
+  if (S < 2) return shd_fail(ctx, SHD_ERR_UNSUPPORTED, "tensor-core linear: token tile too wide");
+  const size_t smem = 1024 + (size_t)S * TcSmem<NT>::kStage + 256;
+  if (!(attr_devices & (1u << (ctx->device & 31)))) {
+    SHD_CHECK_CUDA(ctx, cudaFuncSetAttribute(tc_linear_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kTcSmemLimit));
+    attr_devices |= 1u << (ctx->device & 31);
+  }
+  TcArgs a = ta;
+  a.nstages = S;
+  const int tiles = a.n_row * a.n_tok;
+  const int grid = std::min(tiles, ctx->num_sms);
+  SHD_CHECK_CUDA(ctx, launch_pdl(tc_linear_kernel<NT>, dim3(grid), dim3(kTcThreads), smem, ctx->stream, a, mw, mx));
+  ctx->launches++;
+  return SHD_OK;
+}
+
+}  // namespace
+
+int tc_token_tile(int M) {
+  if (M <= 8) return 8;
+  if (M <= 16) return 16;
+  if (M <= 32) return 32;
+  return 64;
+}
+
+int launch_linear_tc(shd_ctx* ctx, const shd_weight* w, int M, int epi, GemvArgs g) {
+  if (w->kind != WK_BF16) return shd_fail(ctx, SHD_ERR_ARG, "tensor-core linear: need a bf16 weight");
+  if (epi == EPI_LOGITS) return shd_fail(ctx, SHD_ERR_UNSUPPORTED, "tensor-core linear: no logits epilogue");
+  if (M <= 0) return SHD_OK;
+  int rc = gemv_prepare(ctx, w, g, false);
+  if (rc) return rc;
+  const int nt = tc_token_tile(M);
+  const int n_tok = (M + nt - 1) / nt;
+  const int Mp = n_tok * nt;
+  const int KP = w->nKC * kChunkBf16;
+  if ((rc = ensure_planes(ctx, (size_t)6 * Mp * KP))) return rc;
+  uint16_t* planes = reinterpret_cast<uint16_t*>(ctx->d_tc_planes);
+  {
+    const long long total = (long long)Mp * KP;
+    const int blocks = (int)std::min<long long>((total + 255) / 256, 4LL * ctx->num_sms);
+    SHD_CHECK_CUDA(ctx, launch_pdl(split_planes_kernel, dim3(blocks), dim3(256), 0, ctx->stream, g.Xc, g.Xs, g.ldx, M,
+                                   w->K, Mp, KP, planes));
+    ctx->launches++;
+  }
+  if (!w->tmap) {
+    auto* m = new (std::align_val_t(64)) CUtensorMap;
+    rc = weight_map(ctx, w, m);
+    if (rc) {
+      ::operator delete(m, std::align_val_t(64));
+      return rc;
+    }
+    const_cast<shd_weight*>(w)->tmap = m;
+  }
+  alignas(64) CUtensorMap mx;
+  if ((rc = planes_map(ctx, planes, Mp, KP, nt, &mx))) return rc;
+  TcArgs ta{};
+  ta.g = g;
+  ta.epi = epi;
+  ta.M = M;
+  ta.n_tok = n_tok;
+  ta.n_row = (w->nT + 3) / 4;
+  ta.n_kb = w->nKC * (kChunkBf16 / kTcBK);
+  const CUtensorMap& mw = *static_cast<const CUtensorMap*>(w->tmap);
+  switch (nt) {
+    case 8: return launch_tc_t<8>(ctx, ta, mw, mx);
+    case 16: return launch_tc_t<16>(ctx, ta, mw, mx);
+    case 32: return launch_tc_t<32>(ctx, ta, mw, mx);
+    default: return launch_tc_t<64>(ctx, ta, mw, mx);
+  }
+}
+
+void free_weight_map(shd_weight* w) {
+  if (w && w->tmap) {
+    ::operator delete(static_cast<CUtensorMap*>(w->tmap), std::align_val_t(64));
+    w->tmap = nullptr;
+  }
+}
+
+}  // namespace shd

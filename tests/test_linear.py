@@ -51,6 +51,12 @@ def _check(orc, w_u16, xc, xs, b, yc, ys, residual=None):
     (520, 4100, 5, False),     # M=5 -> launches of 4 + 1
     (3584, 3584, 8, True),     # M=8
     (4, 2, 1, True),           # tiny
+    # M > 8: tcgen05 tensor-core path (three bf16 terms per f32 share, f32 accumulation in TMEM)
+    (3584, 4608, 64, True),    # 7B q/k/v shape, one 64-row token tile
+    (1000, 77, 9, True),       # ragged N and K, 16-row token tile
+    (18944, 3584, 33, False),  # 7B down shape
+    (1536, 1536, 130, True),   # three 64-row token tiles, ragged last
+    (4, 2, 17, True),          # tiny
 ])
 def test_linear_dual_f32_matches_oracle(ctx, orc, K, N, M, bias):
     from shardlm_b200.runtime import Weight
@@ -79,6 +85,25 @@ def test_linear_residual_epilogue(ctx, orc):
                                            residual=(ctx.to_device(rc), ctx.to_device(rs)))
     ctx.sync()
     _check(orc, w_u16, xc, xs, None, yc.cpu().numpy(), ys.cpu().numpy(), residual=(rc, rs))
+
+
+def test_linear_tensor_core_residual_and_determinism(ctx, orc):
+    """M > 8 rows through the tensor cores: residual epilogue, and repeated calls bit-identical."""
+    from shardlm_b200.runtime import Weight
+    from shardlm_b200.sharing import GpuSecureLinear
+
+    rng = np.random.default_rng(6)
+    w_u16, xc, xs, _ = _case(rng, 3584, 3584, 40, False)
+    rc = rng.standard_normal((40, 3584)).astype(np.float32)
+    rs = rng.standard_normal((40, 3584)).astype(np.float32)
+    w = Weight.from_bf16_out_in(ctx, torch.from_numpy(w_u16.view(np.int16)).view(torch.bfloat16).cuda())
+    lin = GpuSecureLinear(ctx, w, None)
+    res = (ctx.to_device(rc), ctx.to_device(rs))
+    outs = [lin.forward_secure_gpu_tensor(ctx.to_device(xc), ctx.to_device(xs), residual=res) for _ in range(3)]
+    ctx.sync()
+    _check(orc, w_u16, xc, xs, None, outs[0][0].cpu().numpy(), outs[0][1].cpu().numpy(), residual=(rc, rs))
+    for o in outs[1:]:
+        assert torch.equal(o[0], outs[0][0]) and torch.equal(o[1], outs[0][1])
 
 
 def test_linear_deterministic_across_calls(ctx):
