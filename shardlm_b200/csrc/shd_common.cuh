@@ -47,6 +47,8 @@ struct shd_ctx {
   // bf16 activation planes of the tensor-core linear
   void* d_tc_planes = nullptr;
   size_t tc_planes_elems = 0;
+  float* d_tc_ws = nullptr;  // split-K partial sums of the tensor-core linear
+  size_t tc_ws_floats = 0;
   // NCCL (tensor parallelism), loaded at run time
   void* nccl_comm = nullptr;
   int tp_rank = 0, tp_world = 1;

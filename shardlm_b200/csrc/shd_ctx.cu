@@ -68,6 +68,7 @@ extern "C" int shd_destroy(shd_ctx* ctx) {
   cudaFree(ctx->d_xpad);
   cudaFree(ctx->d_attn_part);
   cudaFree(ctx->d_tc_planes);
+  cudaFree(ctx->d_tc_ws);
   delete ctx;
   return SHD_OK;
 }

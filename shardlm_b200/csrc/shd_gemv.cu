@@ -31,7 +31,6 @@ constexpr int kSmemLimit = 232448;  // dynamic shared memory per CTA on sm_100
 constexpr int kMaxStages = 6;
 constexpr int kSmemPerCta2 = 115712;  // dynamic shared memory per CTA at two CTAs per SM
 constexpr int kTailBytes = 4608;    // tile result, barriers, flags, reduction scratch
-constexpr int kGemvMaxRowsPerLaunch = 8;  // more rows go to the tensor-core linear
 
 template <int M, int CHUNK, typename XT>
 __device__ void gemv_producer(const PipeSmem& sm, const uint8_t* W, const XT* Xc, const XT* Xs,
@@ -589,7 +588,7 @@ extern "C" int shd_linear_dual_f32(shd_ctx* ctx, const shd_weight* w, const floa
     xc = reinterpret_cast<const float*>(pc);
     xs = reinterpret_cast<const float*>(ps);
   }
-  if (M > kGemvMaxRowsPerLaunch) {
+  if (M >= kTcMinRows) {
     // many rows: the tensor-core path (one pass over the weights for all rows)
     GemvArgs a{};
     a.Xc = xc;

@@ -23,6 +23,7 @@
 
 #include "shd_gemv.cuh"
 #include "shd_model.cuh"
+#include "shd_tc.cuh"
 #include "shd_nonlinear.cuh"
 
 using namespace shd;
@@ -31,7 +32,8 @@ int shd_attn_splits(int num_sms, int n_groups, int M, int max_len);
 
 namespace {
 
-constexpr int kMaxRows = 8;  // rows of one GEMV launch / prefill chunk
+constexpr int kMaxRows = 8;        // decode batch (sequence slots stepped together)
+constexpr int kPrefillRows = 128;  // prompt positions per prefill chunk (tensor-core linears)
 
 // Decode bookkeeping after the logits: tokens = keys, history row, position advance.
 __global__ void finish_step_kernel(const unsigned long long* keys, int* tokens, int* pos, int* hist,
@@ -144,7 +146,7 @@ extern "C" int shd_model_create(shd_ctx* ctx, const shd_model_config* cfg, shd_m
   m->kvd = m->sh.kv_head_count * d;
   m->I = m->sh.inter_count;
   m->V = m->sh.vocab_count;
-  m->R = std::max(c.max_batch, kMaxRows);
+  m->R = std::max(c.max_batch, kPrefillRows);
   m->T = c.max_seq;
   m->layers.resize(c.n_layers);
   m->len.assign(c.max_batch, 0);
@@ -214,7 +216,7 @@ extern "C" int shd_model_create(shd_ctx* ctx, const shd_model_config* cfg, shd_m
   if (e != cudaSuccess) return fail(shd_cuda_fail(ctx, e, "shd_model_create: init"));
   // attention scratch for the largest launch (kMaxRows rows)
   m->nsplit = shd_attn_splits(ctx->num_sms, std::max(m->n_groups, 1), c.max_batch, c.max_seq);
-  m->nsplit_prefill = shd_attn_splits(ctx->num_sms, std::max(m->n_groups, 1), kMaxRows, c.max_seq);
+  m->nsplit_prefill = shd_attn_splits(ctx->num_sms, std::max(m->n_groups, 1), kPrefillRows, c.max_seq);
   const int ns = std::max(m->nsplit, m->nsplit_prefill);
   rc = ensure_attn_scratch(ctx, attn_partial_floats((int)R, std::max(m->n_groups, 1), ns, d));
   if (rc) return fail(rc);
@@ -406,7 +408,9 @@ int shd_model::norm_into(GemvArgs& g, const shd_weight* w, int M, const float* H
                          const float* Dc, const float* Ds, float* Oc, float* Os, const float* gamma,
                          int variant, const float* mask, bool& fused) {
   const int h = cfg.hidden;
-  fused = (size_t)M * 2 * w->nKC * kChunkBf16 * 4 <= 120 * 1024;
+  // fused into the GEMV when its activations fit the CTA; the tensor-core path (M >= kTcMinRows,
+  // per-kernel engine) reads staged activations
+  fused = (size_t)M * 2 * w->nKC * kChunkBf16 * 4 <= 120 * 1024 && (M < kTcMinRows || rec != nullptr);
   if (fused) {
     g.nHc = Hc; g.nHs = Hs; g.nDc = Dc; g.nDs = Ds; g.nHout_c = Oc; g.nHout_s = Os; g.n_ldh = h;
     g.gamma = gamma; g.eps = cfg.rms_eps; g.nvariant = variant; g.nmask = mask; g.n_ldmask = 0;
@@ -421,7 +425,10 @@ int shd_model::norm_into(GemvArgs& g, const shd_weight* w, int M, const float* H
 }
 
 int shd_model::op_gemv(const shd_weight* w, int M, int epi, const GemvArgs& g, bool norm, int kind) {
-  if (!rec) return launch_gemv_f32(ctx, w, M, epi, g, norm);
+  if (!rec) {
+    if (M >= kTcMinRows && epi != EPI_LOGITS && !norm) return launch_linear_tc(ctx, w, M, epi, g);
+    return launch_gemv_f32(ctx, w, M, epi, g, norm);
+  }
   StepJob j{};
   j.type = JOB_GEMV;
   j.epi = epi;
@@ -612,20 +619,20 @@ extern "C" int shd_model_prefill(shd_model* m, int slot, const int32_t* tokens_h
   if (rc) return rc;
   if ((rc = m->enter())) return rc;
   const int h = m->cfg.hidden;
-  std::vector<int> hp(3 * kMaxRows);
+  std::vector<int> hp(3 * kPrefillRows);
   int cur = 0;
-  for (int p0 = 0; p0 < n && rc == SHD_OK; p0 += kMaxRows) {
-    const int M = std::min(kMaxRows, n - p0);
+  for (int p0 = 0; p0 < n && rc == SHD_OK; p0 += kPrefillRows) {
+    const int M = std::min(kPrefillRows, n - p0);
     for (int i = 0; i < M; ++i) {
       hp[i] = tokens_host[p0 + i];
-      hp[kMaxRows + i] = m->len[slot] + p0 + i;
-      hp[2 * kMaxRows + i] = slot;
+      hp[kPrefillRows + i] = m->len[slot] + p0 + i;
+      hp[2 * kPrefillRows + i] = slot;
     }
     // the staging vector is reused: finish the previous chunk's copies first
     if (cudaStreamSynchronize(m->stream) != cudaSuccess) { rc = shd_fail(ctx, SHD_ERR_CUDA, "prefill sync"); break; }
     cudaError_t e = cudaMemcpyAsync(m->p_tokens, hp.data(), M * 4, cudaMemcpyHostToDevice, m->stream);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(m->p_pos, hp.data() + kMaxRows, M * 4, cudaMemcpyHostToDevice, m->stream);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(m->p_seq, hp.data() + 2 * kMaxRows, M * 4, cudaMemcpyHostToDevice, m->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(m->p_pos, hp.data() + kPrefillRows, M * 4, cudaMemcpyHostToDevice, m->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(m->p_seq, hp.data() + 2 * kPrefillRows, M * 4, cudaMemcpyHostToDevice, m->stream);
     if (e != cudaSuccess) { rc = shd_cuda_fail(ctx, e, "prefill staging"); break; }
     EmbedArgs ea{};
     ea.table = m->embed; ea.vocab = m->cfg.vocab; ea.hidden = h; ea.tokens = m->p_tokens;

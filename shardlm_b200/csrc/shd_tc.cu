@@ -128,13 +128,17 @@ struct TcArgs {
   int n_tok;     // token tiles (ceil(M / NT))
   int n_row;     // weight row tiles of 128 (ceil(nT / 4))
   int n_kb;      // K blocks of 64
+  int ksplit;    // K ranges per output tile (> 1: partial sums to `ws`, epilogue in tc_reduce_kernel)
   int nstages;
+  float* ws;     // [ksplit][n_tok * NT][n_row * 128][2] partial sums (ksplit > 1)
 };
 
 template <int NT>
 struct TcSmem {
   static constexpr int kBBytes = 6 * NT * kTcBK * 2;
   static constexpr int kStage = kTcABytes + kBBytes;
+  static constexpr int kN = 3 * NT;      // MMA N per share: the three bf16 terms side by side
+  static constexpr int kBuf = 2 * kN;    // tensor-memory columns per accumulator buffer
 };
 
 __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag) {
@@ -144,101 +148,116 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, int* err
   return false;
 }
 
-// Epilogue for one accumulator buffer: this thread owns weight row `r` of the tile (tile-order row
-// index n = row0 + r) and the tile's token columns.
-template <int NT>
-__device__ void tc_epilogue(const TcArgs& ta, uint32_t tacc, int row0, int tok0, int warp, int lane) {
+// The epilogue of one value: weight row n (tile order; 32 consecutive rows per warp, lane = n % 32),
+// token row m. Every lane of the warp calls it together (RoPE and SwiGLU pair rows across lanes).
+__device__ __forceinline__ void tc_epi_value(const TcArgs& ta, int n, int m, bool live, float yc, float ys,
+                                             int lane) {
   const GemvArgs& a = ta.g;
+  if (ta.epi == EPI_STORE) {
+    if (live && n < a.N) {
+      if (a.bias) ys = __fadd_rn(ys, a.bias[n]);
+      if (a.Rc) {
+        yc = __fadd_rn(yc, __ldcg(a.Rc + (size_t)m * a.ldr + n));
+        ys = __fadd_rn(ys, __ldcg(a.Rs + (size_t)m * a.ldr + n));
+      }
+      a.Yc[(size_t)m * a.ldy + n] = yc;
+      a.Ys[(size_t)m * a.ldy + n] = ys;
+    }
+  } else if (ta.epi == EPI_QKV) {
+    // rows 2p, 2p+1 of the tile order are a RoPE pair: exchange with the neighbour lane
+    if (a.bias && n < a.N) ys = __fadd_rn(ys, a.bias[n]);
+    const float oc = __shfl_xor_sync(0xffffffffu, yc, 1);
+    const float os = __shfl_xor_sync(0xffffffffu, ys, 1);
+    if (!live || n >= a.N) return;
+    const int np = n & ~1;  // first row of the pair
+    const bool second = (n & 1) != 0;
+    const float x0c = second ? oc : yc, x1c = second ? yc : oc;
+    const float x0s = second ? os : ys, x1s = second ? ys : os;
+    const int hd = a.head_dim, half = hd >> 1;
+    const int head = np / hd;
+    const int p = (np % hd) >> 1;
+    const int n0 = head * hd + p, n1 = n0 + half;
+    const int pos = a.pos ? a.pos[m] : 0;
+    float oc_, os_;
+    if (n0 < a.q_dim + a.kv_dim) {
+      if (pos < 0 || pos >= a.rope_max_seq) {
+        atomicOr(a.err, SHD_DEVERR_ARG);
+        return;
+      }
+      // RopeFrequencies::apply_to_share (secure_attention.rs:84-121), no fused multiply-add
+      const float cs = a.rope_cos[(size_t)pos * half + p];
+      const float sn = a.rope_sin[(size_t)pos * half + p];
+      if (!second) {
+        oc_ = __fsub_rn(__fmul_rn(x0c, cs), __fmul_rn(x1c, sn));
+        os_ = __fsub_rn(__fmul_rn(x0s, cs), __fmul_rn(x1s, sn));
+      } else {
+        oc_ = __fadd_rn(__fmul_rn(x0c, sn), __fmul_rn(x1c, cs));
+        os_ = __fadd_rn(__fmul_rn(x0s, sn), __fmul_rn(x1s, cs));
+      }
+    } else {
+      oc_ = second ? x1c : x0c;
+      os_ = second ? x1s : x0s;
+    }
+    const int nn = second ? n1 : n0;
+    if (a.Yc) {
+      a.Yc[(size_t)m * a.ldy + nn] = oc_;
+      a.Ys[(size_t)m * a.ldy + nn] = os_;
+    }
+    const float v = __fadd_rn(oc_, os_);
+    if (n0 < a.q_dim) {
+      if (a.Q) a.Q[(size_t)m * a.ldq + nn] = v;
+    } else {
+      const bool isk = n0 < a.q_dim + a.kv_dim;
+      float* cache = isk ? a.Kcache : a.Vcache;
+      const int off = isk ? (nn - a.q_dim) : (nn - a.q_dim - a.kv_dim);
+      if (cache) {
+        const int sq = a.seq ? a.seq[m] : 0;
+        cache[(size_t)sq * a.kv_seq_stride + (size_t)pos * a.kv_dim + off] = v;
+      }
+    }
+  } else {  // EPI_GATEUP: lanes 0-15 gate rows, 16-31 the matching up rows of the 32-row tile
+    const float uc = __shfl_xor_sync(0xffffffffu, yc, 16);
+    const float us = __shfl_xor_sync(0xffffffffu, ys, 16);
+    if (!live || lane >= 16) return;
+    const int I = a.N >> 1;
+    const int i = (n >> 5) * 16 + lane;
+    if (i >= I) return;
+    const float gv = __fadd_rn(yc, ys);
+    const float uv = __fadd_rn(uc, us);
+    const float y = swiglu_variant(gv, uv, a.variant);
+    const float mk = a.mask ? a.mask[(size_t)m * a.ldmask + i] : 0.0f;
+    a.Yc[(size_t)m * a.ldy + i] = __fsub_rn(y, mk);
+    a.Ys[(size_t)m * a.ldy + i] = mk;
+  }
+}
+
+// Epilogue of one accumulator buffer (columns: share, term, token): this thread owns weight row
+// r = 32 warp + lane of the tile. The three terms of a share are summed in order.
+template <int NT>
+__device__ void tc_epilogue(const TcArgs& ta, uint32_t tacc, int row0, int tok0, int ks, int warp, int lane) {
+  using L = TcSmem<NT>;
   const int r = warp * 32 + lane;
   const int n = row0 + r;  // row in tile order
   const uint32_t tl = tacc + ((uint32_t)(warp * 32) << 16);
   const int ntok = min(NT, ta.M - tok0);
+  const int rows_all = ta.n_row * kTcBM;
   for (int c0 = 0; c0 < NT; c0 += 8) {
-    float vc[8], vs[8];
-    tmem_ld8(tl + c0, vc);
-    tmem_ld8(tl + NT + c0, vs);
+    float t[6][8];
+#pragma unroll
+    for (int q = 0; q < 6; ++q) tmem_ld8(tl + (uint32_t)((q / 3) * L::kN + (q % 3) * NT + c0), t[q]);
     tmem_wait_ld();
-    if (c0 >= ntok) continue;  // padding columns (the loads above are warp-collective)
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int m = tok0 + c0 + j;
       const bool live = (c0 + j < ntok);
-      float yc = vc[j], ys = vs[j];
-      if (ta.epi == EPI_STORE) {
-        if (live && n < a.N) {
-          if (a.bias) ys = __fadd_rn(ys, a.bias[n]);
-          if (a.Rc) {
-            yc = __fadd_rn(yc, __ldcg(a.Rc + (size_t)m * a.ldr + n));
-            ys = __fadd_rn(ys, __ldcg(a.Rs + (size_t)m * a.ldr + n));
-          }
-          a.Yc[(size_t)m * a.ldy + n] = yc;
-          a.Ys[(size_t)m * a.ldy + n] = ys;
-        }
-      } else if (ta.epi == EPI_QKV) {
-        // rows 2p, 2p+1 of the tile order are a RoPE pair: exchange with the neighbour lane
-        if (a.bias && n < a.N) ys = __fadd_rn(ys, a.bias[n]);
-        const float oc = __shfl_xor_sync(0xffffffffu, yc, 1);
-        const float os = __shfl_xor_sync(0xffffffffu, ys, 1);
-        if (!live || n >= a.N) continue;
-        const int np = n & ~1;  // first row of the pair
-        const bool second = (n & 1) != 0;
-        const float x0c = second ? oc : yc, x1c = second ? yc : oc;
-        const float x0s = second ? os : ys, x1s = second ? ys : os;
-        const int hd = a.head_dim, half = hd >> 1;
-        const int head = np / hd;
-        const int p = (np % hd) >> 1;
-        const int n0 = head * hd + p, n1 = n0 + half;
-        const int pos = a.pos ? a.pos[m] : 0;
-        float oc_, os_;
-        if (n0 < a.q_dim + a.kv_dim) {
-          if (pos < 0 || pos >= a.rope_max_seq) {
-            atomicOr(a.err, SHD_DEVERR_ARG);
-            continue;
-          }
-          // RopeFrequencies::apply_to_share (secure_attention.rs:84-121), no fused multiply-add
-          const float cs = a.rope_cos[(size_t)pos * half + p];
-          const float sn = a.rope_sin[(size_t)pos * half + p];
-          if (!second) {
-            oc_ = __fsub_rn(__fmul_rn(x0c, cs), __fmul_rn(x1c, sn));
-            os_ = __fsub_rn(__fmul_rn(x0s, cs), __fmul_rn(x1s, sn));
-          } else {
-            oc_ = __fadd_rn(__fmul_rn(x0c, sn), __fmul_rn(x1c, cs));
-            os_ = __fadd_rn(__fmul_rn(x0s, sn), __fmul_rn(x1s, cs));
-          }
-        } else {
-          oc_ = second ? x1c : x0c;
-          os_ = second ? x1s : x0s;
-        }
-        const int nn = second ? n1 : n0;
-        if (a.Yc) {
-          a.Yc[(size_t)m * a.ldy + nn] = oc_;
-          a.Ys[(size_t)m * a.ldy + nn] = os_;
-        }
-        const float v = __fadd_rn(oc_, os_);
-        if (n0 < a.q_dim) {
-          if (a.Q) a.Q[(size_t)m * a.ldq + nn] = v;
-        } else {
-          const bool isk = n0 < a.q_dim + a.kv_dim;
-          float* cache = isk ? a.Kcache : a.Vcache;
-          const int off = isk ? (nn - a.q_dim) : (nn - a.q_dim - a.kv_dim);
-          if (cache) {
-            const int sq = a.seq ? a.seq[m] : 0;
-            cache[(size_t)sq * a.kv_seq_stride + (size_t)pos * a.kv_dim + off] = v;
-          }
-        }
-      } else {  // EPI_GATEUP: lanes 0-15 gate rows, 16-31 the matching up rows of the 32-row tile
-        const float uc = __shfl_xor_sync(0xffffffffu, yc, 16);
-        const float us = __shfl_xor_sync(0xffffffffu, ys, 16);
-        if (!live || lane >= 16) continue;
-        const int I = a.N >> 1;
-        const int i = (n >> 5) * 16 + lane;
-        if (i >= I) continue;
-        const float gv = __fadd_rn(yc, ys);
-        const float uv = __fadd_rn(uc, us);
-        const float y = swiglu_variant(gv, uv, a.variant);
-        const float mk = a.mask ? a.mask[(size_t)m * a.ldmask + i] : 0.0f;
-        a.Yc[(size_t)m * a.ldy + i] = __fsub_rn(y, mk);
-        a.Ys[(size_t)m * a.ldy + i] = mk;
+      const float yc = __fadd_rn(__fadd_rn(t[0][j], t[1][j]), t[2][j]);
+      const float ys = __fadd_rn(__fadd_rn(t[3][j], t[4][j]), t[5][j]);
+      if (ta.ksplit > 1) {
+        float* w = ta.ws + (((size_t)ks * ta.n_tok * NT + (size_t)(tok0 + c0 + j)) * rows_all + n) * 2;
+        w[0] = yc;
+        w[1] = ys;
+      } else {
+        tc_epi_value(ta, n, m, live, yc, ys, lane);
       }
     }
   }
@@ -255,15 +274,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int S = ta.nstages;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * L::kStage);
   uint64_t* empty = full + S;
-  uint64_t* acc_full = empty + S;   // [2] MMA -> epilogue
+  uint64_t* acc_full = empty + S;      // [2] MMA -> epilogue
   uint64_t* acc_empty = acc_full + 2;  // [2] epilogue -> MMA
   uint64_t* done = acc_empty + 2;
   uint32_t* tmem_base = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr uint32_t kCols = (4 * NT < 32) ? 32 : (4 * NT);  // two buffers of [client | server] x NT
-  const int tiles = ta.n_row * ta.n_tok;
+  constexpr uint32_t kCols = 512;  // two buffers of 2 x 3 NT columns (NT <= 32)
+  static_assert(2 * L::kBuf <= (int)kCols, "accumulators exceed tensor memory");
+  const int tiles = ta.n_row * ta.n_tok * ta.ksplit;
+  const int kb_per = ta.n_kb / ta.ksplit;  // the launcher makes ksplit divide n_kb
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -285,6 +306,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t tbase = *tmem_base;
   pdl_wait();  // activation planes and epilogue inputs come from earlier kernels
 
+  // work item t: weight row tile rt, token tile tt, K range ks (token tile fastest: CTAs that run
+  // together share the weight tile through L2)
   if (warp == 4) {
     if (lane == 0) {
       const uint64_t pol_w = l2_policy_evict_first();
@@ -292,10 +315,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       int s = 0;
       uint32_t ph = 0;
       long long n = 0;
-      for (int t = blockIdx.x; t < tiles && !*abort_flag; t += gridDim.x) {
-        const int rt = t / ta.n_tok, tt = t % ta.n_tok;
-        for (int kb = 0; kb < ta.n_kb; ++kb, ++n) {
-          if (n >= S && !tc_wait(&empty[s], ph ^ 1u, ta.g.err, abort_flag)) break;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok && !*abort_flag; t += gridDim.x) {
+        const int tt = t % ta.n_tok, ks = (t / ta.n_tok) % ta.ksplit, rt = t / (ta.n_tok * ta.ksplit);
+        for (int kb = ks * kb_per; kb < (ks + 1) * kb_per; ++kb, ++n) {
+          if (n >= S && !tc_wait(&empty[s], ph ^ 1u, ta.g.err, abort_flag)) {
+            ok = false;
+            break;
+          }
           uint8_t* st = smem + (size_t)s * L::kStage;
           mbar_arrive_expect_tx(&full[s], (uint32_t)L::kStage);
           // weights: columns (kb % 4) * 64 of chunk kb / 4, rows of 32-row tiles 4 rt .. 4 rt + 3
@@ -311,7 +338,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   } else if (warp == 5) {
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(NT);
+      constexpr uint32_t idesc = idesc_bf16_f32(L::kN);
       int s = 0;
       uint32_t ph = 0;
       int it = 0;
@@ -320,9 +347,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const uint32_t use = (uint32_t)(it >> 1);  // uses of this buffer so far
         if (use > 0 && !tc_wait(&acc_empty[buf], (use - 1) & 1u, ta.g.err, abort_flag)) break;
         tc_fence_after();
-        const uint32_t dacc = tbase + (uint32_t)(buf * 2 * NT);
+        const uint32_t dacc = tbase + (uint32_t)(buf * L::kBuf);
         bool ok = true;
-        for (int kb = 0; kb < ta.n_kb; ++kb) {
+        for (int kb = 0; kb < kb_per; ++kb) {
           if (!tc_wait(&full[s], ph, ta.g.err, abort_flag)) {
             ok = false;
             break;
@@ -333,13 +360,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
           for (int k = 0; k < kTcBK / 16; ++k) {
 #pragma unroll
-            for (int sh = 0; sh < 2; ++sh)
-#pragma unroll
-              for (int q = 0; q < 3; ++q) {
-                const uint64_t bd = smem_desc_sw128(st + kTcABytes + (size_t)(sh * 3 + q) * NT * kTcBK * 2);
-                tc_mma(dacc + (uint32_t)(sh * NT), ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc,
-                       (kb > 0 || k > 0 || q > 0) ? 1u : 0u);
-              }
+            for (int sh = 0; sh < 2; ++sh) {
+              // the share's three term planes are 3 NT consecutive rows: one MMA with N = 3 NT
+              const uint64_t bd = smem_desc_sw128(st + kTcABytes + (size_t)sh * 3 * NT * kTcBK * 2);
+              tc_mma(dacc + (uint32_t)(sh * L::kN), ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc,
+                     (kb > 0 || k > 0) ? 1u : 0u);
+            }
           }
           tc_commit(&empty[s]);  // the stage is free once these MMAs have read it
           if (++s == S) {
@@ -366,8 +392,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         break;
       }
       tc_fence_after();
-      const int rt = t / ta.n_tok, tt = t % ta.n_tok;
-      tc_epilogue<NT>(ta, tbase + (uint32_t)(buf * 2 * NT), rt * kTcBM, tt * NT, warp, lane);
+      const int tt = t % ta.n_tok, ks = (t / ta.n_tok) % ta.ksplit, rt = t / (ta.n_tok * ta.ksplit);
+      tc_epilogue<NT>(ta, tbase + (uint32_t)(buf * L::kBuf), rt * kTcBM, tt * NT, ks, warp, lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
@@ -383,11 +409,34 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == 5) tmem_dealloc(tbase, kCols);
 }
 
+// Split-K reduction: CTA (row tile, token tile), thread = weight row; partial sums added in split
+// order, then the epilogue.
+template <int NT>
+__global__ void __launch_bounds__(128) tc_reduce_kernel(const __grid_constant__ TcArgs ta) {
+  pdl_wait();
+  const int rt = blockIdx.x, tt = blockIdx.y;
+  const int lane = threadIdx.x & 31;
+  const int n = rt * kTcBM + threadIdx.x;
+  const int rows_all = ta.n_row * kTcBM;
+  for (int j = 0; j < NT; ++j) {
+    const int m = tt * NT + j;
+    const bool live = m < ta.M;
+    float yc = 0.f, ys = 0.f;
+    for (int ks = 0; ks < ta.ksplit; ++ks) {
+      const float* w = ta.ws + (((size_t)ks * ta.n_tok * NT + (size_t)m) * rows_all + n) * 2;
+      yc = (ks == 0) ? __ldcg(w) : __fadd_rn(yc, __ldcg(w));
+      ys = (ks == 0) ? __ldcg(w + 1) : __fadd_rn(ys, __ldcg(w + 1));
+    }
+    tc_epi_value(ta, n, m, live, yc, ys, lane);
+  }
+}
+
 // Split f32 shares into the six bf16 planes [share * 3 + term][Mp][KP], columns permuted as in the
 // weight blocks (physical j of chunk c <- logical column c*256 + 4 (j/8) + (j%8 < 4 ? j%8 : 124 + j%8)),
 // zero beyond K and beyond M.
 __global__ void split_planes_kernel(const float* __restrict__ xc, const float* __restrict__ xs, int ldx, int M,
                                     int K, int Mp, int KP, uint16_t* __restrict__ out) {
+  pdl_wait();  // the shares come from the previous kernel
   const size_t plane = (size_t)Mp * KP;
   const long long total = (long long)Mp * KP;
   for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
@@ -485,21 +534,30 @@ int launch_tc_t(shd_ctx* ctx, const TcArgs& ta, const CUtensorMap& mw, const CUt
   }
   TcArgs a = ta;
   a.nstages = S;
-  const int tiles = a.n_row * a.n_tok;
+  const int tiles = a.n_row * a.n_tok * a.ksplit;
   const int grid = std::min(tiles, ctx->num_sms);
   SHD_CHECK_CUDA(ctx, launch_pdl(tc_linear_kernel<NT>, dim3(grid), dim3(kTcThreads), smem, ctx->stream, a, mw, mx));
   ctx->launches++;
+  if (a.ksplit > 1) {
+    SHD_CHECK_CUDA(ctx, launch_pdl(tc_reduce_kernel<NT>, dim3(a.n_row, a.n_tok), dim3(128), 0, ctx->stream, a));
+    ctx->launches++;
+  }
+  return SHD_OK;
+}
+
+int ensure_ws(shd_ctx* ctx, size_t floats) {
+  if (ctx->tc_ws_floats >= floats) return SHD_OK;
+  if (ctx->d_tc_ws) cudaFree(ctx->d_tc_ws);
+  ctx->d_tc_ws = nullptr;
+  ctx->tc_ws_floats = 0;
+  SHD_CHECK_CUDA(ctx, cudaMalloc(&ctx->d_tc_ws, floats * 4));
+  ctx->tc_ws_floats = floats;
   return SHD_OK;
 }
 
 }  // namespace
 
-int tc_token_tile(int M) {
-  if (M <= 8) return 8;
-  if (M <= 16) return 16;
-  if (M <= 32) return 32;
-  return 64;
-}
+int tc_token_tile(int M) { return M <= 16 ? 16 : 32; }
 
 int launch_linear_tc(shd_ctx* ctx, const shd_weight* w, int M, int epi, GemvArgs g) {
   if (w->kind != WK_BF16) return shd_fail(ctx, SHD_ERR_ARG, "tensor-core linear: need a bf16 weight");
@@ -538,13 +596,21 @@ int launch_linear_tc(shd_ctx* ctx, const shd_weight* w, int M, int epi, GemvArgs
   ta.n_tok = n_tok;
   ta.n_row = (w->nT + 3) / 4;
   ta.n_kb = w->nKC * (kChunkBf16 / kTcBK);
-  const CUtensorMap& mw = *static_cast<const CUtensorMap*>(w->tmap);
-  switch (nt) {
-    case 8: return launch_tc_t<8>(ctx, ta, mw, mx);
-    case 16: return launch_tc_t<16>(ctx, ta, mw, mx);
-    case 32: return launch_tc_t<32>(ctx, ta, mw, mx);
-    default: return launch_tc_t<64>(ctx, ta, mw, mx);
+  // split K when the output tiles cannot fill the SMs: the largest divisor of the K blocks that
+  // keeps at least 8 blocks per split and about one work item per SM
+  ta.ksplit = 1;
+  {
+    const int items = ta.n_row * n_tok;
+    for (int d = 2; d <= 16; ++d)
+      if (ta.n_kb % d == 0 && ta.n_kb / d >= 8 && items * d <= ctx->num_sms + items) ta.ksplit = d;
   }
+  if (ta.ksplit > 1) {
+    if ((rc = ensure_ws(ctx, (size_t)ta.ksplit * n_tok * nt * ta.n_row * kTcBM * 2))) return rc;
+    ta.ws = ctx->d_tc_ws;
+  }
+  const CUtensorMap& mw = *static_cast<const CUtensorMap*>(w->tmap);
+  if (nt == 16) return launch_tc_t<16>(ctx, ta, mw, mx);
+  return launch_tc_t<32>(ctx, ta, mw, mx);
 }
 
 void free_weight_map(shd_weight* w) {

@@ -5,7 +5,11 @@
 
 namespace shd {
 
-// Token rows per output tile for M rows (8, 16, 32 or 64).
+// Rows from which the tensor cores beat the CUDA-core GEMV (whose arithmetic per weight byte grows
+// with the rows until it is no longer bandwidth-bound).
+constexpr int kTcMinRows = 5;
+
+// Token rows per output tile for M rows (16 or 32).
 int tc_token_tile(int M);
 // Y shares of M rows through the tensor cores with the epilogue `epi` (EPI_STORE, EPI_QKV or
 // EPI_GATEUP; same GemvArgs fields as launch_gemv_f32 with staged activations Xc/Xs/ldx).

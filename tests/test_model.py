@@ -125,10 +125,11 @@ def test_mpc_masks_reshare(ctx, orc):
         assert np.max(np.abs(ls)) > 0
 
 
-@pytest.mark.parametrize("variant", ["approx", "mpc"])
-def test_batched_decode_engines_agree_with_oracle(ctx, orc, variant):
-    """Three slots decoded together (M = 3 rows per step) by both engines, each checked against the
-    oracle slot by slot (teacher-forced on the GPU's tokens)."""
+@pytest.mark.parametrize("variant,slots", [("approx", 3), ("mpc", 3), ("approx", 6)])
+def test_batched_decode_engines_agree_with_oracle(ctx, orc, variant, slots):
+    """Slots decoded together (M rows per step) by both engines, each checked against the oracle slot
+    by slot (teacher-forced on the GPU's tokens). With 6 rows the per-kernel engine runs the layer
+    linears on the tensor cores."""
     from shardlm_b200._lib import NL_APPROX, NL_GPU, NL_MPC
     from shardlm_b200.model import TINY, SecureModel
     from shardlm_b200.sharing import beaver_triples_f32
@@ -136,11 +137,12 @@ def test_batched_decode_engines_agree_with_oracle(ctx, orc, variant):
     shape = TINY.replace(n_layers=2)
     nl = NL_MPC if variant == "mpc" else NL_APPROX
     nl_pre = NL_MPC if variant == "mpc" else NL_GPU
-    prompts = [np.array(p, np.int32) for p in ([5, 17, 300], [9, 2, 44, 11, 7], [999])]
+    prompts = [np.array(p, np.int32) for p in ([5, 17, 300], [9, 2, 44, 11, 7], [999], [1, 2], [640, 3, 3, 8],
+                                               [77, 78, 79, 80, 81, 82])][:slots]
     steps = 5
     results = {}
     for engine in (1, 0):
-        m = SecureModel(ctx, shape, max_seq=32, max_batch=3, share_seed=77, variant_decode=nl,
+        m = SecureModel(ctx, shape, max_seq=32, max_batch=slots, share_seed=77, variant_decode=nl,
                         variant_prefill=nl_pre, variant_attn=nl)
         m.set_engine(engine)
         host = m.load_random_weights(seed=12, host_copy=True)
@@ -151,7 +153,7 @@ def test_batched_decode_engines_agree_with_oracle(ctx, orc, variant):
             m.set_masks(a)
             masks = a.cpu().numpy()
         first = [m.prefill(p, slot=b) for b, p in enumerate(prompts)]
-        toks = m.decode(steps, n_active=3)
+        toks = m.decode(steps, n_active=slots)
         assert m.engine == engine
         results[engine] = toks
         om = [_oracle_for(orc, shape, host, 32) for _ in prompts]
