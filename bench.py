@@ -217,8 +217,30 @@ def run_ours(args, shape):
     model.set_engine(args.engine)
     model.load_random_weights(seed=0)
     rng = np.random.default_rng(0)  # seeded uniform prompt token ids
-    for b in range(B):
-        model.prefill(rng.integers(0, shape.vocab, args.prompt).astype(np.int32), slot=b)
+    prompts = [rng.integers(0, shape.vocab, args.prompt).astype(np.int32) for _ in range(B)]
+    # prefill throughput (config 3/5 report it beside decode): the first slot's prompt warms up the
+    # kernels, the others (or, with one slot, a second prefill after a reset) are timed
+    model.prefill(prompts[0], slot=0)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t_pf = time.perf_counter()
+    if B > 1:
+        for b in range(1, B):
+            model.prefill(prompts[b], slot=b)
+        n_pf = (B - 1) * args.prompt
+    else:
+        model.reset()
+        model.prefill(prompts[0], slot=0)
+        n_pf = args.prompt
+    torch.cuda.synchronize()
+    pf_s = time.perf_counter() - t_pf
+    if world > 1:
+        t = torch.tensor([pf_s], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        pf_s = float(t.item())
+    prefill = {"tokens": n_pf, "seconds": round(pf_s, 4), "tok_s": round(n_pf / pf_s, 1),
+               "path": "shd_model_prefill, 128-position chunks through the tcgen05 linears (host-synchronous)"}
     lib = _lib.lib()
     model.decode_async(args.warmup)
     torch.cuda.synchronize()
@@ -339,6 +361,7 @@ def run_ours(args, shape):
             "step_roofline": {"weight_bytes_per_token_per_gpu": int(weight_bytes),
                               "frac_of_hbm": round(weight_bytes / (ms_step * 1e-3) / 1e9 / peak, 4)},
             "e2e": e2e,
+            "prefill": prefill,
             "cpu_baseline": cpu,
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks.summary(),

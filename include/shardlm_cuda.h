@@ -100,8 +100,9 @@ int64_t shd_weight_device_bytes(const shd_weight* w);
 
 /* GpuSecureLinear::forward_secure_gpu_tensor (crates/v2/sharing/src/secure_linear.rs:357-404):
  *   yc = xc . W^T (+ residual_c),   ys = xs . W^T + bias (+ residual_s)
- * xc, xs: [M][in]; yc, ys, residual_*: [M][out]. M <= 4: one streaming pass over W (CUDA cores)
- * serves both shares and all rows. M >= 5: the tcgen05 tensor-core path, each f32 share split
+ * xc, xs: [M][in]; yc, ys, residual_*: [M][out]. Few rows (up to 8 for weights under 48 M entries,
+ * up to 2 for larger ones): one streaming pass over W on the CUDA cores serves both shares and all
+ * rows. More rows: the tcgen05 tensor-core path, each f32 share split
  * exactly into three bf16 terms, f32 accumulation in tensor memory (same tolerance). bias (device,
  * nullable, [out]) overrides the bias stored with the weight when given.
  * residual_c/residual_s are both null or both set (secure_add_gpu fused in,

@@ -588,7 +588,7 @@ extern "C" int shd_linear_dual_f32(shd_ctx* ctx, const shd_weight* w, const floa
     xc = reinterpret_cast<const float*>(pc);
     xs = reinterpret_cast<const float*>(ps);
   }
-  if (M >= kTcMinRows) {
+  if (tc_preferred(w, M)) {
     // many rows: the tensor-core path (one pass over the weights for all rows)
     GemvArgs a{};
     a.Xc = xc;

@@ -408,9 +408,9 @@ int shd_model::norm_into(GemvArgs& g, const shd_weight* w, int M, const float* H
                          const float* Dc, const float* Ds, float* Oc, float* Os, const float* gamma,
                          int variant, const float* mask, bool& fused) {
   const int h = cfg.hidden;
-  // fused into the GEMV when its activations fit the CTA; the tensor-core path (M >= kTcMinRows,
-  // per-kernel engine) reads staged activations
-  fused = (size_t)M * 2 * w->nKC * kChunkBf16 * 4 <= 120 * 1024 && (M < kTcMinRows || rec != nullptr);
+  // fused into the GEMV when its activations fit the CTA; the tensor-core path (per-kernel engine)
+  // reads staged activations
+  fused = (size_t)M * 2 * w->nKC * kChunkBf16 * 4 <= 120 * 1024 && (rec != nullptr || !tc_preferred(w, M));
   if (fused) {
     g.nHc = Hc; g.nHs = Hs; g.nDc = Dc; g.nDs = Ds; g.nHout_c = Oc; g.nHout_s = Os; g.n_ldh = h;
     g.gamma = gamma; g.eps = cfg.rms_eps; g.nvariant = variant; g.nmask = mask; g.n_ldmask = 0;
@@ -426,7 +426,7 @@ int shd_model::norm_into(GemvArgs& g, const shd_weight* w, int M, const float* H
 
 int shd_model::op_gemv(const shd_weight* w, int M, int epi, const GemvArgs& g, bool norm, int kind) {
   if (!rec) {
-    if (M >= kTcMinRows && epi != EPI_LOGITS && !norm) return launch_linear_tc(ctx, w, M, epi, g);
+    if (epi != EPI_LOGITS && !norm && tc_preferred(w, M)) return launch_linear_tc(ctx, w, M, epi, g);
     return launch_gemv_f32(ctx, w, M, epi, g, norm);
   }
   StepJob j{};

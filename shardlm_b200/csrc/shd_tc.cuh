@@ -5,9 +5,14 @@
 
 namespace shd {
 
-// Rows from which the tensor cores beat the CUDA-core GEMV (whose arithmetic per weight byte grows
-// with the rows until it is no longer bandwidth-bound).
-constexpr int kTcMinRows = 5;
+// Whether M rows of a linear with weight w go to the tensor cores rather than the CUDA-core GEMV.
+// The GEMV's arithmetic per weight byte grows with the rows: measured on B200 it stays ahead up to
+// 8 rows for the latency-bound small projections (q/k/v, o: < 48 M weights) and up to 2 rows for
+// the large ones (gate/up, down, lm_head), where 16-row tensor-core tiles already stream faster.
+inline bool tc_preferred(const shd_weight* w, int M) {
+  if (M > 8) return true;
+  return M >= 3 && (long long)w->N * w->K >= 48ll * 1024 * 1024;
+}
 
 // Token rows per output tile for M rows (16 or 32).
 int tc_token_tile(int M);

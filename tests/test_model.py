@@ -171,6 +171,33 @@ def test_batched_decode_engines_agree_with_oracle(ctx, orc, variant, slots):
     assert np.mean(results[0] == results[1]) >= 0.9
 
 
+def test_batched_decode_tensor_core_rows(ctx, orc):
+    """Three slots of a 7B-shaped layer: gate/up and down (over 48 M weights) run on the tensor cores
+    at 3 rows, q/k/v and o on the CUDA-core GEMV; tokens checked against the oracle."""
+    from shardlm_b200.model import QWEN2_5_7B, SecureModel
+
+    shape = QWEN2_5_7B.replace(n_layers=1, vocab=4096)
+    prompts = [np.array(p, np.int32) for p in ([5, 17, 300], [9, 2, 44, 11, 7], [999])]
+    steps = 4
+    m = SecureModel(ctx, shape, max_seq=32, max_batch=3, share_seed=5)
+    host = m.load_random_weights(seed=21, host_copy=True)
+    first = [m.prefill(p, slot=b) for b, p in enumerate(prompts)]
+    toks = m.decode(steps, n_active=3)
+    exact = 0
+    for b, p in enumerate(prompts):
+        om = _oracle_for(orc, shape, host, 32)
+        for i, t in enumerate(p):
+            hc, hs = orc.embed_shares(host["embed"], shape.hidden, int(t), 5, (b << 32) + i)
+            om.forward(hc, hs, variant=orc.NL_GPU, attn_variant=orc.NL_APPROX)
+        inp = first[b]
+        for i in range(steps):
+            hc, hs = orc.embed_shares(host["embed"], shape.hidden, int(inp), 5, (b << 32) + len(p) + i)
+            _, _, lc, ls = om.forward(hc, hs, variant=orc.NL_APPROX, attn_variant=orc.NL_APPROX)
+            exact += _check_token(int(toks[i, b]), lc, ls, orc)
+            inp = int(toks[i, b])
+    assert exact >= 3 * steps - 1
+
+
 def test_model_rejects_bad_requests(ctx):
     from shardlm_b200._lib import ShdError
     from shardlm_b200.model import TINY, SecureModel
