@@ -100,7 +100,7 @@ int64_t shd_weight_device_bytes(const shd_weight* w);
 
 /* GpuSecureLinear::forward_secure_gpu_tensor (crates/v2/sharing/src/secure_linear.rs:357-404):
  *   yc = xc . W^T (+ residual_c),   ys = xs . W^T + bias (+ residual_s)
- * xc, xs: [M][in]; yc, ys, residual_*: [M][out]. Few rows (up to 8 for weights under 48 M entries,
+ * xc, xs: [M][in]; yc, ys, residual_*: [M][out]. Few rows (up to 4 for weights under 48 M entries,
  * up to 2 for larger ones): one streaming pass over W on the CUDA cores serves both shares and all
  * rows. More rows: the tcgen05 tensor-core path, each f32 share split
  * exactly into three bf16 terms, f32 accumulation in tensor memory (same tolerance). bias (device,

@@ -35,8 +35,8 @@ constexpr int kAttnGroup = 4;     // query heads per group (kAttnGroupMax bounds
 template <int HD>
 struct AttnSmem {
   static constexpr int KS = HD + 4;  // padded row stride (conflict-free column reads)
-  float k[kAttnTile][KS];
-  float v[kAttnTile][HD];
+  float k[2][kAttnTile][KS];         // double-buffered: the next tile loads during this one
+  float v[2][kAttnTile][HD];
   float q[kAttnGroup][HD];
   float spart[kAttnThreads / 32][kAttnGroup][kAttnTile];  // per-warp partial dots
   float p[kAttnGroup][kAttnTile];                         // tile weights
@@ -89,18 +89,27 @@ __global__ void __launch_bounds__(kAttnThreads) attn_cluster_kernel(const AttnAr
 #pragma unroll
     for (int j = 0; j < DW; ++j) qreg[g][j] = S.q[g][warp * DW + j];
 
-  for (int tb = t0; tb < t1; tb += kAttnTile) {
+  // K and V rows of a tile: 16-byte asynchronous copies (L2 only), zero-filled past the split's end
+  auto stage_tile = [&](int buf, int tb) {
     const int nt = min(kAttnTile, t1 - tb);
-    // stage K and V rows of the tile
     for (int i = tid; i < kAttnTile * (HD / 4); i += kAttnThreads) {
       const int r = i / (HD / 4), c4 = i % (HD / 4);
-      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
-      if (r < nt) {
-        kv = *reinterpret_cast<const float4*>(K + (size_t)(tb + r) * a.kvd + 4 * c4);
-        vv = *reinterpret_cast<const float4*>(V + (size_t)(tb + r) * a.kvd + 4 * c4);
-      }
-      *reinterpret_cast<float4*>(&S.k[r][4 * c4]) = kv;
-      *reinterpret_cast<float4*>(&S.v[r][4 * c4]) = vv;
+      const int row = (r < nt) ? tb + r : tb;  // an in-range address even when nothing is copied
+      const uint32_t bytes = (r < nt) ? 16u : 0u;
+      cp_async16(&S.k[buf][r][4 * c4], K + (size_t)row * a.kvd + 4 * c4, bytes);
+      cp_async16(&S.v[buf][r][4 * c4], V + (size_t)row * a.kvd + 4 * c4, bytes);
+    }
+    cp_async_commit();
+  };
+  if (t0 < t1) stage_tile(0, t0);
+  int buf = 0;
+  for (int tb = t0; tb < t1; tb += kAttnTile, buf ^= 1) {
+    const int nt = min(kAttnTile, t1 - tb);
+    if (tb + kAttnTile < t1) {
+      stage_tile(buf ^ 1, tb + kAttnTile);
+      cp_async_wait<1>();  // this tile's copies have landed (the next tile's may be in flight)
+    } else {
+      cp_async_wait<0>();
     }
     __syncthreads();
     // partial dots: warp = dim slice, lane = position
@@ -110,7 +119,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_cluster_kernel(const AttnAr
       for (int g = 0; g < kAttnGroup; ++g) part[g] = 0.0f;
 #pragma unroll
       for (int j = 0; j < DW; j += 4) {
-        const float4 kk = *reinterpret_cast<const float4*>(&S.k[lane][warp * DW + j]);
+        const float4 kk = *reinterpret_cast<const float4*>(&S.k[buf][lane][warp * DW + j]);
 #pragma unroll
         for (int g = 0; g < kAttnGroup; ++g) {
           part[g] = __fmaf_rn(qreg[g][j + 0], kk.x, part[g]);
@@ -157,11 +166,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_cluster_kernel(const AttnAr
       const int g = pg0 + j * (kAttnThreads / HD);
       if (g < G) {
         float v = __fmul_rn(acc[j], S.alpha[g]);
-        for (int r = 0; r < nt; ++r) v = __fmaf_rn(S.p[g][r], S.v[r][pd], v);
+        for (int r = 0; r < nt; ++r) v = __fmaf_rn(S.p[g][r], S.v[buf][r][pd], v);
         acc[j] = v;
       }
     }
-    __syncthreads();  // the tile buffers are reused
+    __syncthreads();  // this buffer is refilled two tiles later
   }
 
   // gather the cluster's partials into CTA 0 (distributed shared memory), then combine in rank order

@@ -6,11 +6,11 @@
 namespace shd {
 
 // Whether M rows of a linear with weight w go to the tensor cores rather than the CUDA-core GEMV.
-// The GEMV's arithmetic per weight byte grows with the rows: measured on B200 it stays ahead up to
-// 8 rows for the latency-bound small projections (q/k/v, o: < 48 M weights) and up to 2 rows for
-// the large ones (gate/up, down, lm_head), where 16-row tensor-core tiles already stream faster.
+// The GEMV's arithmetic per weight byte grows with the rows. Measured on B200: from 5 rows the
+// 16-row tensor-core tiles are at least as fast for every projection; at 3-4 rows only for the large
+// ones (gate/up, down: >= 48 M weights), the small latency-bound ones (q/k/v, o) stay on the GEMV.
 inline bool tc_preferred(const shd_weight* w, int M) {
-  if (M > 8) return true;
+  if (M >= 5) return true;
   return M >= 3 && (long long)w->N * w->K >= 48ll * 1024 * 1024;
 }
 
