@@ -341,6 +341,8 @@ def run_ours(args, shape):
                                    f"positions {args.prompt}..{args.prompt + args.warmup + args.steps}",
                        "model": shape.name, "global_batch": B, "seq_len": args.prompt,
                        "parallelism": f"tp{world}",
+                       "allreduce": (("nvlink peer-memory one-shot" if lib.shd_tp_peer_path(ctx.ptr) else "nccl")
+                                     if world > 1 else None),
                        "l2": "weights streamed per step (>= 1.7 GB per GPU) exceed the 126 MB L2"},
             "roofline": {"bound": "hbm", "kernel": "gemv_f32_kernel (dual-share linear, all launches of one step)",
                          "achieved": round(achieved, 1) if achieved else None, "peak": peak,

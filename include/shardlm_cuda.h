@@ -232,9 +232,15 @@ int shd_argmax_reconstruct(shd_ctx* ctx, const float* lc, const float* ls, int V
  * -------------------------------------------------------------------------------------------- */
 /* ncclGetUniqueId into 128 bytes (rank 0 creates it and shares it with the others). */
 int shd_tp_unique_id(void* out_128_bytes);
-/* Join the TP group as `rank` of `world` on the context's device (world == 1: no NCCL). */
+/* Join the TP group as `rank` of `world` on the context's device (world == 1: no NCCL). Collective:
+ * also maps a receive buffer of every rank into this one through CUDA IPC (NVLink / NVSwitch peer
+ * memory) for the one-shot all-reduce of decode-sized messages; when any rank cannot, all use NCCL. */
 int shd_tp_init(shd_ctx* ctx, int rank, int world, const void* unique_id_128_bytes);
 int shd_tp_destroy(shd_ctx* ctx);
+/* 1 when the peer-memory all-reduce is set up (messages up to 2 x 8 rows x 8192 floats use it: each
+ * rank stores its partial into every rank's slot, then every rank sums the slots in rank order, so
+ * all ranks hold identical sums); 0 when every all-reduce goes through NCCL. */
+int shd_tp_peer_path(const shd_ctx* ctx);
 /* In-place sum over the group of n floats on the context's stream -- the packed [2][M][h] partial
  * shares of a row-parallel projection -- then a host wait bounded by timeout_ms (<= 0: unbounded);
  * on timeout the communicator is aborted and SHD_ERR_TIMEOUT returned. */

@@ -73,6 +73,7 @@ SIGNATURES: dict[str, tuple] = {
     "shd_tp_unique_id": (I32, [P]),
     "shd_tp_init": (I32, [P, I32, I32, P]),
     "shd_tp_destroy": (I32, [P]),
+    "shd_tp_peer_path": (I32, [P]),
     "shd_allreduce_shares": (I32, [P, P, C.c_size_t, I32]),
     "shd_model_create": (I32, [P, P, PP]),
     "shd_model_destroy": (I32, [P]),

@@ -52,6 +52,11 @@ struct shd_ctx {
   // NCCL (tensor parallelism), loaded at run time
   void* nccl_comm = nullptr;
   int tp_rank = 0, tp_world = 1;
+  // NVLink one-shot all-reduce for decode-sized messages: a receive buffer per rank, mapped into
+  // every rank through CUDA IPC (layout in shd_tp.cu); null when unavailable (NCCL is used instead)
+  void* p2p_local = nullptr;
+  void* p2p_peer[8] = {};
+  size_t p2p_slot_bytes = 0;
 };
 
 int shd_fail(shd_ctx* ctx, int code, const std::string& msg);

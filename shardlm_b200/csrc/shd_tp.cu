@@ -9,6 +9,7 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <algorithm>
 #include <chrono>
 #include <cstring>
 #include <mutex>
@@ -71,6 +72,215 @@ int nccl_fail(shd_ctx* ctx, ncclResult_t r, const char* what) {
   return shd_fail(ctx, SHD_ERR_NCCL, m);
 }
 
+// ------------------------------------------------------------------------------------------------
+// NVLink one-shot all-reduce (sum of f32 shares) for decode-sized messages.
+//
+// Every rank owns a receive buffer mapped into all ranks (CUDA IPC over NVLink/NVSwitch):
+//   [state: 64 ints][slots: 2 parities x world sources x capacity x 8 bytes]
+// Each value travels as ONE 8-byte store {float bits, call epoch} (the epoch is the call count + 1,
+// the same on every rank because every rank makes the same calls), so a receiver needs no fence or
+// flag: it polls the values themselves until their epoch is the current one. A call: each CTA stores
+// its slice of the local partial shares into slot (parity, own rank) of EVERY rank (plain peer
+// stores), then polls its slice of the slots of all sources and sums them in rank order
+// 0..world-1 -- the same order on every rank, so all ranks hold identical sums. The last CTA to
+// finish advances the call count (the next call's epoch and parity). A rank writes slot parity p
+// again only two calls later, after every other rank has pushed the intervening call, which each
+// does only after its own kernel of this call has finished reading slot p.
+// ------------------------------------------------------------------------------------------------
+constexpr int kP2pMaxWorld = 8;
+constexpr size_t kP2pHeader = 64 * 4;                           // state, then slots
+constexpr size_t kP2pCapacity = 2 * 8 * 8192;                   // values: both shares of 8 rows x 8192
+constexpr size_t kP2pSlotBytes = kP2pCapacity * 8;              // {value, epoch} pairs
+constexpr int kP2pThreads = 256;
+
+struct P2pArgs {
+  float* buf;        // local partial shares in, sums out
+  size_t n;          // values
+  uint8_t* peer[kP2pMaxWorld];  // every rank's receive buffer (peer[me] = local)
+  int me, world;
+  int* err;
+};
+
+__device__ __forceinline__ int ld_volatile_s32(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
+
+__device__ __forceinline__ unsigned long long ld_volatile_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_volatile_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__global__ void __launch_bounds__(kP2pThreads) p2p_allreduce_kernel(const __grid_constant__ P2pArgs a) {
+  pdl_wait();  // the partial shares come from the previous kernel
+  uint8_t* local = a.peer[a.me];
+  int* state = reinterpret_cast<int*>(local);  // [0] completed calls, [1] CTAs done with this call
+  const int G = gridDim.x, g = blockIdx.x, tid = threadIdx.x;
+  __shared__ unsigned sh_epoch;
+  if (tid == 0) sh_epoch = (unsigned)ld_volatile_s32(&state[0]) + 1u;
+  __syncthreads();
+  const unsigned epoch = sh_epoch;
+  const int p = (int)(epoch & 1u);
+  const size_t per = (a.n + G - 1) / G;
+  const size_t i0 = (size_t)g * per, i1 = min(a.n, i0 + per);
+  const unsigned long long tag = (unsigned long long)epoch << 32;
+  // push this CTA's slice into slot (p, me) of every rank
+  for (size_t i = i0 + tid; i < i1; i += kP2pThreads) {
+    const unsigned long long v = tag | __float_as_uint(a.buf[i]);
+    for (int q = 0; q < a.world; ++q) {
+      unsigned long long* dst =
+          reinterpret_cast<unsigned long long*>(a.peer[q] + kP2pHeader + ((size_t)p * a.world + a.me) * kP2pSlotBytes);
+      st_volatile_u64(dst + i, v);
+    }
+  }
+  // sum the slice over all sources, in rank order, as their values arrive
+  const uint64_t t0 = globaltimer_ns();
+  bool ok = true;
+  for (size_t i = i0 + tid; i < i1 && ok; i += kP2pThreads) {
+    float acc = 0.f;
+    for (int r = 0; r < a.world; ++r) {
+      const unsigned long long* src =
+          reinterpret_cast<const unsigned long long*>(local + kP2pHeader + ((size_t)p * a.world + r) * kP2pSlotBytes) + i;
+      unsigned long long v = ld_volatile_u64(src);
+      while ((unsigned)(v >> 32) != epoch) {
+        if (globaltimer_ns() - t0 > SHD_WAIT_LIMIT_NS) {
+          ok = false;
+          break;
+        }
+        v = ld_volatile_u64(src);
+      }
+      if (!ok) break;
+      const float x = __uint_as_float((unsigned)v);
+      acc = (r == 0) ? x : __fadd_rn(acc, x);
+    }
+    if (ok) a.buf[i] = acc;
+  }
+  if (!ok) atomicOr(a.err, SHD_DEVERR_TIMEOUT_FULL);
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    if (atomicAdd(&state[1], 1) == G - 1) {
+      // every CTA has read this call's slots: the next call may start
+      state[1] = 0;
+      __threadfence();
+      atomicAdd(&state[0], 1);
+    }
+  }
+}
+
+int p2p_setup(shd_ctx* ctx) {
+  NcclApi* api = nccl_api();
+  const int W = ctx->tp_world;
+  if (W > kP2pMaxWorld) return SHD_OK;  // NCCL only
+  // Every rank takes part in both collectives below whatever happens locally (a rank that left
+  // early would leave the others waiting); a local failure only votes the peer path off.
+  bool ok = true;
+  const size_t bytes = kP2pHeader + (size_t)2 * W * kP2pSlotBytes;
+  void* local = nullptr;
+  cudaIpcMemHandle_t mine;
+  std::memset(&mine, 0, sizeof(mine));
+  if (cudaMalloc(&local, bytes) != cudaSuccess) {
+    local = nullptr;
+    ok = false;
+  } else if (cudaMemset(local, 0, bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess ||
+             cudaIpcGetMemHandle(&mine, local) != cudaSuccess) {
+    ok = false;
+  }
+  cudaGetLastError();
+  // exchange the handles with an NCCL all-gather
+  void* d_handles = nullptr;
+  if (cudaMalloc(&d_handles, (size_t)W * sizeof(cudaIpcMemHandle_t)) != cudaSuccess) {
+    if (local) cudaFree(local);
+    return shd_fail(ctx, SHD_ERR_CUDA, "p2p setup: handle buffer");
+  }
+  cudaMemcpy(static_cast<uint8_t*>(d_handles) + (size_t)ctx->tp_rank * sizeof(mine), &mine, sizeof(mine),
+             cudaMemcpyHostToDevice);
+  const ncclResult_t r = api->AllGather(static_cast<uint8_t*>(d_handles) + (size_t)ctx->tp_rank * sizeof(mine),
+                                        d_handles, sizeof(mine), ncclUint8, static_cast<ncclComm_t>(ctx->nccl_comm),
+                                        ctx->stream);
+  std::vector<cudaIpcMemHandle_t> all(W);
+  if (r == ncclSuccess) {
+    cudaStreamSynchronize(ctx->stream);
+    cudaMemcpy(all.data(), d_handles, (size_t)W * sizeof(mine), cudaMemcpyDeviceToHost);
+  }
+  cudaFree(d_handles);
+  if (r != ncclSuccess) {
+    if (local) cudaFree(local);
+    return nccl_fail(ctx, r, "p2p setup: handle exchange");
+  }
+  for (int q = 0; q < W && ok; ++q) {
+    if (q == ctx->tp_rank) {
+      ctx->p2p_peer[q] = local;
+      continue;
+    }
+    void* ptr = nullptr;
+    if (cudaIpcOpenMemHandle(&ptr, all[q], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      ok = false;
+      cudaGetLastError();
+    }
+    ctx->p2p_peer[q] = ptr;
+  }
+  // every rank must agree on whether the peer path is used: all-reduce the outcome
+  int* d_ok = nullptr;
+  int h_ok = ok ? 1 : 0;
+  if (cudaMalloc(&d_ok, 4) == cudaSuccess) {
+    cudaMemcpy(d_ok, &h_ok, 4, cudaMemcpyHostToDevice);
+    if (api->AllReduce(d_ok, d_ok, 1, ncclInt32, ncclMin, static_cast<ncclComm_t>(ctx->nccl_comm), ctx->stream) ==
+        ncclSuccess) {
+      cudaStreamSynchronize(ctx->stream);
+      cudaMemcpy(&h_ok, d_ok, 4, cudaMemcpyDeviceToHost);
+    } else {
+      h_ok = 0;
+    }
+    cudaFree(d_ok);
+  } else {
+    h_ok = 0;
+  }
+  if (!h_ok) {
+    for (int q = 0; q < W; ++q)
+      if (q != ctx->tp_rank && ctx->p2p_peer[q]) cudaIpcCloseMemHandle(ctx->p2p_peer[q]);
+    for (int q = 0; q < kP2pMaxWorld; ++q) ctx->p2p_peer[q] = nullptr;
+    if (local) cudaFree(local);
+    return SHD_OK;
+  }
+  ctx->p2p_local = local;
+  ctx->p2p_slot_bytes = kP2pSlotBytes;
+  return SHD_OK;
+}
+
+void p2p_teardown(shd_ctx* ctx) {
+  if (!ctx->p2p_local) return;
+  for (int q = 0; q < ctx->tp_world && q < kP2pMaxWorld; ++q)
+    if (q != ctx->tp_rank && ctx->p2p_peer[q]) cudaIpcCloseMemHandle(ctx->p2p_peer[q]);
+  cudaFree(ctx->p2p_local);
+  ctx->p2p_local = nullptr;
+  for (int q = 0; q < kP2pMaxWorld; ++q) ctx->p2p_peer[q] = nullptr;
+}
+
+// Sum n floats of buf over the TP group on `stream`: the peer path when it is set up and the
+// message fits a slot (decode), NCCL otherwise.
+int allreduce_f32(shd_ctx* ctx, float* buf, size_t n, cudaStream_t stream) {
+  if (ctx->p2p_local && n <= kP2pCapacity) {
+    P2pArgs a{};
+    a.buf = buf;
+    a.n = n;
+    for (int q = 0; q < ctx->tp_world; ++q) a.peer[q] = static_cast<uint8_t*>(ctx->p2p_peer[q]);
+    a.me = ctx->tp_rank;
+    a.world = ctx->tp_world;
+    a.err = ctx->d_err;
+    const int G = (int)std::max<size_t>(1, std::min<size_t>(32, (n + kP2pThreads - 1) / kP2pThreads));
+    SHD_CHECK_CUDA(ctx, launch_pdl(p2p_allreduce_kernel, dim3(G), dim3(kP2pThreads), 0, stream, a));
+    ctx->launches++;
+    return SHD_OK;
+  }
+  NcclApi* api = nccl_api();
+  const ncclResult_t r = api->AllReduce(buf, buf, n, ncclFloat32, ncclSum, static_cast<ncclComm_t>(ctx->nccl_comm), stream);
+  if (r != ncclSuccess) return nccl_fail(ctx, r, "ncclAllReduce(shares)");
+  return SHD_OK;
+}
+
 }  // namespace
 
 extern "C" int shd_tp_unique_id(void* out_128_bytes) {
@@ -101,8 +311,10 @@ extern "C" int shd_tp_init(shd_ctx* ctx, int rank, int world, const void* unique
   const ncclResult_t r = a->CommInitRank(&comm, world, id, rank);
   if (r != ncclSuccess) return nccl_fail(ctx, r, "ncclCommInitRank");
   ctx->nccl_comm = comm;
-  return SHD_OK;
+  return p2p_setup(ctx);
 }
+
+extern "C" int shd_tp_peer_path(const shd_ctx* ctx) { return (ctx && ctx->p2p_local) ? 1 : 0; }
 
 extern "C" int shd_tp_destroy(shd_ctx* ctx) {
   if (!ctx) return SHD_ERR_ARG;
@@ -110,6 +322,7 @@ extern "C" int shd_tp_destroy(shd_ctx* ctx) {
     NcclApi* a = nccl_api();
     cudaSetDevice(ctx->device);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    p2p_teardown(ctx);
     if (a) a->CommDestroy(static_cast<ncclComm_t>(ctx->nccl_comm));
     ctx->nccl_comm = nullptr;
   }
@@ -145,19 +358,15 @@ extern "C" int shd_allreduce_shares(shd_ctx* ctx, float* buf, size_t n, int time
   if (!ctx) return SHD_ERR_ARG;
   if (ctx->tp_world <= 1 || n == 0) return SHD_OK;
   SHD_REQUIRE(ctx, buf && ctx->nccl_comm, "shd_allreduce_shares: not initialised");
-  NcclApi* a = nccl_api();
   SHD_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
-  const ncclResult_t r = a->AllReduce(buf, buf, n, ncclFloat32, ncclSum, static_cast<ncclComm_t>(ctx->nccl_comm), ctx->stream);
-  if (r != ncclSuccess) return nccl_fail(ctx, r, "ncclAllReduce");
+  const int rc = allreduce_f32(ctx, buf, n, ctx->stream);
+  if (rc) return rc;
   return shd_wait_stream(ctx, ctx->stream, timeout_ms);
 }
 
 int shd_model::allreduce_sum(float* buf, size_t n) {
   if (ctx->tp_world <= 1) return SHD_OK;
-  NcclApi* a = nccl_api();
-  const ncclResult_t r = a->AllReduce(buf, buf, n, ncclFloat32, ncclSum, static_cast<ncclComm_t>(ctx->nccl_comm), stream);
-  if (r != ncclSuccess) return nccl_fail(ctx, r, "ncclAllReduce(shares)");
-  return SHD_OK;
+  return allreduce_f32(ctx, buf, n, stream);
 }
 
 int shd_model::allreduce_max_keys(int M) {

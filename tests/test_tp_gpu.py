@@ -49,6 +49,21 @@ def _rank(rank: int, port: int, q):
 
         ctx = Context(rank)
         init_tensor_parallel(ctx, rank, WORLD)
+        from shardlm_b200._lib import check, lib as _l
+
+        # the all-reduce itself: a decode-sized message (peer path when set up) and a prefill-sized
+        # one (NCCL); every rank must hold the same sums, equal to the rank-order sum
+        sums = []
+        for n in (2 * 1536, 2 * 128 * 1536):
+            parts = [torch.randn(n, generator=torch.Generator().manual_seed(100 + r)) for r in range(WORLD)]
+            buf = parts[rank].cuda()
+            ctx.bind_stream()
+            check(_l().shd_allreduce_shares(ctx.ptr, buf.data_ptr(), n, 60000), ctx.ptr)
+            want = parts[0].clone()
+            for r in range(1, WORLD):
+                want = want + parts[r]
+            sums.append((buf.cpu(), want))
+        peer = int(_l().shd_tp_peer_path(ctx.ptr))
         m = SecureModel(ctx, _shape(), max_seq=64, share_seed=321, tp_rank=rank, tp_world=WORLD)
         m.load_random_weights(seed=11)
         prompt = np.arange(9, dtype=np.int32) * 37 % _shape().vocab
@@ -59,7 +74,8 @@ def _rank(rank: int, port: int, q):
         x = rng.standard_normal(h).astype(np.float32)
         hs = rng.uniform(0, 1, h).astype(np.float32)
         lc, ls = m.forward_host((x - hs).astype(np.float32), hs)
-        q.put((rank, int(first), toks.tolist(), lc.copy(), ls.copy()))
+        q.put((rank, int(first), toks.tolist(), lc.copy(), ls.copy(), peer,
+               [(a.numpy(), b.numpy()) for a, b in sums]))
         m.close()
         from shardlm_b200._lib import lib
 
@@ -68,7 +84,7 @@ def _rank(rank: int, port: int, q):
     except Exception as e:  # reported to the parent
         import traceback
 
-        q.put((rank, "error", f"{e!r}\n{traceback.format_exc()}", None, None))
+        q.put((rank, "error", f"{e!r}\n{traceback.format_exc()}", None, None, None, None))
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
@@ -82,13 +98,21 @@ def test_tp2_tokens_and_logits_match_oracle(orc):
     for p in procs:
         p.start()
     out = {}
+    peers, sums = {}, {}
     for _ in range(WORLD):
-        r, first, toks, lc, ls = q.get(timeout=300)
+        r, first, toks, lc, ls, peer, sm = q.get(timeout=300)
         assert first != "error", toks
         out[r] = (first, toks, lc, ls)
+        peers[r], sums[r] = peer, sm
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
+    # all-reduce: identical on every rank and equal to the rank-order sum (both paths); on NVSwitch
+    # nodes the peer-memory path must have been set up
+    assert peers[0] == peers[1] == 1
+    for i in range(2):
+        assert np.array_equal(sums[0][i][0], sums[1][i][0])
+        np.testing.assert_allclose(sums[0][i][0], sums[0][i][1], rtol=1e-6, atol=1e-6)
     # every rank returns the same tokens and the same gathered logits
     assert out[0][0] == out[1][0] and out[0][1] == out[1][1]
     assert np.array_equal(out[0][2], out[1][2]) and np.array_equal(out[0][3], out[1][3])
