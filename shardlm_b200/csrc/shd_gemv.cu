@@ -398,6 +398,16 @@ static int set_smem_attr(shd_ctx* ctx, Kern kernel, unsigned& devices) {
 // Two CTAs per SM (one streams while the other is in its prologue, split-tile exchange or
 // epilogue) when at least 4 stages fit in half the shared memory and M <= 2 keeps the registers
 // under the two-CTA limit; otherwise one CTA per SM.
+// Grid of a GEMV launch. Stream-K over min(U, per_sm * SMs) CTAs in general; when the weight has at
+// most per_sm * SMs row tiles of at most 16 chunks (256 KB), one CTA per tile instead: every CTA
+// then streams whole tiles and no tile is split, which removes the split-tile exchange from the
+// tail of latency-bound projections (q/k/v, o, and every projection of a tensor-parallel slice).
+static int gemv_grid(const shd_ctx* ctx, const shd_weight* w, long long U, int per_sm) {
+  const long long cap = (long long)per_sm * ctx->num_sms;
+  if (w->nT <= cap && w->nKC <= 16) return w->nT;
+  return (int)std::min<long long>(U, cap);
+}
+
 template <int M, int EPI, bool NORM>
 static int launch_f32_t(shd_ctx* ctx, const shd_weight* w, GemvArgs a) {
   static unsigned attr1 = 0, attr2 = 0;
@@ -411,7 +421,7 @@ static int launch_f32_t(shd_ctx* ctx, const shd_weight* w, GemvArgs a) {
       if (rc) return rc;
       a.nstages = (int)std::min<long long>(kMaxStages, s2);
       const size_t smem = (size_t)a.nstages * stage + xres + kTailBytes;
-      const int G = (int)std::min<long long>(U, 2LL * ctx->num_sms);
+      const int G = gemv_grid(ctx, w, U, 2);
       SHD_CHECK_CUDA(ctx, launch_pdl(gemv_f32_kernel<M, EPI, NORM, 2>, dim3(G), dim3(kGemvThreads), smem, ctx->stream, a));
       ctx->launches++;
       return SHD_OK;
@@ -424,7 +434,7 @@ static int launch_f32_t(shd_ctx* ctx, const shd_weight* w, GemvArgs a) {
   a.nstages = (int)std::min<long long>(kMaxStages, avail / stage);
   if (a.nstages < 2) return shd_fail(ctx, SHD_ERR_ARG, "gemv: activation vector too long for the fused norm");
   const size_t smem = (size_t)a.nstages * stage + xres + kTailBytes;
-  const int G = (int)std::min<long long>(U, ctx->num_sms);
+  const int G = gemv_grid(ctx, w, U, 1);
   SHD_CHECK_CUDA(ctx, launch_pdl(gemv_f32_kernel<M, EPI, NORM, 1>, dim3(G), dim3(kGemvThreads), smem, ctx->stream, a));
   ctx->launches++;
   return SHD_OK;

@@ -242,6 +242,8 @@ __device__ __forceinline__ void red_release_add(int* p, int v) {
   asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
 __device__ __forceinline__ int ld_relaxed_s32(const int* p) {
   int v;
   asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -266,10 +268,9 @@ __device__ int split_tile_close(const PipeSmem& sm, uint32_t& cphase, T* tsum, T
     T* part = partials + (size_t)g * tsum_len;
     for (int k = ctid; k < tsum_len; k += kConsumerWarps * 32) part[k] = tsum[k];
     if (!consumer_sync(sm, cphase, lane)) return -1;
-    if (ctid == 0) {
-      __threadfence();  // the CTA's partial (ordered before by the barrier) before the count
-      red_release_add(&counters[t], 1);
-    }
+    // the release increment orders every thread's partial store before the count: the stores are
+    // ordered before it by the barrier (release/acquire at CTA scope) and release is cumulative
+    if (ctid == 0) red_release_add(&counters[t], 1);
     return 0;
   }
   (void)u1;
@@ -287,7 +288,7 @@ __device__ int split_tile_close(const PipeSmem& sm, uint32_t& cphase, T* tsum, T
       }
     }
     if (ok) {
-      __threadfence();  // acquire side of the contributors' releases
+      fence_acq_rel_gpu();  // acquire side of the contributors' releases
       counters[t] = 0;
     }
     sm.flags[1] = ok ? 1 : 0;
@@ -295,9 +296,18 @@ __device__ int split_tile_close(const PipeSmem& sm, uint32_t& cphase, T* tsum, T
   if (!consumer_sync(sm, cphase, lane)) return -1;
   if (!sm.flags[1]) return -1;
   if (need > 0) {
+    // loads of a batch of contributors are all in flight before the in-order sum consumes them
+    constexpr int B = 8;
     for (int k = ctid; k < tsum_len; k += kConsumerWarps * 32) {
       T sum = tsum[k];
-      for (int gg = g + 1; gg <= gl; ++gg) sum = sum + __ldcg(partials + (size_t)gg * tsum_len + k);
+      for (int g0 = g + 1; g0 <= gl; g0 += B) {
+        T v[B];
+#pragma unroll
+        for (int j = 0; j < B; ++j) v[j] = (g0 + j <= gl) ? __ldcg(partials + (size_t)(g0 + j) * tsum_len + k) : T(0);
+#pragma unroll
+        for (int j = 0; j < B; ++j)
+          if (g0 + j <= gl) sum = sum + v[j];
+      }
       tsum[k] = sum;
     }
     if (!consumer_sync(sm, cphase, lane)) return -1;

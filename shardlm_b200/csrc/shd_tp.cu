@@ -135,27 +135,35 @@ __global__ void __launch_bounds__(kP2pThreads) p2p_allreduce_kernel(const __grid
       st_volatile_u64(dst + i, v);
     }
   }
-  // sum the slice over all sources, in rank order, as their values arrive
+  // sum the slice over all sources, in rank order, as their values arrive: the values of every
+  // source are loaded together, only the ones not yet current are polled again
   const uint64_t t0 = globaltimer_ns();
   bool ok = true;
+  const unsigned long long* slots =
+      reinterpret_cast<const unsigned long long*>(local + kP2pHeader + (size_t)p * a.world * kP2pSlotBytes);
+  const size_t stride = kP2pSlotBytes / 8;
   for (size_t i = i0 + tid; i < i1 && ok; i += kP2pThreads) {
-    float acc = 0.f;
-    for (int r = 0; r < a.world; ++r) {
-      const unsigned long long* src =
-          reinterpret_cast<const unsigned long long*>(local + kP2pHeader + ((size_t)p * a.world + r) * kP2pSlotBytes) + i;
-      unsigned long long v = ld_volatile_u64(src);
-      while ((unsigned)(v >> 32) != epoch) {
-        if (globaltimer_ns() - t0 > SHD_WAIT_LIMIT_NS) {
-          ok = false;
-          break;
+    unsigned long long v[kP2pMaxWorld];
+#pragma unroll
+    for (int r = 0; r < kP2pMaxWorld; ++r) v[r] = (r < a.world) ? ld_volatile_u64(slots + r * stride + i) : tag;
+    while (true) {
+      bool all = true;
+#pragma unroll
+      for (int r = 0; r < kP2pMaxWorld; ++r)
+        if ((unsigned)(v[r] >> 32) != epoch) {
+          all = false;
+          v[r] = ld_volatile_u64(slots + r * stride + i);
         }
-        v = ld_volatile_u64(src);
+      if (all) break;
+      if (globaltimer_ns() - t0 > SHD_WAIT_LIMIT_NS) {
+        ok = false;
+        break;
       }
-      if (!ok) break;
-      const float x = __uint_as_float((unsigned)v);
-      acc = (r == 0) ? x : __fadd_rn(acc, x);
     }
-    if (ok) a.buf[i] = acc;
+    if (!ok) break;
+    float acc = __uint_as_float((unsigned)v[0]);
+    for (int r = 1; r < a.world; ++r) acc = __fadd_rn(acc, __uint_as_float((unsigned)v[r]));
+    a.buf[i] = acc;
   }
   if (!ok) atomicOr(a.err, SHD_DEVERR_TIMEOUT_FULL);
   __syncthreads();
