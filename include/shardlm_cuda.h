@@ -60,6 +60,11 @@ const char* shd_last_error(shd_ctx* ctx);
 /* Synchronise the stream and report any error a kernel recorded in the context's error word
  * (a bounded wait that ran out -> SHD_ERR_TIMEOUT). Clears the word. */
 int shd_sync(shd_ctx* ctx);
+/* Failure-path self-test (no counterpart in the reference): enqueue a kernel that waits on a device
+ * flag nothing sets, bounded by limit_ms (1..2000) of GPU time, then records a timeout in the error
+ * word exactly as an expired pipeline wait does. The next shd_sync returns SHD_ERR_TIMEOUT and clears
+ * the word; the context stays usable. No fault, trap or hang is involved. */
+int shd_wait_selftest(shd_ctx* ctx, int limit_ms);
 /* Number of kernels this context has launched so far (for launch accounting in benchmarks). */
 int64_t shd_launch_count(shd_ctx* ctx);
 

@@ -46,6 +46,7 @@ SIGNATURES: dict[str, tuple] = {
     "shd_last_error": (C.c_char_p, [P]),
     "shd_sync": (I32, [P]),
     "shd_launch_count": (I64, [P]),
+    "shd_wait_selftest": (I32, [P, I32]),
     "shd_weight_upload_f32_as_bf16": (I32, [P, P, I32, I32, PP]),
     "shd_weight_from_bf16": (I32, [P, P, P, I32, I32, I32, I32, PP]),
     "shd_weight_upload_i32": (I32, [P, P, P, I32, I32, PP]),

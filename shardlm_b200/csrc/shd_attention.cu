@@ -67,6 +67,20 @@ __global__ void __launch_bounds__(kAttnThreads) attn_cluster_kernel(const AttnAr
   const float* V = a.Vcache + (size_t)sq * a.kv_seq_stride + (size_t)kvh * HD;
   const bool mpc = a.variant == SHD_NL_MPC;
 
+  // K and V rows of a tile: 16-byte asynchronous copies (L2 only), zero-filled past the split's end
+  auto stage_tile = [&](int buf, int tb) {
+    const int nt = min(kAttnTile, t1 - tb);
+    for (int i = tid; i < kAttnTile * (HD / 4); i += kAttnThreads) {
+      const int r = i / (HD / 4), c4 = i % (HD / 4);
+      const int row = (r < nt) ? tb + r : tb;  // an in-range address even when nothing is copied
+      const uint32_t bytes = (r < nt) ? 16u : 0u;
+      cp_async16(&S.k[buf][r][4 * c4], K + (size_t)row * a.kvd + 4 * c4, bytes);
+      cp_async16(&S.v[buf][r][4 * c4], V + (size_t)row * a.kvd + 4 * c4, bytes);
+    }
+    cp_async_commit();
+  };
+  if (t0 < t1) stage_tile(0, t0);  // in flight while the queries load
+
   for (int i = tid; i < kAttnGroup * HD; i += kAttnThreads) {
     const int g = i / HD, d = i % HD;
     S.q[g][d] = (g < G) ? a.Q[(size_t)m * a.ldq + (size_t)(qh0 + g) * HD + d] : 0.0f;
@@ -89,19 +103,6 @@ __global__ void __launch_bounds__(kAttnThreads) attn_cluster_kernel(const AttnAr
 #pragma unroll
     for (int j = 0; j < DW; ++j) qreg[g][j] = S.q[g][warp * DW + j];
 
-  // K and V rows of a tile: 16-byte asynchronous copies (L2 only), zero-filled past the split's end
-  auto stage_tile = [&](int buf, int tb) {
-    const int nt = min(kAttnTile, t1 - tb);
-    for (int i = tid; i < kAttnTile * (HD / 4); i += kAttnThreads) {
-      const int r = i / (HD / 4), c4 = i % (HD / 4);
-      const int row = (r < nt) ? tb + r : tb;  // an in-range address even when nothing is copied
-      const uint32_t bytes = (r < nt) ? 16u : 0u;
-      cp_async16(&S.k[buf][r][4 * c4], K + (size_t)row * a.kvd + 4 * c4, bytes);
-      cp_async16(&S.v[buf][r][4 * c4], V + (size_t)row * a.kvd + 4 * c4, bytes);
-    }
-    cp_async_commit();
-  };
-  if (t0 < t1) stage_tile(0, t0);
   int buf = 0;
   for (int tb = t0; tb < t1; tb += kAttnTile, buf ^= 1) {
     const int nt = min(kAttnTile, t1 - tb);

@@ -86,6 +86,29 @@ extern "C" const char* shd_last_error(shd_ctx* ctx) {
 
 extern "C" int64_t shd_launch_count(shd_ctx* ctx) { return ctx ? ctx->launches : -1; }
 
+// Waits on a device flag that nothing sets, for at most limit_ns of %globaltimer, then records a
+// stage-fill timeout in the error word and returns, exactly as every pipeline wait does on expiry.
+__global__ void wait_selftest_kernel(const int* flag, uint64_t limit_ns, int* err) {
+  const uint64_t t0 = globaltimer_ns();
+  while (*reinterpret_cast<const volatile int*>(flag) == 0) {
+    if (globaltimer_ns() - t0 > limit_ns) {
+      atomicOr(err, SHD_DEVERR_TIMEOUT_FULL);
+      return;
+    }
+  }
+}
+
+extern "C" int shd_wait_selftest(shd_ctx* ctx, int limit_ms) {
+  if (!ctx) return SHD_ERR_ARG;
+  SHD_REQUIRE(ctx, limit_ms > 0 && limit_ms <= 2000, "shd_wait_selftest: limit_ms must be 1..2000");
+  SHD_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
+  // the error word's allocation holds 4 ints; the last is a zero flag that no kernel ever sets
+  const int* flag = ctx->d_err + 3;
+  wait_selftest_kernel<<<1, 1, 0, ctx->stream>>>(flag, (uint64_t)limit_ms * 1000000ull, ctx->d_err);
+  SHD_CHECK_LAUNCH(ctx, "wait_selftest_kernel");
+  return SHD_OK;
+}
+
 extern "C" int shd_sync(shd_ctx* ctx) {
   if (!ctx) return SHD_ERR_ARG;
   SHD_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));

@@ -415,8 +415,15 @@ static int launch_f32_t(shd_ctx* ctx, const shd_weight* w, GemvArgs a) {
   const size_t xres = NORM ? (size_t)M * 2 * w->nKC * kChunkBf16 * 4 : 0;
   const long long U = (long long)w->nT * w->nKC;
   const long long s2 = ((long long)kSmemPerCta2 - kTailBytes - (long long)xres) / stage;
+  const long long s1 = ((long long)kSmemLimit - kTailBytes - (long long)xres) / stage;
+  // At most one tile per SM: one CTA per SM, with as many stages as the tile has chunks (or as fit
+  // in shared memory). The whole tile is then in flight at once and most of it loads before the
+  // wait on the previous kernel, instead of paying one memory latency per 6 chunks after it.
+  // (Loading the activations whole after the wait, instead of with every block, measured slower:
+  // the first block then waits for the whole vector.)
+  const bool deep_tiles = w->nT <= ctx->num_sms && w->nKC <= 16 && s1 >= std::min<long long>(w->nKC, 8);
   if constexpr (M <= 2) {
-    if (s2 >= 4) {
+    if (s2 >= 4 && !deep_tiles) {
       const int rc = set_smem_attr(ctx, gemv_f32_kernel<M, EPI, NORM, 2>, attr2);
       if (rc) return rc;
       a.nstages = (int)std::min<long long>(kMaxStages, s2);
@@ -430,8 +437,7 @@ static int launch_f32_t(shd_ctx* ctx, const shd_weight* w, GemvArgs a) {
   (void)attr2;
   const int rc = set_smem_attr(ctx, gemv_f32_kernel<M, EPI, NORM, 1>, attr1);
   if (rc) return rc;
-  const long long avail = (long long)kSmemLimit - kTailBytes - (long long)xres;
-  a.nstages = (int)std::min<long long>(kMaxStages, avail / stage);
+  a.nstages = (int)std::min<long long>(deep_tiles ? std::max(w->nKC, 2) : kMaxStages, s1);
   if (a.nstages < 2) return shd_fail(ctx, SHD_ERR_ARG, "gemv: activation vector too long for the fused norm");
   const size_t smem = (size_t)a.nstages * stage + xres + kTailBytes;
   const int G = gemv_grid(ctx, w, U, 1);

@@ -140,6 +140,38 @@ def test_attention_decode(ctx, orc, variant, H, Hkv, kv_len):
         assert err <= 2e-5 * max(1.0, np.max(np.abs(rc))), err
 
 
+@pytest.mark.parametrize("M", [1, 3, 8, 9])
+@pytest.mark.parametrize("H,Hkv,d", [(28, 4, 128), (14, 2, 64)])
+def test_attention_decode_rows(ctx, orc, M, H, Hkv, d):
+    """Several query rows in one launch, each with its own position (0 to the cache's end): the
+    8-CTA cluster of a row and head group splits the row's positions, so short rows leave CTAs
+    without positions, and the combine must weigh them out. A second launch must repeat the
+    first bit for bit."""
+    from shardlm_b200.runtime import ptr
+
+    T = 2048
+    rng = np.random.default_rng(M * 31 + d)
+    q = rng.standard_normal((M, H * d)).astype(np.float32)
+    k = rng.standard_normal((T, Hkv * d)).astype(np.float32)
+    v = rng.standard_normal((T, Hkv * d)).astype(np.float32)
+    pos = np.array([(T - 1, 0, 63, 64, 65, 700, 1500, 128, 2000)[i] for i in range(M)], np.int32)
+    oc, os_ = ctx.empty(M, H * d), ctx.empty(M, H * d)
+    for rep in range(2):
+        ctx.call("shd_attn_decode", ptr(_dev(ctx, q)), ptr(_dev(ctx, k)), ptr(_dev(ctx, v)), T, H, Hkv, d,
+                 pos.ctypes.data, M, 0, None, ptr(oc), ptr(os_))
+        ctx.sync()
+        got = oc.cpu().numpy()
+        for m in range(M):
+            L = int(pos[m]) + 1
+            rc, _ = orc.attention(q[m], k[:L], v[:L], H, Hkv, d, 0, None)
+            err = np.max(np.abs(got[m] - rc))
+            assert err <= 2e-5 * max(1.0, np.max(np.abs(rc))), (rep, m, err)
+        if rep == 0:
+            first = got.copy()
+        else:
+            assert np.array_equal(first, got)
+
+
 def test_embed_shares_bit_exact(ctx, orc):
     from shardlm_b200.runtime import ptr
 

@@ -155,3 +155,44 @@ def test_gloo_world2_row_parallel_and_argmax():
     assert not alive, "a gloo rank did not finish"
     assert not errors, "\n".join(errors)
     assert all(p.exitcode == 0 for p in procs)
+
+
+def _leaver(rank: int, world: int, port: int, errq):
+    """Rank 1 leaves before the unique-id exchange; rank 0 must get an error, not wait forever."""
+    from datetime import timedelta
+
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+        if rank == 1:
+            return  # leaves between steps, with nothing in flight
+        from shardlm_b200.tp import share_unique_id
+
+        try:
+            share_unique_id(rank, "cpu", make_id=lambda: bytes(128))
+        except Exception as e:  # the expected outcome
+            errq.put(("raised", type(e).__name__))
+            return
+        errq.put(("no error", ""))
+    except Exception as e:
+        errq.put(("setup", repr(e)))
+
+
+def test_gloo_rank_leaving_surfaces_as_error():
+    from shardlm_b200._lib import lib
+
+    lib()
+    ctxmp = mp.get_context("spawn")
+    errq = ctxmp.Queue()
+    port = _free_port()
+    procs = [ctxmp.Process(target=_leaver, args=(r, 2, port, errq)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=60)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    assert not alive, "a rank hung instead of failing"
+    outcome = errq.get(timeout=5)
+    assert outcome[0] == "raised", outcome
