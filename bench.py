@@ -23,10 +23,11 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "secret-shared decode tok/s (Qwen2.5-7B shape)"
-# DRAM bytes per algorithmic (weight) byte of the dual-share GEMV launches of a 7B decode step, from
-# ncu captures of each projection (q/k/v 1.002, o 1.003, gate/up 1.014, down 1.026; lm_head taken as
-# 1.0), weighted by their bytes per step.
-TRAFFIC_PER_ALGORITHMIC_BYTE = 1.0151
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per algorithmic (weight) byte of the
+# dual-share GEMV, from one ncu capture of each 7B projection at one row: q/k/v 1.0020, o 1.0026,
+# gate/up 1.0136, down 1.0290, lm_head 1.0043; weighted by their bytes per step 1.0157.
+TRAFFIC_PER_ALGORITHMIC_BYTE_GATEUP = 1.0136
+TRAFFIC_PER_ALGORITHMIC_BYTE = 1.0157
 
 
 def parse():
@@ -329,6 +330,9 @@ def run_ours(args, shape):
         lin_bytes = float(by5[:5].sum())
         n_lin = 4 * shape.n_layers + 1
         achieved = lin_bytes / (lin_ms * 1e-3) / 1e9 if lin_ms > 0 else None
+        gu_bytes = float(by5[2]) / shape.n_layers
+        gu_us = float(ms5[2]) * 1e3 / shape.n_layers if ms5[2] > 0 else None
+        gu_achieved = gu_bytes / (gu_us * 1e-6) / 1e9 if gu_us else None
         ms_step = ms / args.steps
         weight_bytes = shape.linear_params() * 2 / world
         value = B * args.steps / (ms * 1e-3)
@@ -344,16 +348,25 @@ def run_ours(args, shape):
                        "allreduce": (("nvlink peer-memory one-shot" if lib.shd_tp_peer_path(ctx.ptr) else "nccl")
                                      if world > 1 else None),
                        "l2": "weights streamed per step (>= 1.7 GB per GPU) exceed the 126 MB L2"},
-            "roofline": {"bound": "hbm", "kernel": "gemv_f32_kernel (dual-share linear, all launches of one step)",
-                         "achieved": round(achieved, 1) if achieved else None, "peak": peak,
+            # the dominant kernel of the step (about 40 % of it in the ncu launch list): the gate/up
+            # GEMV with its RMSNorm prologue and SwiGLU reshare epilogue, one launch per layer
+            "roofline": {"bound": "hbm",
+                         "kernel": "gemv_f32_kernel<1, 2, 1, 2> (gate/up: RMSNorm prologue, dual-share "
+                                   "linear, SwiGLU reshare epilogue)",
+                         "achieved": round(gu_achieved, 1) if gu_achieved else None, "peak": peak,
                          "peak_source": src, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4) if achieved else None,
-                         "traffic": round(TRAFFIC_PER_ALGORITHMIC_BYTE * lin_bytes / n_lin),
-                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch of "
-                                           "each 7B projection (profiles/gemv_dual_share_7b.md), weighted "
-                                           "over one step: 1.0151 x the algorithmic bytes",
-                         "algorithmic_bytes_per_launch": round(lin_bytes / n_lin),
-                         "avg_launch_us": round(lin_ms * 1e3 / n_lin, 2),
+                         "frac": round(gu_achieved / peak, 4) if gu_achieved else None,
+                         "traffic": round(TRAFFIC_PER_ALGORITHMIC_BYTE_GATEUP * gu_bytes),
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one gate/up "
+                                           "launch (profiles/gemv_dual_share_7b.md): 1.0136 x the "
+                                           "algorithmic bytes",
+                         "algorithmic_bytes_per_launch": round(gu_bytes),
+                         "avg_launch_us": round(gu_us, 2) if gu_us else None,
+                         "all_gemv": {"achieved": round(achieved, 1) if achieved else None,
+                                      "frac": round(achieved / peak, 4) if achieved else None,
+                                      "algorithmic_bytes_per_launch": round(lin_bytes / n_lin),
+                                      "avg_launch_us": round(lin_ms * 1e3 / n_lin, 2),
+                                      "traffic": round(TRAFFIC_PER_ALGORITHMIC_BYTE * lin_bytes / n_lin)},
                          "per_kind_GBps": {k: round(by5[i] / (ms5[i] * 1e-3) / 1e9, 1) if ms5[i] > 0 else None
                                            for i, k in enumerate(["qkv", "o", "gateup", "down", "lm_head"])},
                          "per_kind_us_per_step": {k: round(float(ms5[i]) * 1e3, 1) for i, k in

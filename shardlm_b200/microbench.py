@@ -78,8 +78,9 @@ def linear(args, ctx: Context):
         ms = _time(run, args.iters)
         ctx.sync()
         out[k] = {"N": N, "K": K, "rows": M, "us": round(ms * 1e3, 2), "GBps": round(N * K * 2 / ms / 1e6, 1),
-                  # M > 8 runs on the tensor cores: 2 shares x 3 bf16 terms x 2 flops per weight and row
-                  "tensor_TFLOPs": round(12.0 * M * N * K / ms / 1e9, 1) if M > 8 else None}
+                  # 5 rows and more run on the tensor cores: 2 shares x 3 bf16 terms x 2 flops per
+                  # weight and row
+                  "tensor_TFLOPs": round(12.0 * M * N * K / ms / 1e9, 1) if M >= 5 else None}
         del lins
         torch.cuda.empty_cache()
     print(json.dumps(out))
