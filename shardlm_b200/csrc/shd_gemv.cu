@@ -149,9 +149,11 @@ __global__ void __launch_bounds__(kGemvThreads, MINB) gemv_f32_kernel(const __gr
 
   const int ctid = threadIdx.x;  // 0..255 among consumers
   uint32_t cphase = 0;
+  NormGamma ngam;
+  if constexpr (NORM) norm_gamma_preload(a, ctid, ngam);
   pdl_wait();  // activations, positions and scratch come from earlier kernels
   if constexpr (NORM) {
-    if (!norm_prologue<M>(a, sm, cphase, xres, KP, ctid, lane, warp, g == 0)) {
+    if (!norm_prologue<M>(a, sm, cphase, xres, KP, ctid, lane, warp, g == 0, &ngam)) {
       if (lane == 0) atomicOr(a.err, SHD_DEVERR_TIMEOUT_FULL);
       sm.flags[0] = 1;
       return;
@@ -421,9 +423,15 @@ static int launch_f32_t(shd_ctx* ctx, const shd_weight* w, GemvArgs a) {
   // wait on the previous kernel, instead of paying one memory latency per 6 chunks after it.
   // (Loading the activations whole after the wait, instead of with every block, measured slower:
   // the first block then waits for the whole vector.)
-  const bool deep_tiles = w->nT <= ctx->num_sms && w->nKC <= 16 && s1 >= std::min<long long>(w->nKC, 8);
+  // Fewer row tiles than half the SMs (the q/k/v slice of a tensor-parallel rank): one tile per CTA
+  // would leave most SMs idle and stream a whole tile through each busy one, so the (tile, chunk)
+  // units are spread over one CTA per SM instead, every unit of a CTA in flight at once, and the
+  // split tiles are finished by their owners.
+  const bool few_tiles = 2 * (long long)w->nT < ctx->num_sms && w->nKC >= 4 && s1 >= 2;
+  const bool deep_tiles = !few_tiles && w->nT <= ctx->num_sms && w->nKC <= 16 &&
+                          s1 >= std::min<long long>(w->nKC, 8);
   if constexpr (M <= 2) {
-    if (s2 >= 4 && !deep_tiles) {
+    if (s2 >= 4 && !deep_tiles && !few_tiles) {
       const int rc = set_smem_attr(ctx, gemv_f32_kernel<M, EPI, NORM, 2>, attr2);
       if (rc) return rc;
       a.nstages = (int)std::min<long long>(kMaxStages, s2);
@@ -437,10 +445,15 @@ static int launch_f32_t(shd_ctx* ctx, const shd_weight* w, GemvArgs a) {
   (void)attr2;
   const int rc = set_smem_attr(ctx, gemv_f32_kernel<M, EPI, NORM, 1>, attr1);
   if (rc) return rc;
-  a.nstages = (int)std::min<long long>(deep_tiles ? std::max(w->nKC, 2) : kMaxStages, s1);
+  int G = gemv_grid(ctx, w, U, 1);
+  long long want = deep_tiles ? std::max(w->nKC, 2) : kMaxStages;
+  if (few_tiles) {
+    G = (int)std::min<long long>(U, ctx->num_sms);
+    want = std::max<long long>((U + G - 1) / G, 2);
+  }
+  a.nstages = (int)std::min<long long>(want, s1);
   if (a.nstages < 2) return shd_fail(ctx, SHD_ERR_ARG, "gemv: activation vector too long for the fused norm");
   const size_t smem = (size_t)a.nstages * stage + xres + kTailBytes;
-  const int G = gemv_grid(ctx, w, U, 1);
   SHD_CHECK_CUDA(ctx, launch_pdl(gemv_f32_kernel<M, EPI, NORM, 1>, dim3(G), dim3(kGemvThreads), smem, ctx->stream, a));
   ctx->launches++;
   return SHD_OK;

@@ -340,9 +340,31 @@ __device__ __forceinline__ unsigned long long bf16pair(uint32_t q) {
 // once per group.
 constexpr int kNormGroups = 4;
 
+// The norm's gamma for this thread's first kNormGroups float4 groups, loaded before the wait on
+// the previous kernel: gamma is a weight (written by copies, never by a kernel of the step), so
+// its round trip overlaps the previous kernel instead of following the sum of squares.
+struct NormGamma {
+  float4 g[kNormGroups];
+};
+
+__device__ __forceinline__ void norm_gamma_preload(const GemvArgs& a, int ctid, NormGamma& ng) {
+  constexpr int STEP = kConsumerWarps * 32;
+  const int K4 = a.K >> 2;
+  const bool g_vec = (reinterpret_cast<uintptr_t>(a.gamma) & 15) == 0;
+#pragma unroll
+  for (int j = 0; j < kNormGroups; ++j) {
+    const int i = ctid + j * STEP;
+    ng.g[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (i < K4)
+      ng.g[j] = g_vec ? __ldg(reinterpret_cast<const float4*>(a.gamma) + i)
+                      : make_float4(a.gamma[4 * i], a.gamma[4 * i + 1], a.gamma[4 * i + 2], a.gamma[4 * i + 3]);
+  }
+}
+
 template <int M>
 __device__ bool norm_prologue(const GemvArgs& a, const PipeSmem& sm, uint32_t& cphase, float* xres,
-                              int KP, int ctid, int lane, int warp, bool write_h) {
+                              int KP, int ctid, int lane, int warp, bool write_h,
+                              const NormGamma* pre = nullptr) {
   constexpr int NJ = kNormGroups;
   constexpr int STEP = kConsumerWarps * 32;
   const int K = a.K;
@@ -430,8 +452,11 @@ __device__ bool norm_prologue(const GemvArgs& a, const PipeSmem& sm, uint32_t& c
         gv[j] = z4;
         mv[j] = z4;
         if (i < K4) {
-          gv[j] = g_vec ? reinterpret_cast<const float4*>(a.gamma)[i]
-                        : make_float4(a.gamma[4 * i], a.gamma[4 * i + 1], a.gamma[4 * i + 2], a.gamma[4 * i + 3]);
+          if (pre && b == 0)
+            gv[j] = pre->g[j];
+          else
+            gv[j] = g_vec ? reinterpret_cast<const float4*>(a.gamma)[i]
+                          : make_float4(a.gamma[4 * i], a.gamma[4 * i + 1], a.gamma[4 * i + 2], a.gamma[4 * i + 3]);
           if (mk)
             mv[j] = m_vec ? reinterpret_cast<const float4*>(mk)[i]
                           : make_float4(mk[4 * i], mk[4 * i + 1], mk[4 * i + 2], mk[4 * i + 3]);
