@@ -2,6 +2,7 @@
 #pragma once
 
 #include "shd_common.cuh"
+#include "shd_p2p.cuh"
 
 namespace shd {
 
@@ -92,6 +93,12 @@ struct GemvArgs {
   int* counters;
   int* err;
   int nstages;  // pipeline depth (set by the launcher)
+  // Tensor-parallel push (EPI_STORE, when tp_peer[0] is set): every output value goes, as one
+  // 8-byte {float bits, call epoch} store, into this rank's source slot of every rank's receive
+  // buffer (shd_p2p.cuh) at its index in the packed [2][M][ldy] message, instead of to Yc/Ys; the
+  // receive kernel of the same call sums the sources.
+  uint8_t* tp_peer[8];
+  int tp_me, tp_world;
 };
 
 // Launch the f32-share GEMV for M rows with the given epilogue; `norm` selects the fused RMSNorm

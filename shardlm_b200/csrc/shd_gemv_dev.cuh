@@ -120,6 +120,29 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
 template <int M, int EPI>
 __device__ void epilogue_f32(const GemvArgs& a, int t, const float* tsum, int ctid, int* err) {
   if constexpr (EPI == EPI_STORE) {
+    if (a.tp_peer[0]) {
+      // push the tile to every rank: consecutive threads take consecutive rows of one (peer, share,
+      // row m), so each warp writes 256 contiguous bytes of one peer's slot. The call counter was
+      // last written by the previous receive kernel, which completed before this kernel launched.
+      const unsigned epoch = (unsigned)*reinterpret_cast<const volatile int*>(a.tp_peer[a.tp_me]) + 1u;
+      const unsigned long long tag = (unsigned long long)epoch << 32;
+      const int W = a.tp_world;
+      for (int idx = ctid; idx < kTileRows * M * 2 * W; idx += kConsumerWarps * 32) {
+        const int r = idx % kTileRows;
+        const int m = (idx / kTileRows) % M;
+        const int sh = (idx / (kTileRows * M)) & 1;
+        const int q = idx / (kTileRows * M * 2);
+        const int n = t * kTileRows + r;
+        if (n >= a.N) continue;
+        float y = tsum[(r * 2 + sh) * M + m];
+        if (sh == 1 && a.bias) y = __fadd_rn(y, a.bias[n]);
+        if (a.Rc) y = __fadd_rn(y, __ldcg((sh ? a.Rs : a.Rc) + (size_t)m * a.ldr + n));
+        unsigned long long* dst = p2p_slot(a.tp_peer[q], (int)(epoch & 1u), W, a.tp_me) +
+                                  ((size_t)sh * M + m) * a.ldy + n;
+        asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(dst), "l"(tag | __float_as_uint(y)) : "memory");
+      }
+      return;
+    }
     for (int idx = ctid; idx < kTileRows * M; idx += kConsumerWarps * 32) {
       const int r = idx % kTileRows, m = idx / kTileRows;
       const int n = t * kTileRows + r;

@@ -536,10 +536,11 @@ int shd_model::enqueue_layers(int M, const int* d_pos, const int* d_seq, int var
     GemvArgs go{};
     go.Xc = Abuf; go.Xs = Abuf + (size_t)M * qd; go.ldx = qd;
     go.Yc = Dbuf; go.Ys = Dbuf + (size_t)M * h; go.ldy = h;
+    const bool push_o = tp_push(go, Lw.o, M, (size_t)2 * M * h);
     if ((rc = prof_mark(1, Lw.o, true))) return rc;
     if ((rc = op_gemv(Lw.o, M, EPI_STORE, go, false, KIND_O))) return rc;
     if ((rc = prof_mark(1, Lw.o, false))) return rc;
-    if ((rc = allreduce_sum(Dbuf, (size_t)2 * M * h))) return rc;
+    if ((rc = push_o ? allreduce_recv(Dbuf, (size_t)2 * M * h) : allreduce_sum(Dbuf, (size_t)2 * M * h))) return rc;
     // post-attention norm (h = D + Ho -> Hc) + gate/up + SwiGLU reshare -> ACT
     GemvArgs gu{};
     if ((rc = norm_into(gu, Lw.gateup, M, Ho, Ho + (size_t)M * h, Dbuf, Dbuf + (size_t)M * h, Hc,
@@ -555,10 +556,11 @@ int shd_model::enqueue_layers(int M, const int* d_pos, const int* d_seq, int var
     GemvArgs gd{};
     gd.Xc = ACTbuf; gd.Xs = ACTbuf + (size_t)M * I; gd.ldx = I;
     gd.Yc = Dbuf; gd.Ys = Dbuf + (size_t)M * h; gd.ldy = h;
+    const bool push_d = tp_push(gd, Lw.down, M, (size_t)2 * M * h);
     if ((rc = prof_mark(3, Lw.down, true))) return rc;
     if ((rc = op_gemv(Lw.down, M, EPI_STORE, gd, false, KIND_DOWN))) return rc;
     if ((rc = prof_mark(3, Lw.down, false))) return rc;
-    if ((rc = allreduce_sum(Dbuf, (size_t)2 * M * h))) return rc;
+    if ((rc = push_d ? allreduce_recv(Dbuf, (size_t)2 * M * h) : allreduce_sum(Dbuf, (size_t)2 * M * h))) return rc;
     // the residual stream for the next layer is (Hc, D)
   }
   return SHD_OK;

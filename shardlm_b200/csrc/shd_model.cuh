@@ -88,6 +88,8 @@ struct shd_model {
   int enqueue_decode_step(int M);
   // tensor parallel collectives (no-ops at tp_world == 1)
   int allreduce_sum(float* buf, size_t n);
+  bool tp_push(shd::GemvArgs& g, const shd_weight* w, int M, size_t n);
+  int allreduce_recv(float* buf, size_t n);
   int allreduce_max_keys(int M);
   int gather_logits(float* lc_host, float* ls_host);
 };

@@ -17,8 +17,17 @@
 #include <vector>
 
 #include "shd_model.cuh"
+#include "shd_tc.cuh"
 
 namespace {
+
+using shd::kP2pCapacity;
+using shd::kP2pCtas;
+using shd::kP2pHeader;
+using shd::kP2pMaxWorld;
+using shd::kP2pSlotBytes;
+using shd::kP2pThreads;
+using shd::p2p_slot;
 
 struct NcclApi {
   void* h = nullptr;
@@ -73,35 +82,29 @@ int nccl_fail(shd_ctx* ctx, ncclResult_t r, const char* what) {
 }
 
 // ------------------------------------------------------------------------------------------------
-// NVLink one-shot all-reduce (sum of f32 shares) for decode-sized messages.
+// NVLink one-shot all-reduce (sum of f32 shares) for decode-sized messages; buffer layout, epochs
+// and slot reuse in shd_p2p.cuh.
 //
-// Every rank owns a receive buffer mapped into all ranks (CUDA IPC over NVLink/NVSwitch):
-//   [state: 64 ints][slots: 2 parities x world sources x capacity x 8 bytes]
-// Each value travels as ONE 8-byte store {float bits, call epoch} (the epoch is the call count + 1,
-// the same on every rank because every rank makes the same calls), so a receiver needs no fence or
-// flag: it polls the values themselves until their epoch is the current one. A call: each CTA stores
-// its slice of the local partial shares into slot (parity, own rank) of EVERY rank (plain peer
-// stores), then polls its slice of the slots of all sources and sums them in rank order
-// 0..world-1 -- the same order on every rank, so all ranks hold identical sums. The last CTA to
-// finish advances the call count (the next call's epoch and parity). A rank writes slot parity p
-// again only two calls later, after every other rank has pushed the intervening call, which each
-// does only after its own kernel of this call has finished reading slot p.
+// Two forms. p2p_allreduce_kernel: every CTA stores its slice of the local partial shares into
+// slot (parity, own rank) of EVERY rank (plain peer stores), then polls its slice of the slots of
+// all sources and sums them in rank order 0..world-1 -- the same order on every rank, so all ranks
+// hold identical sums. Fused form: the row-parallel GEMV's epilogue pushes each finished tile
+// itself (GemvArgs::tp_peer), and p2p_recv_kernel only polls and sums; it starts polling as soon as
+// it is resident, before the wait on the GEMV, and writes the sums after that wait (earlier
+// kernels may still read the buffer until then). Neither kernel releases its dependents early:
+// the next kernel starts only after the exchange has completed, which is what makes reading the
+// call counter at the start of the next exchange (or push) safe.
 // ------------------------------------------------------------------------------------------------
-constexpr int kP2pMaxWorld = 8;
-constexpr size_t kP2pHeader = 64 * 4;                           // state, then slots
-constexpr size_t kP2pCapacity = 2 * 8 * 8192;                   // values: both shares of 8 rows x 8192
-constexpr size_t kP2pSlotBytes = kP2pCapacity * 8;              // {value, epoch} pairs
-constexpr int kP2pThreads = 256;
+constexpr int kP2pPer = (int)(kP2pCapacity / ((size_t)kP2pCtas * kP2pThreads));  // values per thread
+static_assert(kP2pPer % 2 == 0, "values per thread come in pairs");
 
 struct P2pArgs {
-  float* buf;        // local partial shares in, sums out
+  float* buf;        // local partial shares in (allreduce form), sums out
   size_t n;          // values
   uint8_t* peer[kP2pMaxWorld];  // every rank's receive buffer (peer[me] = local)
   int me, world;
   int* err;
 };
-
-__device__ __forceinline__ int ld_volatile_s32(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
 
 __device__ __forceinline__ unsigned long long ld_volatile_u64(const unsigned long long* p) {
   unsigned long long v;
@@ -113,69 +116,103 @@ __device__ __forceinline__ void st_volatile_u64(unsigned long long* p, unsigned 
   asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-__global__ void __launch_bounds__(kP2pThreads) p2p_allreduce_kernel(const __grid_constant__ P2pArgs a) {
-  pdl_wait();  // the partial shares come from the previous kernel
-  uint8_t* local = a.peer[a.me];
-  int* state = reinterpret_cast<int*>(local);  // [0] completed calls, [1] CTAs done with this call
-  const int G = gridDim.x, g = blockIdx.x, tid = threadIdx.x;
-  __shared__ unsigned sh_epoch;
-  if (tid == 0) sh_epoch = (unsigned)ld_volatile_s32(&state[0]) + 1u;
-  __syncthreads();
-  const unsigned epoch = sh_epoch;
-  const int p = (int)(epoch & 1u);
-  const size_t per = (a.n + G - 1) / G;
-  const size_t i0 = (size_t)g * per, i1 = min(a.n, i0 + per);
-  const unsigned long long tag = (unsigned long long)epoch << 32;
-  // push this CTA's slice into slot (p, me) of every rank
-  for (size_t i = i0 + tid; i < i1; i += kP2pThreads) {
-    const unsigned long long v = tag | __float_as_uint(a.buf[i]);
-    for (int q = 0; q < a.world; ++q) {
-      unsigned long long* dst =
-          reinterpret_cast<unsigned long long*>(a.peer[q] + kP2pHeader + ((size_t)p * a.world + a.me) * kP2pSlotBytes);
-      st_volatile_u64(dst + i, v);
-    }
-  }
-  // sum the slice over all sources, in rank order, as their values arrive: the values of every
-  // source are loaded together, only the ones not yet current are polled again
-  const uint64_t t0 = globaltimer_ns();
-  bool ok = true;
-  const unsigned long long* slots =
-      reinterpret_cast<const unsigned long long*>(local + kP2pHeader + (size_t)p * a.world * kP2pSlotBytes);
+// This CTA's call counter: written only by CTA blockIdx.x of earlier exchanges, all complete.
+__device__ __forceinline__ int* p2p_counter(const P2pArgs& a) {
+  return reinterpret_cast<int*>(a.peer[a.me]) + blockIdx.x;
+}
+
+// Value k of this thread: index base + k * (all threads of the launch).
+__device__ __forceinline__ size_t p2p_index(int k) {
+  return (size_t)blockIdx.x * kP2pThreads + threadIdx.x + (size_t)k * kP2pCtas * kP2pThreads;
+}
+
+// Poll this thread's values in the slots of every source until all carry `epoch`, two values at a
+// time with every source's word loaded together, and sum each in rank order into acc. False when
+// the wait outlives the limit.
+__device__ bool p2p_collect(const P2pArgs& a, unsigned epoch, float (&acc)[kP2pPer]) {
+  const unsigned long long* slot0 = p2p_slot(a.peer[a.me], (int)(epoch & 1u), a.world, 0);
   const size_t stride = kP2pSlotBytes / 8;
-  for (size_t i = i0 + tid; i < i1 && ok; i += kP2pThreads) {
-    unsigned long long v[kP2pMaxWorld];
+  const unsigned long long tag = (unsigned long long)epoch << 32;
+  const uint64_t t0 = globaltimer_ns();
 #pragma unroll
-    for (int r = 0; r < kP2pMaxWorld; ++r) v[r] = (r < a.world) ? ld_volatile_u64(slots + r * stride + i) : tag;
+  for (int k = 0; k < kP2pPer; k += 2) {
+    const size_t i0 = p2p_index(k), i1 = p2p_index(k + 1);
+    if (i0 >= a.n) break;
+    const bool has1 = i1 < a.n;
+    unsigned long long v0[kP2pMaxWorld], v1[kP2pMaxWorld];
+#pragma unroll
+    for (int r = 0; r < kP2pMaxWorld; ++r) {
+      v0[r] = (r < a.world) ? ld_volatile_u64(slot0 + r * stride + i0) : tag;
+      v1[r] = (r < a.world && has1) ? ld_volatile_u64(slot0 + r * stride + i1) : tag;
+    }
     while (true) {
       bool all = true;
 #pragma unroll
-      for (int r = 0; r < kP2pMaxWorld; ++r)
-        if ((unsigned)(v[r] >> 32) != epoch) {
+      for (int r = 0; r < kP2pMaxWorld; ++r) {
+        if ((unsigned)(v0[r] >> 32) != epoch) {
           all = false;
-          v[r] = ld_volatile_u64(slots + r * stride + i);
+          v0[r] = ld_volatile_u64(slot0 + r * stride + i0);
         }
-      if (all) break;
-      if (globaltimer_ns() - t0 > SHD_WAIT_LIMIT_NS) {
-        ok = false;
-        break;
+        if ((unsigned)(v1[r] >> 32) != epoch) {
+          all = false;
+          v1[r] = ld_volatile_u64(slot0 + r * stride + i1);
+        }
       }
+      if (all) break;
+      if (globaltimer_ns() - t0 > SHD_WAIT_LIMIT_NS) return false;
+      __nanosleep(64);  // polls share the SM with a GEMV still running beside this CTA
     }
-    if (!ok) break;
-    float acc = __uint_as_float((unsigned)v[0]);
-    for (int r = 1; r < a.world; ++r) acc = __fadd_rn(acc, __uint_as_float((unsigned)v[r]));
-    a.buf[i] = acc;
+    float s0 = __uint_as_float((unsigned)v0[0]), s1 = __uint_as_float((unsigned)v1[0]);
+#pragma unroll
+    for (int r = 1; r < kP2pMaxWorld; ++r)
+      if (r < a.world) {
+        s0 = __fadd_rn(s0, __uint_as_float((unsigned)v0[r]));
+        s1 = __fadd_rn(s1, __uint_as_float((unsigned)v1[r]));
+      }
+    acc[k] = s0;
+    acc[k + 1] = s1;
   }
-  if (!ok) atomicOr(a.err, SHD_DEVERR_TIMEOUT_FULL);
-  __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    if (atomicAdd(&state[1], 1) == G - 1) {
-      // every CTA has read this call's slots: the next call may start
-      state[1] = 0;
-      __threadfence();
-      atomicAdd(&state[0], 1);
+  return true;
+}
+
+__device__ __forceinline__ void p2p_finish(const P2pArgs& a, const float (&acc)[kP2pPer], bool ok, unsigned epoch) {
+  if (ok) {
+#pragma unroll
+    for (int k = 0; k < kP2pPer; ++k) {
+      const size_t i = p2p_index(k);
+      if (i < a.n) a.buf[i] = acc[k];
     }
+  } else {
+    atomicOr(a.err, SHD_DEVERR_TIMEOUT_FULL);
   }
+  __syncthreads();  // every thread of the CTA has read the counter
+  if (threadIdx.x == 0) *reinterpret_cast<volatile int*>(p2p_counter(a)) = (int)epoch;
+}
+
+__global__ void __launch_bounds__(kP2pThreads) p2p_allreduce_kernel(const __grid_constant__ P2pArgs a) {
+  const unsigned epoch = (unsigned)*reinterpret_cast<const volatile int*>(p2p_counter(a)) + 1u;
+  pdl_wait();  // the partial shares come from the previous kernel
+  const unsigned long long tag = (unsigned long long)epoch << 32;
+  const int p = (int)(epoch & 1u);
+#pragma unroll
+  for (int k = 0; k < kP2pPer; ++k) {
+    const size_t i = p2p_index(k);
+    if (i >= a.n) break;
+    const unsigned long long v = tag | __float_as_uint(a.buf[i]);
+    for (int q = 0; q < a.world; ++q) st_volatile_u64(p2p_slot(a.peer[q], p, a.world, a.me) + i, v);
+  }
+  float acc[kP2pPer];
+  const bool ok = p2p_collect(a, epoch, acc);
+  p2p_finish(a, acc, ok, epoch);
+}
+
+__global__ void __launch_bounds__(kP2pThreads) p2p_recv_kernel(const __grid_constant__ P2pArgs a) {
+  const unsigned epoch = (unsigned)*reinterpret_cast<const volatile int*>(p2p_counter(a)) + 1u;
+  // polling needs nothing from the previous kernel: only values tagged with this call's epoch count
+  float acc[kP2pPer];
+  const bool ok = p2p_collect(a, epoch, acc);
+  pdl_wait();  // kernels before the pushing GEMV may read the output buffer until it completes
+  p2p_finish(a, acc, ok, epoch);
 }
 
 int p2p_setup(shd_ctx* ctx) {
@@ -278,14 +315,28 @@ int allreduce_f32(shd_ctx* ctx, float* buf, size_t n, cudaStream_t stream) {
     a.me = ctx->tp_rank;
     a.world = ctx->tp_world;
     a.err = ctx->d_err;
-    const int G = (int)std::max<size_t>(1, std::min<size_t>(32, (n + kP2pThreads - 1) / kP2pThreads));
-    SHD_CHECK_CUDA(ctx, launch_pdl(p2p_allreduce_kernel, dim3(G), dim3(kP2pThreads), 0, stream, a));
+    SHD_CHECK_CUDA(ctx, launch_pdl(p2p_allreduce_kernel, dim3(kP2pCtas), dim3(kP2pThreads), 0, stream, a));
     ctx->launches++;
     return SHD_OK;
   }
   NcclApi* api = nccl_api();
   const ncclResult_t r = api->AllReduce(buf, buf, n, ncclFloat32, ncclSum, static_cast<ncclComm_t>(ctx->nccl_comm), stream);
   if (r != ncclSuccess) return nccl_fail(ctx, r, "ncclAllReduce(shares)");
+  return SHD_OK;
+}
+
+// Receive half of the fused exchange: the previous kernel (a GEMV with push fields) has pushed this
+// rank's partial shares; sum every rank's into buf.
+int allreduce_recv_f32(shd_ctx* ctx, float* buf, size_t n, cudaStream_t stream) {
+  P2pArgs a{};
+  a.buf = buf;
+  a.n = n;
+  for (int q = 0; q < ctx->tp_world; ++q) a.peer[q] = static_cast<uint8_t*>(ctx->p2p_peer[q]);
+  a.me = ctx->tp_rank;
+  a.world = ctx->tp_world;
+  a.err = ctx->d_err;
+  SHD_CHECK_CUDA(ctx, launch_pdl(p2p_recv_kernel, dim3(kP2pCtas), dim3(kP2pThreads), 0, stream, a));
+  ctx->launches++;
   return SHD_OK;
 }
 
@@ -376,6 +427,21 @@ int shd_model::allreduce_sum(float* buf, size_t n) {
   if (ctx->tp_world <= 1) return SHD_OK;
   return allreduce_f32(ctx, buf, n, stream);
 }
+
+// A row-parallel GEMV of M rows of w pushes its tiles to the peers itself when the peer path is up,
+// the n-value message fits a slot, the GEMV (not the tensor-core linear) runs it and kernels are
+// launched one by one (engine 0); then fill g's push fields. allreduce_recv completes the sum.
+bool shd_model::tp_push(shd::GemvArgs& g, const shd_weight* w, int M, size_t n) {
+  if (ctx->tp_world <= 1 || !ctx->p2p_local || ctx->tp_world > kP2pMaxWorld || n > kP2pCapacity || rec ||
+      shd::tc_preferred(w, M))
+    return false;
+  for (int q = 0; q < ctx->tp_world; ++q) g.tp_peer[q] = static_cast<uint8_t*>(ctx->p2p_peer[q]);
+  g.tp_me = ctx->tp_rank;
+  g.tp_world = ctx->tp_world;
+  return true;
+}
+
+int shd_model::allreduce_recv(float* buf, size_t n) { return allreduce_recv_f32(ctx, buf, n, stream); }
 
 int shd_model::allreduce_max_keys(int M) {
   if (ctx->tp_world <= 1) return SHD_OK;
