@@ -55,23 +55,25 @@ __global__ void __launch_bounds__(kAttnThreads) attn_cluster_kernel(const AttnAr
   constexpr int NW = kAttnThreads / 32;  // 8 warps
   constexpr int DW = HD / NW;            // dims per warp in the score phase (16 or 8)
   if (tid == 0) pdl_trigger();
-  pdl_wait();  // positions, queries and the cache come from earlier kernels
-
+  // the head groups are copied in before any kernel of the launch sequence runs
   const int4 grp = a.groups[gi];
   const int kvh = grp.x, qh0 = grp.y, G = grp.z;
-  const int kv_len = a.pos[m] + 1;
-  const int sq = a.seq ? a.seq[m] : 0;
+  const bool early = a.early_kv != 0;
+  if (!early) pdl_wait();  // positions, queries and the cache come from earlier kernels
+  const int kv_len = __ldcg(a.pos + m) + 1;
+  const int sq = a.seq ? __ldcg(a.seq + m) : 0;
   const int per = (kv_len + kAttnCluster - 1) / kAttnCluster;
   const int t0 = min(rank * per, kv_len), t1 = min(t0 + per, kv_len);
   const float* K = a.Kcache + (size_t)sq * a.kv_seq_stride + (size_t)kvh * HD;
   const float* V = a.Vcache + (size_t)sq * a.kv_seq_stride + (size_t)kvh * HD;
   const bool mpc = a.variant == SHD_NL_MPC;
 
-  // K and V rows of a tile: 16-byte asynchronous copies (L2 only), zero-filled past the split's end
-  auto stage_tile = [&](int buf, int tb) {
+  // K and V rows [tb + r_lo, tb + r_hi) of a tile: 16-byte asynchronous copies (L2 only); rows of
+  // the tile past the split's end are zero-filled with the first part
+  auto stage_rows = [&](int buf, int tb, int r_lo, int r_hi) {
     const int nt = min(kAttnTile, t1 - tb);
-    for (int i = tid; i < kAttnTile * (HD / 4); i += kAttnThreads) {
-      const int r = i / (HD / 4), c4 = i % (HD / 4);
+    for (int i = tid; i < (r_hi - r_lo) * (HD / 4); i += kAttnThreads) {
+      const int r = r_lo + i / (HD / 4), c4 = i % (HD / 4);
       const int row = (r < nt) ? tb + r : tb;  // an in-range address even when nothing is copied
       const uint32_t bytes = (r < nt) ? 16u : 0u;
       cp_async16(&S.k[buf][r][4 * c4], K + (size_t)row * a.kvd + 4 * c4, bytes);
@@ -79,7 +81,23 @@ __global__ void __launch_bounds__(kAttnThreads) attn_cluster_kernel(const AttnAr
     }
     cp_async_commit();
   };
-  if (t0 < t1) stage_tile(0, t0);  // in flight while the queries load
+  auto stage_tile = [&](int buf, int tb) { stage_rows(buf, tb, 0, kAttnTile); };
+  if (early) {
+    // every row of tile 0 but this step's own (kv_len - 1) before the wait, that row after it
+    const int r_new = kv_len - 1 - t0;  // within tile 0 when 0 <= r_new < kAttnTile
+    if (t0 < t1) {
+      if (r_new >= 0 && r_new < kAttnTile) {
+        stage_rows(0, t0, 0, r_new);
+        stage_rows(0, t0, r_new + 1, kAttnTile);
+      } else {
+        stage_tile(0, t0);
+      }
+    }
+    pdl_wait();  // queries and this step's K/V row come from the q/k/v kernel
+    if (t0 < t1 && r_new >= 0 && r_new < kAttnTile) stage_rows(0, t0, r_new, r_new + 1);
+  } else if (t0 < t1) {
+    stage_tile(0, t0);  // in flight while the queries load
+  }
 
   for (int i = tid; i < kAttnGroup * HD; i += kAttnThreads) {
     const int g = i / HD, d = i % HD;

@@ -35,10 +35,11 @@ namespace {
 constexpr int kMaxRows = 8;        // decode batch (sequence slots stepped together)
 constexpr int kPrefillRows = 128;  // prompt positions per prefill chunk (tensor-core linears)
 
-// Decode bookkeeping after the logits: tokens = keys, history row, position advance.
+// Decode bookkeeping after the logits: tokens = keys, history row, position advance. It does not
+// release its dependents early: the next step's kernels all start after it has completed, so the
+// positions it writes (and every K/V row of earlier steps) may be read before their own waits.
 __global__ void finish_step_kernel(const unsigned long long* keys, int* tokens, int* pos, int* hist,
                                    int hist_cap, unsigned long long* step, int M) {
-  if (threadIdx.x == 0) pdl_trigger();
   pdl_wait();  // the argmax keys come from the lm_head kernel
   const int m = threadIdx.x;
   const unsigned long long s = *step;
@@ -488,7 +489,7 @@ int shd_model::build_step(int M) {
   return rc;
 }
 
-int shd_model::enqueue_layers(int M, const int* d_pos, const int* d_seq, int variant, int& cur) {
+int shd_model::enqueue_layers(int M, const int* d_pos, const int* d_seq, int variant, int& cur, bool decode) {
   const shd_model_config& c = cfg;
   const int h = c.hidden, d = c.head_dim;
   const size_t kv_layer = (size_t)c.max_batch * c.max_seq * kvd;
@@ -529,6 +530,7 @@ int shd_model::enqueue_layers(int M, const int* d_pos, const int* d_seq, int var
     at.partials = ctx->d_attn_part;
     at.counters = ctx->d_counters + (ctx->n_counters - 8192);
     at.err = ctx->d_err;
+    at.early_kv = decode ? 1 : 0;
     if ((rc = prof_mark(5, nullptr, true))) return rc;
     if ((rc = op_attn(at, M))) return rc;
     if ((rc = prof_mark(5, nullptr, false))) return rc;
@@ -642,7 +644,7 @@ extern "C" int shd_model_prefill(shd_model* m, int slot, const int32_t* tokens_h
     ea.Hc = m->Hbuf[0]; ea.Hs = m->Hbuf[0] + (size_t)M * h; ea.ldh = h;
     ea.Dc = m->Dbuf; ea.Ds = m->Dbuf + (size_t)M * h; ea.amax = m->amax; ea.err = ctx->d_err;
     if ((rc = launch_embed(ctx, ea, M))) break;
-    if ((rc = m->enqueue_layers(M, m->p_pos, m->p_seq, m->cfg.variant_prefill, cur))) break;
+    if ((rc = m->enqueue_layers(M, m->p_pos, m->p_seq, m->cfg.variant_prefill, cur, false))) break;
     if (p0 + M == n) {
       if ((rc = m->enqueue_head(M, M - 1, cur, m->cfg.variant_prefill, false, 0))) break;
       if ((rc = m->allreduce_max_keys(1))) break;
@@ -685,7 +687,7 @@ int shd_model::enqueue_decode_step(int M) {
     return shd::step_launch(ctx, step_plan, stream, amax, tokens, pos, hist, hist_cap, step, profiling != 0);
   if ((rc = op_embed(ea, M))) return rc;
   int cur = 0;
-  if ((rc = enqueue_layers(M, pos, seq, cfg.variant_decode, cur))) return rc;
+  if ((rc = enqueue_layers(M, pos, seq, cfg.variant_decode, cur, true))) return rc;
   if ((rc = enqueue_head_rows(M, cur, cfg.variant_decode))) return rc;
   if (rec) return SHD_OK;  // the step kernel does the token update itself
   if ((rc = allreduce_max_keys(M))) return rc;
@@ -804,7 +806,7 @@ extern "C" int shd_model_forward_host(shd_model* m, int slot, const float* hc_ho
   if (e == cudaSuccess) e = cudaMemsetAsync(m->amax, 0, 8, m->stream);
   if (e != cudaSuccess) rc = shd_cuda_fail(ctx, e, "shd_model_forward_host: upload");
   int cur = 0;
-  if (rc == SHD_OK) rc = m->enqueue_layers(1, m->p_pos, m->p_seq, m->cfg.variant_decode, cur);
+  if (rc == SHD_OK) rc = m->enqueue_layers(1, m->p_pos, m->p_seq, m->cfg.variant_decode, cur, true);
   if (rc == SHD_OK) rc = m->enqueue_head(1, 0, cur, m->cfg.variant_decode, true, 0);
   if (rc == SHD_OK) rc = m->gather_logits(logits_c_host, logits_s_host);
   if (rc == SHD_OK) {

@@ -82,7 +82,8 @@ struct shd_model {
   int norm_into(shd::GemvArgs& g, const shd_weight* w, int M, const float* Hc, const float* Hs,
                 const float* Dc, const float* Ds, float* Oc, float* Os, const float* gamma, int variant,
                 const float* mask, bool& fused);
-  int enqueue_layers(int M, const int* d_pos, const int* d_seq, int variant, int& cur);
+  // decode: one new K/V row per sequence row (attention may read the older rows before the wait)
+  int enqueue_layers(int M, const int* d_pos, const int* d_seq, int variant, int& cur, bool decode);
   int enqueue_head(int M, int row, int cur, int variant, bool want_logits, int key_row);
   int enqueue_head_rows(int M, int cur, int variant);
   int enqueue_decode_step(int M);

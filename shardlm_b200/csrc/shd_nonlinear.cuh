@@ -70,6 +70,10 @@ struct AttnArgs {
   float* Os;
   int ldo;
   int nsplit;
+  // Decode launches: every K/V row before pos[m] of row m's slot, and pos/seq themselves, were
+  // written before the previous step ended (only row pos[m] comes from the q/k/v kernel right
+  // before), so they may be read before the wait on that kernel. 0 for prefill chunks.
+  int early_kv;
   float* partials;         // [M][n_groups][nsplit][kAttnGroupMax][head_dim + 2]
   int* counters;           // [M][n_groups]
   int* err;
