@@ -427,7 +427,7 @@ int shd_model::norm_into(GemvArgs& g, const shd_weight* w, int M, const float* H
 
 int shd_model::op_gemv(const shd_weight* w, int M, int epi, const GemvArgs& g, bool norm, int kind) {
   if (!rec) {
-    if (epi != EPI_LOGITS && !norm && tc_preferred(w, M)) return launch_linear_tc(ctx, w, M, epi, g);
+    if (!norm && tc_preferred(w, M)) return launch_linear_tc(ctx, w, M, epi, g);
     return launch_gemv_f32(ctx, w, M, epi, g, norm);
   }
   StepJob j{};

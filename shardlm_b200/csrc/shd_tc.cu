@@ -215,6 +215,27 @@ __device__ __forceinline__ void tc_epi_value(const TcArgs& ta, int n, int m, boo
         cache[(size_t)sq * a.kv_seq_stride + (size_t)pos * a.kv_dim + off] = v;
       }
     }
+  } else if (ta.epi == EPI_LOGITS) {
+    // logit shares (optional) and the greedy key of the reconstructed logit; the 32 lanes are 32
+    // vocabulary rows of one token row, reduced in the warp before one atomic max (as the GEMV)
+    unsigned long long key = 0ull;
+    bool nan = false;
+    if (live && n < a.N) {
+      if (a.Yc) {
+        a.Yc[(size_t)m * a.ldy + n] = yc;
+        a.Ys[(size_t)m * a.ldy + n] = ys;
+      }
+      const float l = __fadd_rn(yc, ys);
+      nan = isnan(l);
+      key = argmax_key(l, n + a.idx_offset);
+    }
+    if (__any_sync(0xffffffffu, nan) && lane == 0) atomicOr(a.err, SHD_DEVERR_NONFINITE);
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+      key = other > key ? other : key;
+    }
+    if (lane == 0 && key != 0ull) atomicMax(&a.amax[m], key);
   } else {  // EPI_GATEUP: lanes 0-15 gate rows, 16-31 the matching up rows of the 32-row tile
     const float uc = __shfl_xor_sync(0xffffffffu, yc, 16);
     const float us = __shfl_xor_sync(0xffffffffu, ys, 16);
@@ -409,26 +430,50 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == 5) tmem_dealloc(tbase, kCols);
 }
 
-// Split-K reduction: CTA (row tile, token tile), thread = weight row; partial sums added in split
-// order, then the epilogue.
+// Split-K reduction: CTA (row tile, token tile) of 128 x 4 threads, threadIdx.x = weight row,
+// threadIdx.y = a quarter of the token tile's rows. Partial sums are added in split order, with the
+// partials of up to 4 splits x NT/4 rows (both shares in one 8-byte load) in flight at once, then
+// the epilogue (its pair exchanges stay within a warp: 32 consecutive weight rows).
+constexpr int kTcReduceY = 4;
+
 template <int NT>
-__global__ void __launch_bounds__(128) tc_reduce_kernel(const __grid_constant__ TcArgs ta) {
+__global__ void __launch_bounds__(kTcBM * kTcReduceY) tc_reduce_kernel(const __grid_constant__ TcArgs ta) {
+  constexpr int JT = NT / kTcReduceY;
+  constexpr int KQ = 16 / JT;  // splits loaded together: 16 partial pairs in flight per thread
   pdl_wait();
   const int rt = blockIdx.x, tt = blockIdx.y;
   const int lane = threadIdx.x & 31;
   const int n = rt * kTcBM + threadIdx.x;
   const int rows_all = ta.n_row * kTcBM;
-  for (int j = 0; j < NT; ++j) {
-    const int m = tt * NT + j;
-    const bool live = m < ta.M;
-    float yc = 0.f, ys = 0.f;
-    for (int ks = 0; ks < ta.ksplit; ++ks) {
-      const float* w = ta.ws + (((size_t)ks * ta.n_tok * NT + (size_t)m) * rows_all + n) * 2;
-      yc = (ks == 0) ? __ldcg(w) : __fadd_rn(yc, __ldcg(w));
-      ys = (ks == 0) ? __ldcg(w + 1) : __fadd_rn(ys, __ldcg(w + 1));
-    }
-    tc_epi_value(ta, n, m, live, yc, ys, lane);
+  const int m0 = tt * NT + threadIdx.y * JT;
+  float yc[JT], ys[JT];
+  for (int ks0 = 0; ks0 < ta.ksplit; ks0 += KQ) {
+    float2 p[KQ][JT];
+#pragma unroll
+    for (int q = 0; q < KQ; ++q)
+#pragma unroll
+      for (int j = 0; j < JT; ++j) {
+        p[q][j] = make_float2(0.f, 0.f);
+        if (ks0 + q < ta.ksplit)
+          p[q][j] = __ldcg(reinterpret_cast<const float2*>(
+              ta.ws + (((size_t)(ks0 + q) * ta.n_tok * NT + (size_t)(m0 + j)) * rows_all + n) * 2));
+      }
+#pragma unroll
+    for (int q = 0; q < KQ; ++q)
+#pragma unroll
+      for (int j = 0; j < JT; ++j) {
+        const int ks = ks0 + q;
+        if (ks == 0) {
+          yc[j] = p[q][j].x;
+          ys[j] = p[q][j].y;
+        } else if (ks < ta.ksplit) {
+          yc[j] = __fadd_rn(yc[j], p[q][j].x);
+          ys[j] = __fadd_rn(ys[j], p[q][j].y);
+        }
+      }
   }
+#pragma unroll
+  for (int j = 0; j < JT; ++j) tc_epi_value(ta, n, m0 + j, m0 + j < ta.M, yc[j], ys[j], lane);
 }
 
 // Split f32 shares into the six bf16 planes [share * 3 + term][Mp][KP], columns permuted as in the
@@ -539,7 +584,8 @@ int launch_tc_t(shd_ctx* ctx, const TcArgs& ta, const CUtensorMap& mw, const CUt
   SHD_CHECK_CUDA(ctx, launch_pdl(tc_linear_kernel<NT>, dim3(grid), dim3(kTcThreads), smem, ctx->stream, a, mw, mx));
   ctx->launches++;
   if (a.ksplit > 1) {
-    SHD_CHECK_CUDA(ctx, launch_pdl(tc_reduce_kernel<NT>, dim3(a.n_row, a.n_tok), dim3(128), 0, ctx->stream, a));
+    SHD_CHECK_CUDA(ctx, launch_pdl(tc_reduce_kernel<NT>, dim3(a.n_row, a.n_tok), dim3(kTcBM, kTcReduceY), 0,
+                                   ctx->stream, a));
     ctx->launches++;
   }
   return SHD_OK;
@@ -561,7 +607,6 @@ int tc_token_tile(int M) { return M <= 16 ? 16 : 32; }
 
 int launch_linear_tc(shd_ctx* ctx, const shd_weight* w, int M, int epi, GemvArgs g) {
   if (w->kind != WK_BF16) return shd_fail(ctx, SHD_ERR_ARG, "tensor-core linear: need a bf16 weight");
-  if (epi == EPI_LOGITS) return shd_fail(ctx, SHD_ERR_UNSUPPORTED, "tensor-core linear: no logits epilogue");
   if (M <= 0) return SHD_OK;
   int rc = gemv_prepare(ctx, w, g, false);
   if (rc) return rc;
