@@ -409,8 +409,9 @@ int shd_model::norm_into(GemvArgs& g, const shd_weight* w, int M, const float* H
                          const float* Dc, const float* Ds, float* Oc, float* Os, const float* gamma,
                          int variant, const float* mask, bool& fused) {
   const int h = cfg.hidden;
+  has_pend_norm = false;
   // fused into the GEMV when its activations fit the CTA; the tensor-core path (per-kernel engine)
-  // reads staged activations
+  // computes it in its plane split
   fused = (size_t)M * 2 * w->nKC * kChunkBf16 * 4 <= 120 * 1024 && (rec != nullptr || !tc_preferred(w, M));
   if (fused) {
     g.nHc = Hc; g.nHs = Hs; g.nDc = Dc; g.nDs = Ds; g.nHout_c = Oc; g.nHout_s = Os; g.n_ldh = h;
@@ -422,12 +423,24 @@ int shd_model::norm_into(GemvArgs& g, const shd_weight* w, int M, const float* H
   na.gamma = gamma; na.eps = cfg.rms_eps; na.variant = variant; na.mask = mask; na.ldmask = 0;
   na.Xc = Xbuf; na.Xs = Xbuf + (size_t)M * h; na.ldx = h; na.n = h;
   g.Xc = Xbuf; g.Xs = Xbuf + (size_t)M * h; g.ldx = h;
+  if (!rec && tc_preferred(w, M)) {
+    // the tensor-core linear computes the norm itself while it splits the bf16 planes (op_gemv)
+    pend_norm = na;
+    has_pend_norm = true;
+    return SHD_OK;
+  }
   return op_norm(na, M);
 }
 
 int shd_model::op_gemv(const shd_weight* w, int M, int epi, const GemvArgs& g, bool norm, int kind) {
   if (!rec) {
-    if (!norm && tc_preferred(w, M)) return launch_linear_tc(ctx, w, M, epi, g);
+    const bool pend = has_pend_norm;
+    has_pend_norm = false;
+    if (!norm && tc_preferred(w, M)) return launch_linear_tc(ctx, w, M, epi, g, pend ? &pend_norm : nullptr);
+    if (pend) {
+      const int rc = op_norm(pend_norm, M);
+      if (rc) return rc;
+    }
     return launch_gemv_f32(ctx, w, M, epi, g, norm);
   }
   StepJob j{};

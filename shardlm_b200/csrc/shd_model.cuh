@@ -90,6 +90,9 @@ struct shd_model {
   // tensor parallel collectives (no-ops at tp_world == 1)
   int allreduce_sum(float* buf, size_t n);
   bool tp_push(shd::GemvArgs& g, const shd_weight* w, int M, size_t n);
+  // norm left for the next tensor-core linear to compute with its plane split (norm_into -> op_gemv)
+  shd::NormArgs pend_norm{};
+  bool has_pend_norm = false;
   int allreduce_recv(float* buf, size_t n);
   int allreduce_max_keys(int M);
   int gather_logits(float* lc_host, float* ls_host);

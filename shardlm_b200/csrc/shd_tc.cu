@@ -509,6 +509,137 @@ __global__ void split_planes_kernel(const float* __restrict__ xc, const float* _
   }
 }
 
+// Logical column of physical plane column j (the weight blocks' column permutation).
+__device__ __forceinline__ int plane_col(int j) {
+  const int c = j >> 8, jj = j & 255;
+  const int l = jj >> 3, i = jj & 7;
+  return c * 256 + (i < 4 ? 4 * l + i : 128 + 4 * l + (i - 4));
+}
+
+// Exact three-term bf16 split of v: v = b0 + b1 + b2.
+__device__ __forceinline__ void split3(float v, uint16_t (&b)[3]) {
+  const __nv_bfloat16 b0 = __float2bfloat16_rn(v);
+  const float r1 = __fsub_rn(v, __bfloat162float(b0));
+  const __nv_bfloat16 b1 = __float2bfloat16_rn(r1);
+  const float r2 = __fsub_rn(r1, __bfloat162float(b1));
+  b[0] = __bfloat16_as_ushort(b0);
+  b[1] = __bfloat16_as_ushort(b1);
+  b[2] = __bfloat16_as_ushort(__float2bfloat16_rn(r2));
+}
+
+// RMSNorm + reshare straight into the six bf16 planes (replaces the norm kernel + split_planes
+// pair before a tensor-core linear). CTA (row m, slice): every CTA of a row reduces the whole row
+// (same thread count and per-thread order as norm_reshare_kernel, so the same inverse RMS) into
+// shared memory, then writes its slice of 256-column chunks of the planes and of h = D + H. Rows
+// from M to Mp are zero.
+constexpr int kNormBatch = 4;
+
+__global__ void norm_planes_kernel(const NormArgs a, int M, int Mp, int KP, int chunks_per_slice,
+                                   uint16_t* __restrict__ out) {
+  extern __shared__ float xrow[];  // [K] x = h_c + h_s of this row
+  __shared__ float red[33];
+  if (threadIdx.x == 0) pdl_trigger();
+  pdl_wait();  // the shares come from earlier kernels
+  const int m = blockIdx.x;
+  const int K = a.n;
+  const size_t plane = (size_t)Mp * KP;
+  const int j0 = blockIdx.y * chunks_per_slice * 256, j1 = min(KP, j0 + chunks_per_slice * 256);
+  const int T = blockDim.x, tid = threadIdx.x;
+  if (m >= M) {
+    for (int j = j0 + tid; j < j1; j += T)
+#pragma unroll
+      for (int p = 0; p < 6; ++p) out[(size_t)p * plane + (size_t)m * KP + j] = 0;
+    return;
+  }
+  const float* hc = a.Hc + (size_t)m * a.ldh;
+  const float* hs = a.Hs + (size_t)m * a.ldh;
+  const float* dc = a.Dc ? a.Dc + (size_t)m * a.ldh : nullptr;
+  const float* ds = a.Ds ? a.Ds + (size_t)m * a.ldh : nullptr;
+  float* oc = a.Hout_c ? a.Hout_c + (size_t)m * a.ldh : nullptr;
+  float* os = a.Hout_s ? a.Hout_s + (size_t)m * a.ldh : nullptr;
+  float sq = 0.0f;
+  for (int b = tid; b < K; b += kNormBatch * T) {
+    float c[kNormBatch], s[kNormBatch], e[kNormBatch], f[kNormBatch];
+#pragma unroll
+    for (int q = 0; q < kNormBatch; ++q) {
+      const int i = b + q * T;
+      c[q] = s[q] = e[q] = f[q] = 0.0f;
+      if (i < K) {
+        c[q] = __ldcg(hc + i);
+        s[q] = __ldcg(hs + i);
+        if (dc) {
+          e[q] = __ldcg(dc + i);
+          f[q] = __ldcg(ds + i);
+        }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < kNormBatch; ++q) {
+      const int i = b + q * T;
+      if (i >= K) break;
+      float cc = c[q], ss = s[q];
+      if (dc) {
+        // residual: sublayer output + residual stream, per share
+        cc = __fadd_rn(e[q], cc);
+        ss = __fadd_rn(f[q], ss);
+        if (oc && i >= j0 && i < j1) {
+          oc[i] = cc;
+          os[i] = ss;
+        }
+      }
+      const float x = __fadd_rn(cc, ss);
+      xrow[i] = x;
+      sq = __fmaf_rn(x, x, sq);
+    }
+  }
+  // block sum (the norm kernel's reduction)
+  {
+    const int lane = tid & 31, warp = tid >> 5, nw = T >> 5;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) sq = __fadd_rn(sq, __shfl_xor_sync(0xffffffffu, sq, o));
+    if (lane == 0) red[warp] = sq;
+    __syncthreads();
+    if (warp == 0) {
+      float w = lane < nw ? red[lane] : 0.0f;
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) w = __fadd_rn(w, __shfl_xor_sync(0xffffffffu, w, o));
+      if (lane == 0) red[32] = w;
+    }
+    __syncthreads();
+  }
+  const float mean_sq = __fdiv_rn(red[32], (float)K);
+  float inv;
+  if (a.variant == SHD_NL_GPU) {
+    inv = rsqrtf(__fadd_rn(mean_sq, a.eps));
+  } else {
+    const float rms = __fsqrt_rn(__fadd_rn(mean_sq, a.eps));
+    if (a.variant == SHD_NL_MPC)
+      inv = (rms > 1e-6f && isfinite(rms)) ? __fdiv_rn(1.0f, rms) : 1.0f;
+    else
+      inv = __fdiv_rn(1.0f, rms);
+  }
+  const float* mk = a.mask ? a.mask + (size_t)m * a.ldmask : nullptr;
+  for (int j = j0 + tid; j < j1; j += T) {
+    const int col = plane_col(j);
+    float vc = 0.0f, vs = 0.0f;
+    if (col < K) {
+      float r = __fmul_rn(__fmul_rn(xrow[col], inv), a.gamma[col]);
+      if (a.variant == SHD_NL_MPC && !isfinite(r)) r = 0.0f;
+      const float mv = mk ? mk[col] : 0.0f;
+      vc = __fsub_rn(r, mv);
+      vs = mv;
+    }
+    uint16_t bc[3], bs[3];
+    split3(vc, bc);
+    split3(vs, bs);
+#pragma unroll
+    for (int t = 0; t < 3; ++t) {
+      out[(size_t)t * plane + (size_t)m * KP + j] = bc[t];
+      out[(size_t)(3 + t) * plane + (size_t)m * KP + j] = bs[t];
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------------------------
@@ -605,7 +736,7 @@ int ensure_ws(shd_ctx* ctx, size_t floats) {
 
 int tc_token_tile(int M) { return M <= 16 ? 16 : 32; }
 
-int launch_linear_tc(shd_ctx* ctx, const shd_weight* w, int M, int epi, GemvArgs g) {
+int launch_linear_tc(shd_ctx* ctx, const shd_weight* w, int M, int epi, GemvArgs g, const NormArgs* norm) {
   if (w->kind != WK_BF16) return shd_fail(ctx, SHD_ERR_ARG, "tensor-core linear: need a bf16 weight");
   if (M <= 0) return SHD_OK;
   int rc = gemv_prepare(ctx, w, g, false);
@@ -616,7 +747,25 @@ int launch_linear_tc(shd_ctx* ctx, const shd_weight* w, int M, int epi, GemvArgs
   const int KP = w->nKC * kChunkBf16;
   if ((rc = ensure_planes(ctx, (size_t)6 * Mp * KP))) return rc;
   uint16_t* planes = reinterpret_cast<uint16_t*>(ctx->d_tc_planes);
-  {
+  if (norm) {
+    if (norm->n != w->K) return shd_fail(ctx, SHD_ERR_ARG, "tensor-core linear: norm width != in_features");
+    // one slice per 256-column chunk up to about two CTAs per SM over the rows
+    const int n_chunks = w->nKC;
+    const int want = std::max(1, (2 * ctx->num_sms) / std::max(Mp, 1));
+    const int cps = std::max(1, (n_chunks + want - 1) / want);
+    const int slices = (n_chunks + cps - 1) / cps;
+    const int threads = norm->n >= 4096 ? 1024 : (norm->n >= 1024 ? 512 : 128);  // as launch_norm
+    const size_t smem = (size_t)norm->n * 4;
+    static unsigned attr_devices = 0;
+    if (smem > 48 * 1024 && !(attr_devices & (1u << (ctx->device & 31)))) {
+      SHD_CHECK_CUDA(ctx, cudaFuncSetAttribute(norm_planes_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+      attr_devices |= 1u << (ctx->device & 31);
+    }
+    if (smem > 200 * 1024) return shd_fail(ctx, SHD_ERR_ARG, "tensor-core linear: norm row too long");
+    SHD_CHECK_CUDA(ctx, launch_pdl(norm_planes_kernel, dim3(Mp, slices), dim3(threads), smem, ctx->stream, *norm, M, Mp,
+                                   KP, cps, planes));
+    ctx->launches++;
+  } else {
     const long long total = (long long)Mp * KP;
     const int blocks = (int)std::min<long long>((total + 255) / 256, 4LL * ctx->num_sms);
     SHD_CHECK_CUDA(ctx, launch_pdl(split_planes_kernel, dim3(blocks), dim3(256), 0, ctx->stream, g.Xc, g.Xs, g.ldx, M,

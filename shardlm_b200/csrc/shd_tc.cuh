@@ -2,6 +2,7 @@
 #pragma once
 
 #include "shd_gemv.cuh"
+#include "shd_nonlinear.cuh"
 
 namespace shd {
 
@@ -16,9 +17,11 @@ inline bool tc_preferred(const shd_weight* w, int M) {
 
 // Token rows per output tile for M rows (16 or 32).
 int tc_token_tile(int M);
-// Y shares of M rows through the tensor cores with the epilogue `epi` (EPI_STORE, EPI_QKV or
-// EPI_GATEUP; same GemvArgs fields as launch_gemv_f32 with staged activations Xc/Xs/ldx).
-int launch_linear_tc(shd_ctx* ctx, const shd_weight* w, int M, int epi, GemvArgs g);
+// Y shares of M rows through the tensor cores with the epilogue `epi` (EPI_STORE, EPI_QKV,
+// EPI_GATEUP or EPI_LOGITS; same GemvArgs fields as launch_gemv_f32 with staged activations
+// Xc/Xs/ldx). With `norm`, the activations are instead reshare(RMSNorm(D + H)) of its fields
+// (n = in_features; its Xc/Xs are not written), computed by the kernel that splits the bf16 planes.
+int launch_linear_tc(shd_ctx* ctx, const shd_weight* w, int M, int epi, GemvArgs g, const NormArgs* norm = nullptr);
 // Release the weight's cached tensor map.
 void free_weight_map(shd_weight* w);
 
