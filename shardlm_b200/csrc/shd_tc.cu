@@ -380,12 +380,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const uint64_t ad = smem_desc_sw128(st);
 #pragma unroll
           for (int k = 0; k < kTcBK / 16; ++k) {
-#pragma unroll
-            for (int sh = 0; sh < 2; ++sh) {
-              // the share's three term planes are 3 NT consecutive rows: one MMA with N = 3 NT
-              const uint64_t bd = smem_desc_sw128(st + kTcABytes + (size_t)sh * 3 * NT * kTcBK * 2);
-              tc_mma(dacc + (uint32_t)(sh * L::kN), ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc,
+            if constexpr (NT == 8) {
+              // 3 NT = 24 is no valid N for M = 128: the six planes (48 consecutive rows) go through
+              // ONE MMA with N = 48, whose columns sh * 3 NT + term * NT + token are the layout the
+              // two per-share MMAs of wider tiles produce
+              const uint64_t bd = smem_desc_sw128(st + kTcABytes);
+              tc_mma(dacc, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc_bf16_f32(6 * NT),
                      (kb > 0 || k > 0) ? 1u : 0u);
+            } else {
+#pragma unroll
+              for (int sh = 0; sh < 2; ++sh) {
+                // the share's three term planes are 3 NT consecutive rows: one MMA with N = 3 NT
+                const uint64_t bd = smem_desc_sw128(st + kTcABytes + (size_t)sh * 3 * NT * kTcBK * 2);
+                tc_mma(dacc + (uint32_t)(sh * L::kN), ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc,
+                       (kb > 0 || k > 0) ? 1u : 0u);
+              }
             }
           }
           tc_commit(&empty[s]);  // the stage is free once these MMAs have read it
@@ -700,7 +709,7 @@ int ensure_planes(shd_ctx* ctx, size_t elems) {
 template <int NT>
 int launch_tc_t(shd_ctx* ctx, const TcArgs& ta, const CUtensorMap& mw, const CUtensorMap& mx) {
   static unsigned attr_devices = 0;
-  const int S = std::min(8, (kTcSmemLimit - 1024 - 256) / TcSmem<NT>::kStage);
+  const int S = std::min(10, (kTcSmemLimit - 1024 - 256) / TcSmem<NT>::kStage);  // barriers: 256-byte tail
   if (S < 2) return shd_fail(ctx, SHD_ERR_UNSUPPORTED, "tensor-core linear: token tile too wide");
   const size_t smem = 1024 + (size_t)S * TcSmem<NT>::kStage + 256;
   if (!(attr_devices & (1u << (ctx->device & 31)))) {
@@ -734,7 +743,7 @@ int ensure_ws(shd_ctx* ctx, size_t floats) {
 
 }  // namespace
 
-int tc_token_tile(int M) { return M <= 16 ? 16 : 32; }
+int tc_token_tile(int M) { return M <= 8 ? 8 : (M <= 16 ? 16 : 32); }
 
 int launch_linear_tc(shd_ctx* ctx, const shd_weight* w, int M, int epi, GemvArgs g, const NormArgs* norm) {
   if (w->kind != WK_BF16) return shd_fail(ctx, SHD_ERR_ARG, "tensor-core linear: need a bf16 weight");
@@ -803,6 +812,7 @@ int launch_linear_tc(shd_ctx* ctx, const shd_weight* w, int M, int epi, GemvArgs
     ta.ws = ctx->d_tc_ws;
   }
   const CUtensorMap& mw = *static_cast<const CUtensorMap*>(w->tmap);
+  if (nt == 8) return launch_tc_t<8>(ctx, ta, mw, mx);
   if (nt == 16) return launch_tc_t<16>(ctx, ta, mw, mx);
   return launch_tc_t<32>(ctx, ta, mw, mx);
 }

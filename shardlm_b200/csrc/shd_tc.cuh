@@ -15,7 +15,7 @@ inline bool tc_preferred(const shd_weight* w, int M) {
   return M >= 3 && (long long)w->N * w->K >= 48ll * 1024 * 1024;
 }
 
-// Token rows per output tile for M rows (16 or 32).
+// Token rows per output tile for M rows (8, 16 or 32).
 int tc_token_tile(int M);
 // Y shares of M rows through the tensor cores with the epilogue `epi` (EPI_STORE, EPI_QKV,
 // EPI_GATEUP or EPI_LOGITS; same GemvArgs fields as launch_gemv_f32 with staged activations

@@ -48,10 +48,12 @@ def _check(orc, w_u16, xc, xs, b, yc, ys, residual=None):
     (3584, 512, 1, True),      # 7B k/v shape
     (1000, 77, 3, True),       # ragged N and K (K % 4 == 0, not a multiple of 256)
     (8960, 1536, 2, False),    # 1.5B down projection, split-K across CTAs
-    (520, 4100, 5, False),     # M=5 -> launches of 4 + 1
-    (3584, 3584, 8, True),     # M=8
     (4, 2, 1, True),           # tiny
-    # M > 8: tcgen05 tensor-core path (three bf16 terms per f32 share, f32 accumulation in TMEM)
+    # 5 rows and more: tcgen05 tensor-core path (three bf16 terms per f32 share, f32 accumulation
+    # in TMEM); up to 8 rows an 8-row token tile, whose one MMA covers both shares
+    (520, 4100, 5, False),     # 5 rows, ragged K
+    (3584, 3584, 8, True),     # 8 rows, 7B o shape
+    (18944, 3584, 6, False),   # 6 rows, 7B down shape: split K and the reduce kernel
     (3584, 4608, 64, True),    # 7B q/k/v shape, one 64-row token tile
     (1000, 77, 9, True),       # ragged N and K, 16-row token tile
     (18944, 3584, 33, False),  # 7B down shape
