@@ -32,22 +32,22 @@ constexpr int kAttnTile = 32;     // positions per tile
 constexpr int kAttnThreads = 256;
 constexpr int kAttnGroup = 4;     // query heads per group (kAttnGroupMax bounds the scratch)
 
-template <int HD>
+template <int HD, int GS>
 struct AttnSmem {
   static constexpr int KS = HD + 4;  // padded row stride (conflict-free column reads)
   float k[2][kAttnTile][KS];         // double-buffered: the next tile loads during this one
   float v[2][kAttnTile][HD];
-  float q[kAttnGroup][HD];
-  float spart[kAttnThreads / 32][kAttnGroup][kAttnTile];  // per-warp partial dots
-  float p[kAttnGroup][kAttnTile];                         // tile weights
-  float m[kAttnGroup], l[kAttnGroup], alpha[kAttnGroup];
-  float gather[kAttnCluster][kAttnGroup][HD + 2];         // CTA 0: partials of the cluster
+  float q[GS][HD];
+  float spart[kAttnThreads / 32][GS][kAttnTile];  // per-warp partial dots
+  float p[GS][kAttnTile];                         // tile weights
+  float m[GS], l[GS], alpha[GS];
+  float gather[kAttnCluster][GS][HD + 2];         // CTA 0: partials of the cluster
 };
 
-template <int HD>
+template <int HD, int GS>
 __global__ void __launch_bounds__(kAttnThreads) attn_cluster_kernel(const AttnArgs a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
-  AttnSmem<HD>& S = *reinterpret_cast<AttnSmem<HD>*>(smem_raw);
+  AttnSmem<HD, GS>& S = *reinterpret_cast<AttnSmem<HD, GS>*>(smem_raw);
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
   const int gi = blockIdx.y, m = blockIdx.z;
@@ -99,27 +99,32 @@ __global__ void __launch_bounds__(kAttnThreads) attn_cluster_kernel(const AttnAr
     stage_tile(0, t0);  // in flight while the queries load
   }
 
-  for (int i = tid; i < kAttnGroup * HD; i += kAttnThreads) {
+  for (int i = tid; i < GS * HD; i += kAttnThreads) {
     const int g = i / HD, d = i % HD;
     S.q[g][d] = (g < G) ? a.Q[(size_t)m * a.ldq + (size_t)(qh0 + g) * HD + d] : 0.0f;
   }
-  if (tid < kAttnGroup) {
+  if (tid < GS) {
     S.m[tid] = -INFINITY;
     S.l[tid] = 0.0f;
   }
   // PV mapping: thread -> dim d, heads g0 and g0 + 2 (kAttnThreads = 2 * HD for HD = 128)
-  constexpr int GPT = kAttnGroup * HD / kAttnThreads;  // heads per thread: 2 (HD 128) or 1 (HD 64)
+  constexpr int GPT = GS * HD / kAttnThreads;  // heads per thread: 2 (HD 128) or 1 (HD 64)
   float acc[GPT];
 #pragma unroll
   for (int j = 0; j < GPT; ++j) acc[j] = 0.0f;
   const int pd = tid % HD, pg0 = tid / HD;  // head of acc[j] = pg0 + j * (kAttnThreads / HD)
   __syncthreads();
 
-  float qreg[kAttnGroup][DW];  // this warp's slice of the queries
+  // this warp's slice of the queries: in registers for groups of up to 4 heads, read from shared
+  // memory (the same float4 for every lane) for wider groups
+  constexpr bool kQReg = GS <= 4;
+  float qreg[kQReg ? GS : 1][kQReg ? DW : 1];
+  if constexpr (kQReg) {
 #pragma unroll
-  for (int g = 0; g < kAttnGroup; ++g)
+    for (int g = 0; g < GS; ++g)
 #pragma unroll
-    for (int j = 0; j < DW; ++j) qreg[g][j] = S.q[g][warp * DW + j];
+      for (int j = 0; j < DW; ++j) qreg[g][j] = S.q[g][warp * DW + j];
+  }
 
   int buf = 0;
   for (int tb = t0; tb < t1; tb += kAttnTile, buf ^= 1) {
@@ -133,22 +138,27 @@ __global__ void __launch_bounds__(kAttnThreads) attn_cluster_kernel(const AttnAr
     __syncthreads();
     // partial dots: warp = dim slice, lane = position
     {
-      float part[kAttnGroup];
+      float part[GS];
 #pragma unroll
-      for (int g = 0; g < kAttnGroup; ++g) part[g] = 0.0f;
+      for (int g = 0; g < GS; ++g) part[g] = 0.0f;
 #pragma unroll
       for (int j = 0; j < DW; j += 4) {
         const float4 kk = *reinterpret_cast<const float4*>(&S.k[buf][lane][warp * DW + j]);
 #pragma unroll
-        for (int g = 0; g < kAttnGroup; ++g) {
-          part[g] = __fmaf_rn(qreg[g][j + 0], kk.x, part[g]);
-          part[g] = __fmaf_rn(qreg[g][j + 1], kk.y, part[g]);
-          part[g] = __fmaf_rn(qreg[g][j + 2], kk.z, part[g]);
-          part[g] = __fmaf_rn(qreg[g][j + 3], kk.w, part[g]);
+        for (int g = 0; g < GS; ++g) {
+          float4 qq;
+          if constexpr (kQReg)
+            qq = make_float4(qreg[g][j + 0], qreg[g][j + 1], qreg[g][j + 2], qreg[g][j + 3]);
+          else
+            qq = *reinterpret_cast<const float4*>(&S.q[g][warp * DW + j]);
+          part[g] = __fmaf_rn(qq.x, kk.x, part[g]);
+          part[g] = __fmaf_rn(qq.y, kk.y, part[g]);
+          part[g] = __fmaf_rn(qq.z, kk.z, part[g]);
+          part[g] = __fmaf_rn(qq.w, kk.w, part[g]);
         }
       }
 #pragma unroll
-      for (int g = 0; g < kAttnGroup; ++g) S.spart[warp][g][lane] = part[g];
+      for (int g = 0; g < GS; ++g) S.spart[warp][g][lane] = part[g];
     }
     __syncthreads();
     // scores and online softmax: warp g (< G) owns head g, lane = position
@@ -193,7 +203,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_cluster_kernel(const AttnAr
   }
 
   // gather the cluster's partials into CTA 0 (distributed shared memory), then combine in rank order
-  AttnSmem<HD>* root = cluster.map_shared_rank(&S, 0);
+  AttnSmem<HD, GS>* root = cluster.map_shared_rank(&S, 0);
 #pragma unroll
   for (int j = 0; j < GPT; ++j) {
     const int g = pg0 + j * (kAttnThreads / HD);
@@ -238,12 +248,12 @@ __global__ void __launch_bounds__(kAttnThreads) attn_cluster_kernel(const AttnAr
   }
 }
 
-template <int HD>
+template <int HD, int GS>
 static int launch_attn_t(shd_ctx* ctx, const AttnArgs& a, int M) {
   static unsigned attr_devices = 0;
-  const size_t smem = sizeof(AttnSmem<HD>);
+  const size_t smem = sizeof(AttnSmem<HD, GS>);
   if (!(attr_devices & (1u << (ctx->device & 31)))) {
-    SHD_CHECK_CUDA(ctx, cudaFuncSetAttribute(attn_cluster_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    SHD_CHECK_CUDA(ctx, cudaFuncSetAttribute(attn_cluster_kernel<HD, GS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attr_devices |= 1u << (ctx->device & 31);
   }
   cudaLaunchConfig_t cfg = {};
@@ -260,26 +270,31 @@ static int launch_attn_t(shd_ctx* ctx, const AttnArgs& a, int M) {
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  SHD_CHECK_CUDA(ctx, cudaLaunchKernelEx(&cfg, attn_cluster_kernel<HD>, a));
+  SHD_CHECK_CUDA(ctx, cudaLaunchKernelEx(&cfg, attn_cluster_kernel<HD, GS>, a));
   ctx->launches++;
   return SHD_OK;
 }
 
 int launch_attention(shd_ctx* ctx, const AttnArgs& a, int M) {
-  if (a.head_dim == 128) return launch_attn_t<128>(ctx, a, M);
-  if (a.head_dim == 64) return launch_attn_t<64>(ctx, a, M);
+  // group_cap 8: groups of up to 8 q heads (one per kv head for groups of 5-8), else up to 4
+  if (a.group_cap == 8) {
+    if (a.head_dim == 128) return launch_attn_t<128, 8>(ctx, a, M);
+    if (a.head_dim == 64) return launch_attn_t<64, 8>(ctx, a, M);
+  }
+  if (a.head_dim == 128) return launch_attn_t<128, kAttnGroup>(ctx, a, M);
+  if (a.head_dim == 64) return launch_attn_t<64, kAttnGroup>(ctx, a, M);
   return shd_fail(ctx, SHD_ERR_UNSUPPORTED, "attention: head_dim must be 64 or 128");
 }
 
-// Consecutive local q heads with the same kv head, cut into near-equal groups of <= 4.
-std::vector<int4> attn_groups(int q_begin, int q_count, int kv_begin, int group) {
+// Consecutive local q heads with the same kv head, cut into near-equal groups of <= cap.
+std::vector<int4> attn_groups(int q_begin, int q_count, int kv_begin, int group, int cap) {
   std::vector<int4> out;
   int i = 0;
   while (i < q_count) {
     const int kv = (q_begin + i) / group;
     int n = 0;
     while (i + n < q_count && (q_begin + i + n) / group == kv) ++n;
-    const int parts = (n + kAttnGroup - 1) / kAttnGroup;
+    const int parts = (n + cap - 1) / cap;
     int done = 0;
     for (int p = 0; p < parts; ++p) {
       const int cnt = (n - done) / (parts - p);
@@ -314,7 +329,9 @@ extern "C" int shd_attn_decode(shd_ctx* ctx, const float* q, const float* k_cach
   for (int i = 0; i < M; ++i)
     SHD_REQUIRE(ctx, pos_host[i] >= 0 && pos_host[i] < kv_capacity, "shd_attn_decode: position outside the cache");
   SHD_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
-  const std::vector<int4> groups = attn_groups(0, H, 0, H / Hkv);
+  // from 4 rows, one group of up to 8 q heads per kv head (each K/V row read once), as the model does
+  const int cap = (M >= 4 && H / Hkv > kAttnGroup) ? 8 : kAttnGroup;
+  const std::vector<int4> groups = attn_groups(0, H, 0, H / Hkv, cap);
   const int ng = (int)groups.size();
   // per-call staging of groups and positions
   int* d_meta = nullptr;
@@ -344,6 +361,7 @@ extern "C" int shd_attn_decode(shd_ctx* ctx, const float* q, const float* k_cach
   a.Os = out_s;
   a.ldo = H * head_dim;
   a.nsplit = kAttnCluster;
+  a.group_cap = cap;
   a.err = ctx->d_err;
   int rc = launch_attention(ctx, a, M);
   cudaFreeAsync(d_meta, ctx->stream);

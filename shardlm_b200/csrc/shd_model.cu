@@ -33,7 +33,8 @@ int shd_attn_splits(int num_sms, int n_groups, int M, int max_len);
 namespace {
 
 constexpr int kMaxRows = 8;        // decode batch (sequence slots stepped together)
-constexpr int kPrefillRows = 128;  // prompt positions per prefill chunk (tensor-core linears)
+constexpr int kPrefillRows = 128;
+constexpr int kAttnWideRows = 4;   // from this many rows, attention groups of up to 8 q heads  // prompt positions per prefill chunk (tensor-core linears)
 
 // Decode bookkeeping after the logits: tokens = keys, history row, position advance. It does not
 // release its dependents early: the next step's kernels all start after it has completed, so the
@@ -210,6 +211,16 @@ extern "C" int shd_model_create(shd_ctx* ctx, const shd_model_config* cfg, shd_m
   if (e == cudaSuccess) {
     m->owned.push_back(m->attn_groups_dev);
     e = cudaMemcpy(m->attn_groups_dev, groups.data(), groups.size() * sizeof(int4), cudaMemcpyHostToDevice);
+  }
+  if (e == cudaSuccess && group > 4) {
+    // batched launches: one group of up to 8 q heads per kv head, so every K/V row is read once
+    const std::vector<int4> g8 = attn_groups(m->sh.q_head_begin, m->sh.q_head_count, m->sh.kv_head_begin, group, 8);
+    m->n_groups8 = (int)g8.size();
+    e = cudaMalloc(&m->attn_groups8_dev, g8.size() * sizeof(int4) + 16);
+    if (e == cudaSuccess) {
+      m->owned.push_back(m->attn_groups8_dev);
+      e = cudaMemcpy(m->attn_groups8_dev, g8.data(), g8.size() * sizeof(int4), cudaMemcpyHostToDevice);
+    }
   }
   if (e == cudaSuccess) e = cudaMemset(m->step, 0, 8);
   if (e == cudaSuccess) e = cudaMemset(m->kcache, 0, kv_elems * 4);
@@ -544,6 +555,11 @@ int shd_model::enqueue_layers(int M, const int* d_pos, const int* d_seq, int var
     at.counters = ctx->d_counters + (ctx->n_counters - 8192);
     at.err = ctx->d_err;
     at.early_kv = decode ? 1 : 0;
+    if (!rec && M >= kAttnWideRows && attn_groups8_dev) {
+      at.groups = attn_groups8_dev;
+      at.n_groups = n_groups8;
+      at.group_cap = 8;
+    }
     if ((rc = prof_mark(5, nullptr, true))) return rc;
     if ((rc = op_attn(at, M))) return rc;
     if ((rc = prof_mark(5, nullptr, false))) return rc;

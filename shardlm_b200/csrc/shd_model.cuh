@@ -37,7 +37,9 @@ struct shd_model {
   float *kcache = nullptr, *vcache = nullptr;  // [L][slots][T][kvd]
   int *tokens = nullptr, *pos = nullptr, *seq = nullptr;
   int *p_tokens = nullptr, *p_pos = nullptr, *p_seq = nullptr;
-  int4* attn_groups_dev = nullptr;  // attention head groups (kv head, first q head, count)
+  int4* attn_groups_dev = nullptr;  // attention head groups (kv head, first q head, count), <= 4 q heads
+  int4* attn_groups8_dev = nullptr; // the same with up to 8 q heads (null when no kv head has more than 4)
+  int n_groups8 = 0;
   int n_groups = 0;
   unsigned long long* amax = nullptr;
   unsigned long long* step = nullptr;
