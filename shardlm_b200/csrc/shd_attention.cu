@@ -189,14 +189,42 @@ __global__ void __launch_bounds__(kAttnThreads) attn_cluster_kernel(const AttnAr
       }
     }
     __syncthreads();
-    // weighted V: thread -> (head, dim)
+    // weighted V: thread -> (dim, its heads). Wide groups: each V element is loaded once for all of
+    // the thread's heads and the weights 4 positions at a time (rows past the tile's end have p = 0
+    // and V = 0); measured faster at 8-head groups, slower at 4 (single-row decode), which keeps
+    // the per-head loop.
+    if constexpr (GS <= 4) {
 #pragma unroll
-    for (int j = 0; j < GPT; ++j) {
-      const int g = pg0 + j * (kAttnThreads / HD);
-      if (g < G) {
-        float v = __fmul_rn(acc[j], S.alpha[g]);
-        for (int r = 0; r < nt; ++r) v = __fmaf_rn(S.p[g][r], S.v[buf][r][pd], v);
-        acc[j] = v;
+      for (int j = 0; j < GPT; ++j) {
+        const int g = pg0 + j * (kAttnThreads / HD);
+        if (g < G) {
+          float v = __fmul_rn(acc[j], S.alpha[g]);
+          for (int r = 0; r < nt; ++r) v = __fmaf_rn(S.p[g][r], S.v[buf][r][pd], v);
+          acc[j] = v;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < GPT; ++j) {
+        const int g = pg0 + j * (kAttnThreads / HD);
+        if (g < G) acc[j] = __fmul_rn(acc[j], S.alpha[g]);
+      }
+      for (int r = 0; r < nt; r += 4) {
+        const float v0 = S.v[buf][r][pd], v1 = S.v[buf][r + 1][pd];
+        const float v2 = S.v[buf][r + 2][pd], v3 = S.v[buf][r + 3][pd];
+#pragma unroll
+        for (int j = 0; j < GPT; ++j) {
+          const int g = pg0 + j * (kAttnThreads / HD);
+          if (g < G) {
+            const float4 pp = *reinterpret_cast<const float4*>(&S.p[g][r]);
+            float v = acc[j];
+            v = __fmaf_rn(pp.x, v0, v);
+            v = __fmaf_rn(pp.y, v1, v);
+            v = __fmaf_rn(pp.z, v2, v);
+            v = __fmaf_rn(pp.w, v3, v);
+            acc[j] = v;
+          }
+        }
       }
     }
     __syncthreads();  // this buffer is refilled two tiles later

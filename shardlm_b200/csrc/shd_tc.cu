@@ -799,13 +799,23 @@ int launch_linear_tc(shd_ctx* ctx, const shd_weight* w, int M, int epi, GemvArgs
   ta.n_tok = n_tok;
   ta.n_row = (w->nT + 3) / 4;
   ta.n_kb = w->nKC * (kChunkBf16 / kTcBK);
-  // split K when the output tiles cannot fill the SMs: the largest divisor of the K blocks that
-  // keeps at least 8 blocks per split and about one work item per SM
+  // split K to balance the SMs: work items (row tile, token tile, K range) go round-robin to one CTA
+  // per SM, so the time is about ceil(items * d / SMs) / d full-K items for d splits. Take the d
+  // (a divisor of the K blocks keeping at least 8 blocks per split) with the fewest, the smallest on
+  // ties: a whole last wave of a few items costs as much as a full one.
   ta.ksplit = 1;
   {
     const int items = ta.n_row * n_tok;
-    for (int d = 2; d <= 16; ++d)
-      if (ta.n_kb % d == 0 && ta.n_kb / d >= 8 && items * d <= ctx->num_sms + items) ta.ksplit = d;
+    const int sms = ctx->num_sms;
+    double best = (double)((items + sms - 1) / sms);
+    for (int d = 2; d <= 16; ++d) {
+      if (ta.n_kb % d != 0 || ta.n_kb / d < 8) continue;
+      const double cost = (double)((items * d + sms - 1) / sms) / d;
+      if (cost < best - 1e-9) {
+        best = cost;
+        ta.ksplit = d;
+      }
+    }
   }
   if (ta.ksplit > 1) {
     if ((rc = ensure_ws(ctx, (size_t)ta.ksplit * n_tok * nt * ta.n_row * kTcBM * 2))) return rc;
