@@ -541,7 +541,7 @@ __device__ __forceinline__ void split3(float v, uint16_t (&b)[3]) {
 // (same thread count and per-thread order as norm_reshare_kernel, so the same inverse RMS) into
 // shared memory, then writes its slice of 256-column chunks of the planes and of h = D + H. Rows
 // from M to Mp are zero.
-constexpr int kNormBatch = 4;
+constexpr int kNormBatch = 8;  // a 5120-wide row in one round of loads at 1024 threads
 
 __global__ void norm_planes_kernel(const NormArgs a, int M, int Mp, int KP, int chunks_per_slice,
                                    uint16_t* __restrict__ out) {
@@ -800,17 +800,20 @@ int launch_linear_tc(shd_ctx* ctx, const shd_weight* w, int M, int epi, GemvArgs
   ta.n_row = (w->nT + 3) / 4;
   ta.n_kb = w->nKC * (kChunkBf16 / kTcBK);
   // split K to balance the SMs: work items (row tile, token tile, K range) go round-robin to one CTA
-  // per SM, so the time is about ceil(items * d / SMs) / d full-K items for d splits. Take the d
-  // (a divisor of the K blocks keeping at least 8 blocks per split) with the fewest, the smallest on
-  // ties: a whole last wave of a few items costs as much as a full one.
+  // per SM, so d splits take about ceil(items * d / SMs) / d full-K item times, plus the reduce
+  // kernel (a launch and the partial sums through L2). Model: an item streams its weights at about
+  // 45 GB/s per SM, the reduce costs 6 us plus its partials at 2 TB/s. Take the cheapest d (a
+  // divisor of the K blocks keeping at least 8 blocks per split), the smallest on ties.
   ta.ksplit = 1;
   {
     const int items = ta.n_row * n_tok;
     const int sms = ctx->num_sms;
-    double best = (double)((items + sms - 1) / sms);
+    const double item_us = (double)kTcBM * ta.n_kb * kTcBK * 2 / 45.0e3;
+    double best = (double)((items + sms - 1) / sms) * item_us;
     for (int d = 2; d <= 16; ++d) {
       if (ta.n_kb % d != 0 || ta.n_kb / d < 8) continue;
-      const double cost = (double)((items * d + sms - 1) / sms) / d;
+      const double partial_bytes = (double)d * n_tok * nt * ta.n_row * kTcBM * 8;
+      const double cost = (double)((items * d + sms - 1) / sms) / d * item_us + 6.0 + partial_bytes / 2.0e6;
       if (cost < best - 1e-9) {
         best = cost;
         ta.ksplit = d;
