@@ -23,6 +23,11 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "secret-shared decode tok/s (Qwen2.5-7B shape)"
+
+
+def metric_for(model: str) -> str:
+    """The headline metric for the default 7B workload; other shapes name themselves."""
+    return METRIC if model == "qwen2.5-7b" else f"secret-shared decode tok/s ({model} shape)"
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per algorithmic (weight) byte of the
 # dual-share GEMV, from one ncu capture of each 7B projection at one row: q/k/v 1.0020, o 1.0026,
 # gate/up 1.0136, down 1.0290, lm_head 1.0043; weighted by their bytes per step 1.0157.
@@ -120,7 +125,7 @@ def run_reference(args, shape):
     sec = float(np.median(t))
     v = args.batch / sec
     line = {
-        "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tok/s",
+        "impl": "reference", "metric": metric_for(shape.name), "value": round(v, 4), "unit": "tok/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
@@ -337,7 +342,7 @@ def run_ours(args, shape):
         weight_bytes = shape.linear_params() * 2 / world
         value = B * args.steps / (ms * 1e-3)
         line = {
-            "metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": world,
+            "metric": metric_for(shape.name), "value": round(value, 3), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic",
