@@ -125,26 +125,28 @@ def ring(args, ctx: Context):
 
 
 def attn(args, ctx: Context):
-    """Decode attention over reconstructed caches (one query row at position kv_len - 1)."""
+    """Decode attention over reconstructed caches: --rows query rows (sequence 0), the last one at
+    position kv_len - 1 and each earlier row one position before the next."""
     sh = SHAPES[args.model]
     H, Hkv, d, L = sh.n_heads, sh.n_kv_heads, sh.head_dim, args.kv_len
+    M = args.rows
     cap = L + 16
     copies = max(1, -(-2 * L2_BYTES // (2 * cap * Hkv * d * 4)))
     ks = [torch.randn(cap, Hkv * d, device="cuda") for _ in range(copies)]
     vs = [torch.randn(cap, Hkv * d, device="cuda") for _ in range(copies)]
-    q = torch.randn(H * d, device="cuda")
-    oc, os_ = torch.empty(H * d, device="cuda"), torch.empty(H * d, device="cuda")
-    pos = np.array([L - 1], np.int32)
+    q = torch.randn(M, H * d, device="cuda")
+    oc, os_ = torch.empty(M, H * d, device="cuda"), torch.empty(M, H * d, device="cuda")
+    pos = np.array([L - M + i for i in range(M)], np.int32)
 
     def run(i):
         ctx.call("shd_attn_decode", ptr(q), ptr(ks[i % copies]), ptr(vs[i % copies]), cap, H, Hkv, d,
-                 pos.ctypes.data, 1, 0, None, ptr(oc), ptr(os_))
+                 pos.ctypes.data, M, 0, None, ptr(oc), ptr(os_))
 
     ms = _time(run, args.iters)
     ctx.sync()
-    kv_bytes = 2 * L * Hkv * d * 4
-    print(json.dumps({"attn": {"H": H, "Hkv": Hkv, "kv_len": L, "us": round(ms * 1e3, 2),
-                               "GBps": round(kv_bytes / ms / 1e6, 1)}}))
+    kv_bytes = 2 * int(pos.astype(np.int64).sum() + M) * Hkv * d * 4
+    print(json.dumps({"attn": {"H": H, "Hkv": Hkv, "rows": M, "kv_len": L, "us_per_call_incl_host": round(ms * 1e3, 2),
+                               "kv_bytes": kv_bytes}}))
 
 
 def main():
