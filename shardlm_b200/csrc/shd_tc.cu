@@ -548,12 +548,15 @@ __global__ void norm_planes_kernel(const NormArgs a, int M, int Mp, int KP, int 
   extern __shared__ float xrow[];  // [K] x = h_c + h_s of this row
   __shared__ float red[33];
   if (threadIdx.x == 0) pdl_trigger();
-  pdl_wait();  // the shares come from earlier kernels
   const int m = blockIdx.x;
   const int K = a.n;
   const size_t plane = (size_t)Mp * KP;
   const int j0 = blockIdx.y * chunks_per_slice * 256, j1 = min(KP, j0 + chunks_per_slice * 256);
   const int T = blockDim.x, tid = threadIdx.x;
+  // gamma of this thread's first column of the slice: a weight, loaded before the wait
+  float g_first = 0.0f;
+  if (j0 + tid < j1 && plane_col(j0 + tid) < K) g_first = __ldg(a.gamma + plane_col(j0 + tid));
+  pdl_wait();  // the shares come from earlier kernels
   if (m >= M) {
     for (int j = j0 + tid; j < j1; j += T)
 #pragma unroll
@@ -632,7 +635,8 @@ __global__ void norm_planes_kernel(const NormArgs a, int M, int Mp, int KP, int 
     const int col = plane_col(j);
     float vc = 0.0f, vs = 0.0f;
     if (col < K) {
-      float r = __fmul_rn(__fmul_rn(xrow[col], inv), a.gamma[col]);
+      const float gm = (j == j0 + tid) ? g_first : a.gamma[col];
+      float r = __fmul_rn(__fmul_rn(xrow[col], inv), gm);
       if (a.variant == SHD_NL_MPC && !isfinite(r)) r = 0.0f;
       const float mv = mk ? mk[col] : 0.0f;
       vc = __fsub_rn(r, mv);
@@ -758,12 +762,12 @@ int launch_linear_tc(shd_ctx* ctx, const shd_weight* w, int M, int epi, GemvArgs
   uint16_t* planes = reinterpret_cast<uint16_t*>(ctx->d_tc_planes);
   if (norm) {
     if (norm->n != w->K) return shd_fail(ctx, SHD_ERR_ARG, "tensor-core linear: norm width != in_features");
-    // one slice per 256-column chunk up to about two CTAs per SM over the rows
+    // every CTA of a row reloads the whole row for its sum: slices of one column per thread (at
+    // least one 256-column chunk), so the planes pass keeps all threads busy
     const int n_chunks = w->nKC;
-    const int want = std::max(1, (2 * ctx->num_sms) / std::max(Mp, 1));
-    const int cps = std::max(1, (n_chunks + want - 1) / want);
-    const int slices = (n_chunks + cps - 1) / cps;
     const int threads = norm->n >= 4096 ? 1024 : (norm->n >= 1024 ? 512 : 128);  // as launch_norm
+    const int cps = std::max(1, threads / 256);
+    const int slices = (n_chunks + cps - 1) / cps;
     const size_t smem = (size_t)norm->n * 4;
     static unsigned attr_devices = 0;
     if (smem > 48 * 1024 && !(attr_devices & (1u << (ctx->device & 31)))) {
