@@ -443,11 +443,14 @@ int shd_model::norm_into(GemvArgs& g, const shd_weight* w, int M, const float* H
   return op_norm(na, M);
 }
 
-int shd_model::op_gemv(const shd_weight* w, int M, int epi, const GemvArgs& g, bool norm, int kind) {
+int shd_model::op_gemv(const shd_weight* w, int M, int epi, const GemvArgs& g, bool norm, int kind,
+                       const PlaneOut* out_planes, bool* wrote_out) {
+  if (wrote_out) *wrote_out = false;
   if (!rec) {
     const bool pend = has_pend_norm;
     has_pend_norm = false;
-    if (!norm && tc_preferred(w, M)) return launch_linear_tc(ctx, w, M, epi, g, pend ? &pend_norm : nullptr);
+    if (!norm && tc_preferred(w, M))
+      return launch_linear_tc(ctx, w, M, epi, g, pend ? &pend_norm : nullptr, false, out_planes, wrote_out);
     if (pend) {
       const int rc = op_norm(pend_norm, M);
       if (rc) return rc;
@@ -581,7 +584,12 @@ int shd_model::enqueue_layers(int M, const int* d_pos, const int* d_seq, int var
     gu.variant = variant;
     gu.mask = lm ? lm + 3 * (size_t)h + sh.inter_begin : nullptr; gu.ldmask = 0;
     if ((rc = prof_mark(2, Lw.gateup, true))) return rc;
-    if ((rc = op_gemv(Lw.gateup, M, EPI_GATEUP, gu, fused, KIND_GATEUP))) return rc;
+    // gate/up with split K writes its output as the down linear's planes from the reduce kernel
+    const PlaneOut d_planes = (rec || fused) ? PlaneOut{} : tc_input_planes(ctx, Lw.down, M);
+    bool down_ready = false;
+    if ((rc = op_gemv(Lw.gateup, M, EPI_GATEUP, gu, fused, KIND_GATEUP, d_planes.p ? &d_planes : nullptr,
+                      &down_ready)))
+      return rc;
     if ((rc = prof_mark(2, Lw.gateup, false))) return rc;
     // down -> D
     GemvArgs gd{};
@@ -589,7 +597,9 @@ int shd_model::enqueue_layers(int M, const int* d_pos, const int* d_seq, int var
     gd.Yc = Dbuf; gd.Ys = Dbuf + (size_t)M * h; gd.ldy = h;
     const bool push_d = tp_push(gd, Lw.down, M, (size_t)2 * M * h);
     if ((rc = prof_mark(3, Lw.down, true))) return rc;
-    if ((rc = op_gemv(Lw.down, M, EPI_STORE, gd, false, KIND_DOWN))) return rc;
+    if ((rc = down_ready ? launch_linear_tc(ctx, Lw.down, M, EPI_STORE, gd, nullptr, true)
+                         : op_gemv(Lw.down, M, EPI_STORE, gd, false, KIND_DOWN)))
+      return rc;
     if ((rc = prof_mark(3, Lw.down, false))) return rc;
     if ((rc = push_d ? allreduce_recv(Dbuf, (size_t)2 * M * h) : allreduce_sum(Dbuf, (size_t)2 * M * h))) return rc;
     // the residual stream for the next layer is (Hc, D)

@@ -4,6 +4,7 @@
 #include <vector>
 
 #include "shd_gemv.cuh"
+#include "shd_planes.cuh"
 #include "shd_step.cuh"
 
 struct LayerW {
@@ -70,7 +71,9 @@ struct shd_model {
   bool step_usable(int M) const { return engine == 1 && ctx->tp_world <= 1 && step_plan.M == M; }
   int build_step(int M);
   // launch (or record) one operation of the layer loop
-  int op_gemv(const shd_weight* w, int M, int epi, const shd::GemvArgs& g, bool norm, int kind);
+  // out_planes / wrote_out: see launch_linear_tc (tensor-core path only)
+  int op_gemv(const shd_weight* w, int M, int epi, const shd::GemvArgs& g, bool norm, int kind,
+              const shd::PlaneOut* out_planes = nullptr, bool* wrote_out = nullptr);
   int op_attn(const shd::AttnArgs& at, int M);
   int op_norm(const shd::NormArgs& na, int M);
   int op_embed(const shd::EmbedArgs& ea, int M);

@@ -131,6 +131,7 @@ struct TcArgs {
   int ksplit;    // K ranges per output tile (> 1: partial sums to `ws`, epilogue in tc_reduce_kernel)
   int nstages;
   float* ws;     // [ksplit][n_tok * NT][n_row * 128][2] partial sums (ksplit > 1)
+  PlaneOut out;  // EPI_GATEUP in the reduce kernel: the output as the next linear's planes
 };
 
 template <int NT>
@@ -247,8 +248,12 @@ __device__ __forceinline__ void tc_epi_value(const TcArgs& ta, int n, int m, boo
     const float uv = __fadd_rn(uc, us);
     const float y = swiglu_variant(gv, uv, a.variant);
     const float mk = a.mask ? a.mask[(size_t)m * a.ldmask + i] : 0.0f;
-    a.Yc[(size_t)m * a.ldy + i] = __fsub_rn(y, mk);
-    a.Ys[(size_t)m * a.ldy + i] = mk;
+    if (ta.out.p) {
+      planes_store(ta.out, m, i, __fsub_rn(y, mk), mk);
+    } else {
+      a.Yc[(size_t)m * a.ldy + i] = __fsub_rn(y, mk);
+      a.Ys[(size_t)m * a.ldy + i] = mk;
+    }
   }
 }
 
@@ -525,17 +530,6 @@ __device__ __forceinline__ int plane_col(int j) {
   return c * 256 + (i < 4 ? 4 * l + i : 128 + 4 * l + (i - 4));
 }
 
-// Exact three-term bf16 split of v: v = b0 + b1 + b2.
-__device__ __forceinline__ void split3(float v, uint16_t (&b)[3]) {
-  const __nv_bfloat16 b0 = __float2bfloat16_rn(v);
-  const float r1 = __fsub_rn(v, __bfloat162float(b0));
-  const __nv_bfloat16 b1 = __float2bfloat16_rn(r1);
-  const float r2 = __fsub_rn(r1, __bfloat162float(b1));
-  b[0] = __bfloat16_as_ushort(b0);
-  b[1] = __bfloat16_as_ushort(b1);
-  b[2] = __bfloat16_as_ushort(__float2bfloat16_rn(r2));
-}
-
 // RMSNorm + reshare straight into the six bf16 planes (replaces the norm kernel + split_planes
 // pair before a tensor-core linear). CTA (row m, slice): every CTA of a row reduces the whole row
 // (same thread count and per-thread order as norm_reshare_kernel, so the same inverse RMS) into
@@ -749,7 +743,21 @@ int ensure_ws(shd_ctx* ctx, size_t floats) {
 
 int tc_token_tile(int M) { return M <= 8 ? 8 : (M <= 16 ? 16 : 32); }
 
-int launch_linear_tc(shd_ctx* ctx, const shd_weight* w, int M, int epi, GemvArgs g, const NormArgs* norm) {
+PlaneOut tc_input_planes(shd_ctx* ctx, const shd_weight* w, int M) {
+  PlaneOut o{};
+  if (M <= 0 || w->kind != WK_BF16 || !tc_preferred(w, M)) return o;
+  if (M % tc_token_tile(M) != 0 || w->K % kChunkBf16 != 0) return o;
+  const int KP = w->nKC * kChunkBf16;
+  if (ensure_planes(ctx, (size_t)6 * M * KP) != SHD_OK) return o;
+  o.p = reinterpret_cast<uint16_t*>(ctx->d_tc_planes);
+  o.Mp = M;
+  o.KP = KP;
+  return o;
+}
+
+int launch_linear_tc(shd_ctx* ctx, const shd_weight* w, int M, int epi, GemvArgs g, const NormArgs* norm,
+                     bool planes_ready, const PlaneOut* out_planes, bool* wrote_out) {
+  if (wrote_out) *wrote_out = false;
   if (w->kind != WK_BF16) return shd_fail(ctx, SHD_ERR_ARG, "tensor-core linear: need a bf16 weight");
   if (M <= 0) return SHD_OK;
   int rc = gemv_prepare(ctx, w, g, false);
@@ -760,7 +768,9 @@ int launch_linear_tc(shd_ctx* ctx, const shd_weight* w, int M, int epi, GemvArgs
   const int KP = w->nKC * kChunkBf16;
   if ((rc = ensure_planes(ctx, (size_t)6 * Mp * KP))) return rc;
   uint16_t* planes = reinterpret_cast<uint16_t*>(ctx->d_tc_planes);
-  if (norm) {
+  if (planes_ready) {
+    if (Mp != M || KP != w->K) return shd_fail(ctx, SHD_ERR_ARG, "tensor-core linear: planes written for another shape");
+  } else if (norm) {
     if (norm->n != w->K) return shd_fail(ctx, SHD_ERR_ARG, "tensor-core linear: norm width != in_features");
     // every CTA of a row reloads the whole row for its sum: slices of one column per thread (at
     // least one 256-column chunk), so the planes pass keeps all threads busy
@@ -827,6 +837,11 @@ int launch_linear_tc(shd_ctx* ctx, const shd_weight* w, int M, int epi, GemvArgs
   if (ta.ksplit > 1) {
     if ((rc = ensure_ws(ctx, (size_t)ta.ksplit * n_tok * nt * ta.n_row * kTcBM * 2))) return rc;
     ta.ws = ctx->d_tc_ws;
+    // the epilogue runs in the reduce kernel, after this linear has read its planes
+    if (out_planes && out_planes->p && epi == EPI_GATEUP) {
+      ta.out = *out_planes;
+      if (wrote_out) *wrote_out = true;
+    }
   }
   const CUtensorMap& mw = *static_cast<const CUtensorMap*>(w->tmap);
   if (nt == 8) return launch_tc_t<8>(ctx, ta, mw, mx);

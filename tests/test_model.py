@@ -198,6 +198,36 @@ def test_batched_decode_tensor_core_rows(ctx, orc):
     assert exact >= 3 * steps - 1
 
 
+def test_batched_decode_producers_write_planes(ctx, orc):
+    """Eight slots of a 14B-shaped layer: every projection runs on the tensor cores with 8-row
+    token tiles, and gate/up (K split in 2 by the launcher) writes the down linear's bf16 planes
+    from its reduce kernel, so the down input goes through no split kernel. Tokens checked against
+    the oracle."""
+    from shardlm_b200.model import QWEN2_5_14B, SecureModel
+
+    shape = QWEN2_5_14B.replace(n_layers=1, vocab=4096)
+    rng = np.random.default_rng(8)
+    prompts = [rng.integers(0, shape.vocab, 1 + (b % 3)).astype(np.int32) for b in range(8)]
+    steps = 3
+    m = SecureModel(ctx, shape, max_seq=16, max_batch=8, share_seed=6)
+    host = m.load_random_weights(seed=22, host_copy=True)
+    first = [m.prefill(p, slot=b) for b, p in enumerate(prompts)]
+    toks = m.decode(steps, n_active=8)
+    exact = 0
+    for b, p in enumerate(prompts):
+        om = _oracle_for(orc, shape, host, 16)
+        for i, t in enumerate(p):
+            hc, hs = orc.embed_shares(host["embed"], shape.hidden, int(t), 6, (b << 32) + i)
+            om.forward(hc, hs, variant=orc.NL_GPU, attn_variant=orc.NL_APPROX)
+        inp = first[b]
+        for i in range(steps):
+            hc, hs = orc.embed_shares(host["embed"], shape.hidden, int(inp), 6, (b << 32) + len(p) + i)
+            _, _, lc, ls = om.forward(hc, hs, variant=orc.NL_APPROX, attn_variant=orc.NL_APPROX)
+            exact += _check_token(int(toks[i, b]), lc, ls, orc)
+            inp = int(toks[i, b])
+    assert exact >= 8 * steps - 1
+
+
 def test_model_rejects_bad_requests(ctx):
     from shardlm_b200._lib import ShdError
     from shardlm_b200.model import TINY, SecureModel
