@@ -334,15 +334,10 @@ std::vector<int4> attn_groups(int q_begin, int q_count, int kv_begin, int group,
   return out;
 }
 
-size_t attn_partial_floats(int, int, int, int) { return 0; }
-
 }  // namespace shd
 
 using namespace shd;
 
-int shd::ensure_attn_scratch(shd_ctx*, size_t) { return SHD_OK; }
-
-int shd_attn_splits(int, int, int, int) { return kAttnCluster; }
 
 extern "C" int shd_attn_decode(shd_ctx* ctx, const float* q, const float* k_cache,
                                const float* v_cache, int kv_capacity, int H, int Hkv, int head_dim,
@@ -388,7 +383,6 @@ extern "C" int shd_attn_decode(shd_ctx* ctx, const float* q, const float* k_cach
   a.Oc = out_c;
   a.Os = out_s;
   a.ldo = H * head_dim;
-  a.nsplit = kAttnCluster;
   a.group_cap = cap;
   a.err = ctx->d_err;
   int rc = launch_attention(ctx, a, M);

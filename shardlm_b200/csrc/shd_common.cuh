@@ -42,8 +42,6 @@ struct shd_ctx {
   void* d_xpad = nullptr;
   size_t xpad_bytes = 0;
   // split partials of the decode attention kernel
-  float* d_attn_part = nullptr;
-  size_t attn_part_floats = 0;
   // bf16 activation planes of the tensor-core linear
   void* d_tc_planes = nullptr;
   size_t tc_planes_elems = 0;

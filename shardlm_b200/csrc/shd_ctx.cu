@@ -66,7 +66,6 @@ extern "C" int shd_destroy(shd_ctx* ctx) {
   cudaFree(ctx->d_rope_cos);
   cudaFree(ctx->d_rope_sin);
   cudaFree(ctx->d_xpad);
-  cudaFree(ctx->d_attn_part);
   cudaFree(ctx->d_tc_planes);
   cudaFree(ctx->d_tc_ws);
   delete ctx;

@@ -28,7 +28,6 @@
 
 using namespace shd;
 
-int shd_attn_splits(int num_sms, int n_groups, int M, int max_len);
 
 namespace {
 
@@ -226,12 +225,6 @@ extern "C" int shd_model_create(shd_ctx* ctx, const shd_model_config* cfg, shd_m
   if (e == cudaSuccess) e = cudaMemset(m->kcache, 0, kv_elems * 4);
   if (e == cudaSuccess) e = cudaMemset(m->vcache, 0, kv_elems * 4);
   if (e != cudaSuccess) return fail(shd_cuda_fail(ctx, e, "shd_model_create: init"));
-  // attention scratch for the largest launch (kMaxRows rows)
-  m->nsplit = shd_attn_splits(ctx->num_sms, std::max(m->n_groups, 1), c.max_batch, c.max_seq);
-  m->nsplit_prefill = shd_attn_splits(ctx->num_sms, std::max(m->n_groups, 1), kPrefillRows, c.max_seq);
-  const int ns = std::max(m->nsplit, m->nsplit_prefill);
-  rc = ensure_attn_scratch(ctx, attn_partial_floats((int)R, std::max(m->n_groups, 1), ns, d));
-  if (rc) return fail(rc);
   SHD_REQUIRE(ctx, (int)R * std::max(m->n_groups, 1) <= 8192, "shd_model_create: too many head groups x rows");
   *out = m;
   return SHD_OK;
@@ -553,9 +546,6 @@ int shd_model::enqueue_layers(int M, const int* d_pos, const int* d_seq, int var
     at.scale = 1.0f / sqrtf((float)d);
     at.mask = lm ? lm + h + (size_t)sh.q_head_begin * d : nullptr; at.ldmask = 0;
     at.Oc = Abuf; at.Os = Abuf + (size_t)M * qd; at.ldo = qd;
-    at.nsplit = (M <= cfg.max_batch) ? nsplit : nsplit_prefill;
-    at.partials = ctx->d_attn_part;
-    at.counters = ctx->d_counters + (ctx->n_counters - 8192);
     at.err = ctx->d_err;
     at.early_kv = decode ? 1 : 0;
     if (!rec && M >= kAttnWideRows && attn_groups8_dev) {

@@ -52,7 +52,6 @@ struct shd_model {
   std::vector<void*> owned;
   std::vector<int> len;
   int n_active = 0;
-  int nsplit = 1, nsplit_prefill = 1;
   cudaGraphExec_t graph = nullptr;
   int graph_rows = 0;
   int64_t graph_launches = 0, graph_launch_mark = 0;

@@ -69,23 +69,21 @@ struct AttnArgs {
   float* Oc;               // attention output shares [M][ldo]
   float* Os;
   int ldo;
-  int nsplit;
+  int nsplit;              // position splits: set by the persistent step engine for its own attention
   // Decode launches: every K/V row before pos[m] of row m's slot, and pos/seq themselves, were
   // written before the previous step ended (only row pos[m] comes from the q/k/v kernel right
   // before), so they may be read before the wait on that kernel. 0 for prefill chunks.
   int early_kv;
   int group_cap;           // 8: `groups` hold up to 8 q heads each; otherwise up to 4
-  float* partials;         // [M][n_groups][nsplit][kAttnGroupMax][head_dim + 2]
-  int* counters;           // [M][n_groups]
+  float* partials;         // step engine: [M][n_groups][nsplit][kAttnGroupMax][head_dim + 2]
+  int* counters;           // step engine: [M][n_groups]
   int* err;
 };
 
 int launch_attention(shd_ctx* ctx, const AttnArgs& a, int M);
-int ensure_attn_scratch(shd_ctx* ctx, size_t floats);
 // Groups of at most `cap` (4 or 8) consecutive local q heads sharing one kv head. Local q heads are
 // [q_begin, q_begin + q_count) of the model, local kv heads start at kv_begin; group = H / Hkv.
 std::vector<int4> attn_groups(int q_begin, int q_count, int kv_begin, int group, int cap = 4);
-size_t attn_partial_floats(int M, int n_groups, int nsplit, int head_dim);
 
 int shd_build_rope(shd_ctx* ctx, int head_dim, int max_seq, float theta);
 // RopeFrequencies::new table ([max_seq][head_dim/2] cos and sin) in new device allocations.
