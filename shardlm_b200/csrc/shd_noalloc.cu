@@ -90,7 +90,7 @@ extern "C" int shd_linear_dual_f32_noalloc(const shd_weight* w, const float* bia
   tmp.d_partials = partials;
   tmp.partial_floats = kNaPartialFloats;
   tmp.d_counters = counters;
-  tmp.n_counters = kNaMaxTiles + 8192;  // the launcher reserves the top 8192 for attention
+  tmp.n_counters = kNaMaxTiles + 8192;  // the GEMV launcher keeps the top 8192 counters out of its tiles
   tmp.d_err = err;
   for (int m0 = 0; m0 < M;) {
     const int mm = (M - m0) >= kNaMaxRowsPerLaunch ? kNaMaxRowsPerLaunch : (M - m0);
