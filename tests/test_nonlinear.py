@@ -141,13 +141,13 @@ def test_attention_decode(ctx, orc, variant, H, Hkv, kv_len):
 
 
 @pytest.mark.parametrize("M", [1, 3, 8, 9])
-@pytest.mark.parametrize("H,Hkv,d", [(28, 4, 128), (14, 2, 64), (40, 8, 128)])
+@pytest.mark.parametrize("H,Hkv,d", [(28, 4, 128), (14, 2, 64), (40, 8, 128), (4, 1, 128)])
 def test_attention_decode_rows(ctx, orc, M, H, Hkv, d):
     """Several query rows in one launch, each with its own position (0 to the cache's end): the
     8-CTA cluster of a row and head group splits the row's positions, so short rows leave CTAs
     without positions, and the combine must weigh them out. From 4 rows each kv head's query heads
-    form one group (the 8-head kernel, here with groups of 7 and of 5). A second launch
-    must repeat the first bit for bit."""
+    form one group (the 8-head kernel, here with groups of 7 and of 5); 4 query heads on 1 kv
+    head is a tensor-parallel rank's slice. A second launch must repeat the first bit for bit."""
     from shardlm_b200.runtime import ptr
 
     T = 2048
