@@ -32,10 +32,13 @@ constexpr int kMaxStages = 6;
 constexpr int kSmemPerCta2 = 115712;  // dynamic shared memory per CTA at two CTAs per SM
 constexpr int kTailBytes = 4608;    // tile result, barriers, flags, reduction scratch
 
+// Called by all 32 lanes of the producer warp: lane 0 streams the weights; after the wait on the
+// previous kernel every lane issues the activation copies of some prefetched stages (each bulk copy
+// costs its issuing thread ~0.1 us, so one thread issuing them all delayed the first blocks).
 template <int M, int CHUNK, typename XT>
 __device__ void gemv_producer(const PipeSmem& sm, const uint8_t* W, const XT* Xc, const XT* Xs,
                               int ldx, int K, int nKC, long long u0, long long u1, bool staged_x,
-                              int* err) {
+                              int* err, int lane) {
   const uint64_t pol_w = l2_policy_evict_first();
   const uint64_t pol_x = l2_policy_evict_last();
   const int S = sm.S;
@@ -58,16 +61,20 @@ __device__ void gemv_producer(const PipeSmem& sm, const uint8_t* W, const XT* Xc
     }
   };
   // phase A: weights of the first npre units (no dependency on earlier kernels)
-  for (int i = 0; i < npre; ++i) {
-    const long long u = u0 + i;
-    const uint32_t tx = (uint32_t)kBlockBytes + (staged_x ? (uint32_t)(M * 2) * xbytes_of(u) : 0u);
-    mbar_arrive_expect_tx(&sm.full[i], tx);
-    bulk_g2s(sm.stages + (size_t)i * sm.stage_bytes, W + (size_t)u * kBlockBytes, kBlockBytes, &sm.full[i], pol_w);
+  if (lane == 0) {
+    for (int i = 0; i < npre; ++i) {
+      const long long u = u0 + i;
+      const uint32_t tx = (uint32_t)kBlockBytes + (staged_x ? (uint32_t)(M * 2) * xbytes_of(u) : 0u);
+      mbar_arrive_expect_tx(&sm.full[i], tx);
+      bulk_g2s(sm.stages + (size_t)i * sm.stage_bytes, W + (size_t)u * kBlockBytes, kBlockBytes, &sm.full[i], pol_w);
+    }
   }
   if (staged_x) {
+    __syncwarp();  // every stage's expected bytes are set before any lane's copies
     pdl_wait();
-    for (int i = 0; i < npre; ++i) issue_x(i, u0 + i);
+    for (int i = lane; i < npre; i += 32) issue_x(i, u0 + i);
   }
+  if (lane != 0) return;
   // phase B: the rest, refilling stages as consumers release them
   int s = 0;
   uint32_t ph = 0;  // parity of the empty-barrier phase to wait for
@@ -142,8 +149,7 @@ __global__ void __launch_bounds__(kGemvThreads, MINB) gemv_f32_kernel(const __gr
   if (threadIdx.x == 0) pdl_trigger();
 
   if (warp == kConsumerWarps) {
-    if (lane == 0)
-      gemv_producer<M, kChunkBf16, float>(sm, a.W, a.Xc, a.Xs, a.ldx, a.K, a.nKC, u0, u1, !NORM, a.err);
+    gemv_producer<M, kChunkBf16, float>(sm, a.W, a.Xc, a.Xs, a.ldx, a.K, a.nKC, u0, u1, !NORM, a.err, lane);
     return;
   }
 
@@ -281,7 +287,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_ring_kernel(const __grid
   if (threadIdx.x == 0) pdl_trigger();
 
   if (warp == kConsumerWarps) {
-    if (lane == 0) gemv_producer<M, kChunkI32, int32_t>(sm, a.W, a.Xc, a.Xs, a.ldx, a.K, a.nKC, u0, u1, true, a.err);
+    gemv_producer<M, kChunkI32, int32_t>(sm, a.W, a.Xc, a.Xs, a.ldx, a.K, a.nKC, u0, u1, true, a.err, lane);
     return;
   }
 
