@@ -45,10 +45,8 @@ def parse():
     p.add_argument("--prompt", type=int, default=512)
     p.add_argument("--batch", type=int, default=1)
     p.add_argument("--e2e-steps", type=int, default=24)
-    p.add_argument("--cpu-sample-steps", type=int, default=2)
+    p.add_argument("--cpu-sample-steps", type=int, default=8)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--engine", type=int, default=0, choices=[0, 1],
-                   help="decode engine: 0 = one kernel per operation (default), 1 = one persistent kernel per step")
     return p.parse_args()
 
 
@@ -64,54 +62,50 @@ def peaks():
 # ------------------------------------------------------------------------------------------------
 # CPU path: the oracle (restatement of the reference's CPU share arithmetic), bounded sample
 # ------------------------------------------------------------------------------------------------
-def cpu_sample(shape, pos: int, steps: int, threads: int):
-    """Time one layer's decode step at position `pos` and the lm_head on the host cores; a token is
-    n_layers * layer + head. Returns (seconds per token, description)."""
-    from oracle import oracle as orc
+def cpu_decode(shape, prompt: int, n_tokens: int, threads: int, seed: int = 0):
+    """Greedy decode of whole tokens on the host cores through the oracle port: the reference's
+    CPU share path (crates/v2/server/src/routes/secure_inference.rs:1553-1796 order: embedding
+    shares, every layer's norm / q,k,v / RoPE / attention / o / residual / norm / gate,up / SwiGLU /
+    down / residual, final norm, lm_head, client reconstruct + greedy argmax) with every linear on
+    the CPU (SecureLinear::matmul, crates/v2/sharing/src/secure_linear.rs:103-117).
 
-    import torch
+    Weights: random-init N(0, 0.02) bf16 matrices and q/k/v biases, unit norms, in the model's
+    shape, generated on the host (same distribution as the GPU arm, not the same values; the work
+    does not depend on them). The KV rows of the prompt's positions are zero-filled rather than
+    computed by a CPU prefill, so the decode positions match the GPU arm's. Returns (seconds per
+    token for each of the n_tokens decoded, description)."""
+    from oracle import oracle as orc
 
     h, d, I, V = shape.hidden, shape.head_dim, shape.intermediate, shape.vocab
     qd, kvd = shape.n_heads * d, shape.n_kv_heads * d
-
-    def w(rows, cols, key):
-        if torch.cuda.is_available():
-            g = torch.Generator(device="cuda").manual_seed(key)
-            t = (torch.randn(cols, rows, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
-            return t.view(torch.int16).cpu().numpy().view(np.uint16)  # [in=cols][out=rows] after .T below
-        rng = np.random.default_rng(key)
-        f = (rng.standard_normal((cols, rows), dtype=np.float32) * 0.02).astype(np.float32)
-        return (f.view(np.uint32) >> 16).astype(np.uint16)
-
     orc.set_threads(threads)
-    om = orc.Model(h, 1, shape.n_heads, shape.n_kv_heads, d, I, V, shape.rope_theta, shape.rms_eps, pos + steps + 4)
-    # [in][out] layouts: wq [h][qd], wo [qd][h], wg/wu [h][I], wd [I][h]
-    layer = [w(qd, h, 1), w(kvd, h, 2), w(kvd, h, 3), w(h, qd, 4), w(I, h, 5), w(I, h, 6), w(h, I, 7)]
-    bias = [np.zeros(qd, np.float32), np.zeros(kvd, np.float32), np.zeros(kvd, np.float32)]
+    om = orc.Model(h, shape.n_layers, shape.n_heads, shape.n_kv_heads, d, I, V, shape.rope_theta,
+                   shape.rms_eps, prompt + n_tokens + 2)
     ones = np.ones(h, np.float32)
-    om.set_layer(0, *layer, *bias, ones, ones)
-    lm = w(V, h, 8)
+    f32 = lambda u16: (u16.astype(np.uint32) << 16).view(np.float32)
+    for l in range(shape.n_layers):
+        k = 16 * (l + 1)
+        # [in][out] layouts: wq [h][qd], wk/wv [h][kvd], wo [qd][h], wg/wu [h][I], wd [I][h]
+        ws = [orc.normal_bf16(s_, seed, k + i) for i, s_ in
+              enumerate([(h, qd), (h, kvd), (h, kvd), (qd, h), (h, I), (h, I), (I, h)])]
+        bs = [f32(orc.normal_bf16(n, seed, k + 8 + i)) if shape.qkv_bias else None
+              for i, n in enumerate([qd, kvd, kvd])]
+        om.set_layer(l, *ws, *bs, ones, ones)
+    embed = orc.normal_bf16((V, h), seed, 1)
+    lm = embed.T.copy() if shape.tied else orc.normal_bf16((h, V), seed, 2)
     om.set_head(lm, ones)
-    om.set_len(pos)
-    rng = np.random.default_rng(0)
-    x = rng.standard_normal(h).astype(np.float32)
-    s = rng.uniform(0, 1, h).astype(np.float32)
-    c = (x - s).astype(np.float32)
-    lc = np.empty(V, np.float32)
-    ls = np.empty(V, np.float32)
+    om.set_len(prompt)
+    tok = int(np.random.default_rng(0).integers(0, V))
     per_tok = []
-    for _ in range(steps):
+    for i in range(n_tokens):
         t0 = time.perf_counter()
-        om.forward(c, s, n_layers=1)  # one layer (logits not produced for a partial model run)
-        t1 = time.perf_counter()
-        yc, ys = orc.rmsnorm_reshare(c, s, ones, shape.rms_eps, orc.NL_APPROX)
-        orc.lib().orc_linear_bf16(lm.ctypes.data, None, h, V, yc.ctypes.data, ys.ctypes.data, lc.ctypes.data, ls.ctypes.data, 1)
-        orc.argmax_last(lc, ls)
-        t2 = time.perf_counter()
-        per_tok.append(shape.n_layers * (t1 - t0) + (t2 - t1))
-    desc = (f"oracle port (C++, {threads} threads): 1 of {shape.n_layers} layers at position {pos} "
-            f"+ lm_head/argmax per step, scaled to a token = {shape.n_layers} x layer + head; "
-            f"median of {steps}")
+        hc, hs = orc.embed_shares(embed, h, tok, 0x5EED, prompt + i)
+        _, _, lc, ls = om.forward(hc, hs, variant=orc.NL_APPROX, attn_variant=orc.NL_APPROX)
+        tok = orc.argmax_last(lc, ls)
+        per_tok.append(time.perf_counter() - t0)
+    desc = (f"oracle port (C++, {threads} threads): whole greedy decode tokens of the {shape.n_layers}-layer "
+            f"model (embedding shares, every layer, lm_head, argmax) at positions {prompt}.."
+            f"{prompt + n_tokens - 1}; prompt KV rows zero-filled")
     return per_tok, desc
 
 
@@ -120,22 +114,32 @@ def run_reference(args, shape):
     if rank != 0:
         return  # the reference arm runs on rank 0 only
     threads = os.cpu_count() or 1
-    per_tok, desc = cpu_sample(shape, args.prompt, args.warmup + args.steps, threads)
+    B = args.batch
+    per_tok, desc = cpu_decode(shape, args.prompt, args.warmup + args.steps, threads)
     t = per_tok[args.warmup:] or per_tok
-    sec = float(np.median(t))
-    v = args.batch / sec
+    sec = float(np.sum(t)) / len(t)  # one sequence decoded: a step is one token of it
+    v = 1.0 / sec
+    desc += f"; {len(t)} timed tokens after {len(per_tok) - len(t)} warm-up tokens, mean"
+    if B > 1:
+        desc += f"; one sequence of the {B}-sequence batch (the CPU path decodes sequences one by one)"
     line = {
         "impl": "reference", "metric": metric_for(shape.name), "value": round(v, 4), "unit": "tok/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"{shape.name} decode, prompt {args.prompt}, batch {args.batch}",
-                   "model": shape.name, "global_batch": args.batch, "seq_len": args.prompt,
-                   "parallelism": "cpu"},
+        "config": workload_config(args, shape, args.gpus, "cpu"),
         "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": threads, "kind": "port", "sample": desc},
         "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def workload_config(args, shape, world: int, parallelism: str) -> dict:
+    """The workload both arms name (same string, so the driver can pair them)."""
+    B = args.batch
+    return {"workload": f"{shape.name} V3 greedy decode, prompt {args.prompt}, batch {B}, "
+                        f"positions {args.prompt}..{args.prompt + args.warmup + args.steps}",
+            "model": shape.name, "global_batch": B, "seq_len": args.prompt, "parallelism": parallelism}
 
 
 # ------------------------------------------------------------------------------------------------
@@ -220,7 +224,6 @@ def run_ours(args, shape):
     prof_steps = 3
     max_seq = args.prompt + args.warmup + args.steps + prof_steps + e2e_steps + 8
     model = SecureModel(ctx, shape, max_seq=max_seq, max_batch=B, share_seed=0x5EED, tp_rank=rank, tp_world=world)
-    model.set_engine(args.engine)
     model.load_random_weights(seed=0)
     rng = np.random.default_rng(0)  # seeded uniform prompt token ids
     prompts = [rng.integers(0, shape.vocab, args.prompt).astype(np.int32) for _ in range(B)]
@@ -331,9 +334,11 @@ def run_ours(args, shape):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        per_tok, desc = cpu_sample(shape, args.prompt, args.cpu_sample_steps, threads)
-        sec = float(np.median(per_tok))
-        cpu = {"value": round(B / sec, 4), "unit": "tok/s", "cores": threads, "kind": "port", "sample": desc}
+        n, nw = args.cpu_sample_steps, 2
+        per_tok, desc = cpu_decode(shape, args.prompt, nw + n, threads)
+        sec = float(np.sum(per_tok[nw:])) / n
+        desc += f"; {n} timed tokens after {nw} warm-up tokens, mean (one sequence)"
+        cpu = {"value": round(1.0 / sec, 4), "unit": "tok/s", "cores": threads, "kind": "port", "sample": desc}
 
     if rank == 0:
         peak, src = peaks()
@@ -352,10 +357,7 @@ def run_ours(args, shape):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic",
-            "config": {"workload": f"{shape.name} V3 greedy decode, prompt {args.prompt}, batch {B}, "
-                                   f"positions {args.prompt}..{args.prompt + args.warmup + args.steps}",
-                       "model": shape.name, "global_batch": B, "seq_len": args.prompt,
-                       "parallelism": f"tp{world}",
+            "config": {**workload_config(args, shape, world, f"tp{world}"),
                        "allreduce": (("nvlink peer-memory one-shot" if lib.shd_tp_peer_path(ctx.ptr) else "nccl")
                                      if world > 1 else None),
                        "l2": "weights streamed per step (>= 1.7 GB per GPU) exceed the 126 MB L2"},

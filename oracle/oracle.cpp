@@ -266,6 +266,34 @@ ORC_API void orc_fill_uniform(uint64_t seed, uint64_t offset, float lo, float hi
   for (int64_t i = 0; i < n; ++i) out[i] = uniform_f32(philox_word(seed, 0, offset + (uint64_t)i), lo, hi);
 }
 
+// Random-init weights for the CPU timing leg (not part of the reference): N(0, std) by Box-Muller
+// over two counter words, rounded to bf16 (nearest, ties to even), on all oracle threads. Values
+// only need the benchmark's distribution; nothing compares them with the GPU's own weights.
+ORC_API void orc_fill_normal_bf16(uint64_t seed, uint64_t stream, float stdev, uint16_t* out, int64_t n) {
+  const int64_t groups = (n + 3) / 4;  // four values (two Box-Muller pairs) per counter block
+  parallel_run([&](int tid, int nth) {
+    const int64_t per = (groups + nth - 1) / nth;
+    const int64_t g0 = tid * per, g1 = g0 + per < groups ? g0 + per : groups;
+    for (int64_t g = g0; g < g1; ++g) {
+      uint32_t o[4];
+      philox((uint64_t)g, stream, seed, o);
+      float z[4];
+      for (int p = 0; p < 2; ++p) {
+        const float u1 = ((float)(o[2 * p] >> 8) + 1.0f) * 5.9604644775390625e-08f;  // (0, 1]
+        const float u2 = (float)(o[2 * p + 1] >> 8) * 5.9604644775390625e-08f;
+        const float r = sqrtf(-2.0f * logf(u1)) * stdev, t = 6.2831853071795865f * u2;
+        z[2 * p] = r * cosf(t);
+        z[2 * p + 1] = r * sinf(t);
+      }
+      for (int k = 0; k < 4 && 4 * g + k < n; ++k) {
+        uint32_t u;
+        std::memcpy(&u, &z[k], 4);
+        out[4 * g + k] = (uint16_t)((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
+      }
+    }
+  });
+}
+
 // BeaverTriple::random (beaver.rs:44-68) restated over the counter generator.
 ORC_API void orc_triples_f32(uint64_t seed, uint64_t offset, int64_t n, float* a, float* b, float* c,
                              float* ac, float* as, float* bc, float* bs, float* cc, float* cs) {

@@ -37,6 +37,7 @@ _SIGS = {
     "orc_beaver_ring": (None, [P] * 14 + [I64, I32]),
     "orc_philox_words": (None, [U64, U64, U64, P, I64]),
     "orc_fill_uniform": (None, [U64, U64, F32, F32, P, I64]),
+    "orc_fill_normal_bf16": (None, [U64, U64, F32, P, I64]),
     "orc_triples_f32": (None, [U64, U64, I64] + [P] * 9),
     "orc_triples_ring": (None, [U64, U64, I64] + [P] * 6),
     "orc_embed_shares": (None, [P, I32, I32, U64, U64, P, P]),
@@ -88,6 +89,13 @@ def set_threads(n: int) -> None:
 
 def max_threads() -> int:
     return int(lib().orc_max_threads())
+
+
+def normal_bf16(shape, seed: int, stream: int, std: float = 0.02) -> np.ndarray:
+    """N(0, std) values rounded to bf16 (uint16 bit patterns), generated on the oracle's threads."""
+    out = np.empty(shape, np.uint16)
+    lib().orc_fill_normal_bf16(seed, stream, std, _p(out), out.size)
+    return out
 
 
 def linear_f32(w_in_out, bias, xc, xs):
