@@ -72,7 +72,8 @@ int64_t shd_launch_count(shd_ctx* ctx);
  * Weights
  * -------------------------------------------------------------------------------------------- */
 
-/* Row orders of the tiled device format (see DESIGN.md "weight tiling"). */
+/* Row orders of the tiled device format: blocks of 32 output rows x 256 input columns (bf16,
+ * 16 KB), block (t, c) at offset (t * column_blocks + c) * 16 KB, zero-padded. */
 #define SHD_ROWS_PLAIN 0   /* rows in output order                                          */
 #define SHD_ROWS_QKV 1     /* fused q|k|v, RoPE pairs (i, i+head_dim/2) adjacent per head     */
 #define SHD_ROWS_GATEUP 2  /* fused gate|up, 16 gate rows then the same 16 up rows per tile   */
@@ -87,7 +88,10 @@ int shd_weight_upload_f32_as_bf16(shd_ctx* ctx, const float* w_in_out_host, int 
  * reference's loader reads, crates/v2/model/src/sharded_loader.rs:445-486). `rows` is one of
  * SHD_ROWS_*; for SHD_ROWS_QKV `out_features` = q_dim + 2*kv_dim and head_dim gives the pairing;
  * for SHD_ROWS_GATEUP `out_features` = 2*intermediate with gate rows first. bias (device,
- * nullable, out_features floats in the same row order as w) is added to the server share. */
+ * nullable, out_features floats in the same row order as w) is added to the server share.
+ * Reads the inputs in the context's stream order and returns once the tiles are written (it
+ * synchronizes that stream), so the weight may then be used from any stream.
+ * Every shd_weight_* constructor returns a complete weight in this sense. */
 int shd_weight_from_bf16(shd_ctx* ctx, const uint16_t* w_out_in_dev, const float* bias_dev,
                          int in_features, int out_features, int rows, int head_dim,
                          shd_weight** out);
@@ -95,6 +99,7 @@ int shd_weight_from_bf16(shd_ctx* ctx, const uint16_t* w_out_in_dev, const float
  * Q16.16 raw values, optional host i32 bias added (wrapping) to the server share. */
 int shd_weight_upload_i32(shd_ctx* ctx, const int32_t* w_in_out_host, const int32_t* bias_host,
                           int in_features, int out_features, shd_weight** out);
+/* Frees the weight; no call that reads it may still be running on any stream. */
 int shd_weight_destroy(shd_weight* w);
 /* Bytes the weight occupies on the device (tiled, padded). */
 int64_t shd_weight_device_bytes(const shd_weight* w);
@@ -125,9 +130,12 @@ int shd_linear_dual_f32(shd_ctx* ctx, const shd_weight* w, const float* bias, co
  * default stream), but the split-K scratch is a static device array of about 1.3 MB that every GPU
  * loading the library keeps until exit; nothing is allocated or freed. Limits: out_features <=
  * 262144, in_features % 4 == 0 and 16-byte aligned rows (SHD_ERR_ARG otherwise). The first call on
- * a device looks up the array's device address; make it before any stream capture. All calls share
- * the array (its tile counters are cleared at the start of each call): calls that overlap on the GPU
- * race. Device-side timeouts are not reported by this entry point. */
+ * a device looks up the array's device address and, with lazy module loading, may be when the
+ * array is placed in device memory: make one call per device before the host framework freezes
+ * device memory and before any stream capture. All calls share the array (its tile counters are
+ * cleared at the start of each call): calls that overlap on the GPU race. The weight and the call
+ * must not overlap its shd_weight_destroy. Device-side timeouts are not reported by this entry
+ * point. */
 int shd_linear_dual_f32_noalloc(const shd_weight* w, const float* bias, const float* xc,
                                 const float* xs, float* yc, float* ys, int M,
                                 const float* residual_c, const float* residual_s, void* stream);
@@ -138,6 +146,18 @@ int shd_linear_dual_f32_noalloc(const shd_weight* w, const float* bias, const fl
  * xc, xs: [M][in] i32; yc, ys: [M][out] i32; any M and in (rows are staged when unaligned). */
 int shd_linear_dual_ring(shd_ctx* ctx, const shd_weight* w, const int32_t* bias, const int32_t* xc,
                          const int32_t* xs, int32_t* yc, int32_t* ys, int M, int scale);
+
+/* FixedVector::from_f64_slice / Fixed::from_f64 (crates/fixed_point/src/vector.rs:22-29,
+ * fixed.rs:30-49) on n device doubles: out = round(x * 2^scale), half away from zero; NaN -> 0.
+ * Synchronous: SHD_ERR_ARG "Overflow { value } / Underflow { value } at element i" for the first
+ * element beyond i32 (the reference stops at the first error), "InvalidScale" for scale > 30. */
+int shd_fixed_from_f64(shd_ctx* ctx, const double* x, int64_t n, int scale, int32_t* out);
+/* SharePair::from_plaintext_seeded (crates/sharing/src/share.rs:116-135, Share::random_seeded
+ * :44-54; LinearClient::new_seeded, linear.rs:88-106) on n device i32 values: xs[i] = word i of
+ * ChaCha20Rng::seed_from_u64(seed) (rand_chacha 0.3.1 / rand_core 0.6.4, bit-exact), xc[i] = x[i]
+ * wrapping_sub xs[i]. Asynchronous on the context's stream. */
+int shd_ring_share_seeded(shd_ctx* ctx, const int32_t* x, int64_t n, uint64_t seed, int32_t* xc,
+                          int32_t* xs);
 
 /* ----------------------------------------------------------------------------------------------
  * Reconstruct / reshare and elementwise share ops (all device pointers, n elements)
@@ -220,16 +240,55 @@ int shd_rope_shares(shd_ctx* ctx, float* xc, float* xs, int M, int n_heads, int 
 int shd_attn_decode(shd_ctx* ctx, const float* q, const float* k_cache, const float* v_cache,
                     int kv_capacity, int H, int Hkv, int head_dim, const int32_t* pos_host, int M,
                     int variant, const float* mask, float* out_c, float* out_s);
+/* The same attention for a block of M consecutive prompt positions pos0 .. pos0 + M - 1 of one
+ * sequence (the prefill layer loop; the reference runs them one by one on the CPU), each row
+ * attending to [0, its position], on the tensor cores: Q, K and V split exactly into three bf16
+ * terms, QK^T and PV as tcgen05 MMAs with f32 accumulation, online softmax. q [M][H*128],
+ * caches [kv_capacity][Hkv*128] (rows up to pos0 + M - 1 written), mask/out [M][H*128].
+ * head_dim must be 128. */
+int shd_attn_prefill(shd_ctx* ctx, const float* q, const float* k_cache, const float* v_cache,
+                     int kv_capacity, int H, int Hkv, int head_dim, int pos0, int M, int variant,
+                     const float* mask, float* out_c, float* out_s);
 /* Server-side embedding share generation (get_embeddings_direct, crates/v2/server/src/routes/
  * secure_inference.rs:387-460): e = bf16 table row, server share uniform [0,1) (24-bit, rand's
  * Standard f32 construction) from Philox(seed, counter + m), client share e - s. */
 int shd_embed_shares(shd_ctx* ctx, const uint16_t* table, int vocab, int hidden,
                      const int32_t* tokens, int M, uint64_t seed, uint64_t counter, float* hc,
                      float* hs);
+/* get_embeddings_direct exactly as the reference draws it (secure_inference.rs:387-460): one
+ * ChaCha20Rng::from_seed(session_id16 || 16 zero bytes) per request, token t's element k takes
+ * keystream word t*hidden + k, s = (word >> 8) * 2^-24, c = e - s; tokens: n_tokens device ids
+ * (out of range -> SHD_ERR_ARG at shd_sync, as the reference's InvalidRequest); hc, hs:
+ * [n_tokens][hidden]. session_id16 is host memory (the UUID's 16 bytes). */
+int shd_embed_shares_session(shd_ctx* ctx, const uint16_t* table, int vocab, int hidden,
+                             const int32_t* tokens, int n_tokens, const uint8_t* session_id16,
+                             float* hc, float* hs);
 /* Client reconstruct + greedy sample (crates/v2/client/src/lib.rs:604-640): argmax of lc + ls,
  * the LAST index among equal maxima (Iterator::max_by). NaN -> SHD_ERR_NUMERIC at shd_sync. */
 int shd_argmax_reconstruct(shd_ctx* ctx, const float* lc, const float* ls, int V, int M,
                            int32_t* tokens);
+
+/* ----------------------------------------------------------------------------------------------
+ * V3-OT: the server's side of the OT function-table lookups
+ * -------------------------------------------------------------------------------------------- */
+
+/* StandardOtTables::new(table_size) (crates/v2/sharing/src/secure_nonlinear_ot.rs:44-72,554-575):
+ * writes [4][table_size] f32 to dev_out -- SiLU on [-8, 8], exp on [-10, 0], 1/sqrt on [0.01, 10],
+ * 1/x on [0.01, 100] -- built with the reference's f32 operations and libm calls (identical bits).
+ * Synchronous. */
+int shd_ot_standard_tables(shd_ctx* ctx, int table_size, float* dev_out);
+/* IknpOtExtension::process_query (crates/ot/src/iknp.rs:495-572) for one batch query against a
+ * device-resident table (row_bytes per row, table_bytes / row_bytes rows): per entry, the item key
+ * from SHA-256 over the session commitment (32 host bytes), the batch seed, the entry index and
+ * ctr; the index and row key decrypted with its AES-128 PRF; the row masked with the row key's PRF.
+ * One GPU thread per entry. query / response are host bytes (the route's Vec<u8>): query = u16 m ||
+ * seed[32] || m x 20 bytes; response = m x row_bytes. *response_len = m * row_bytes; a NULL or small
+ * `response` fails with SHD_ERR_ARG naming the size. SHD_ERR_ARG "InvalidMessageFormat" for a
+ * malformed query, "InvalidIndex at entry j" when entry j's index is past the table (the first
+ * such entry, as the reference stops there). Synchronous. */
+int shd_ot_process_query(shd_ctx* ctx, const uint8_t* commitment32, uint64_t ctr, const uint8_t* query,
+                         size_t query_len, const uint8_t* table_dev, size_t table_bytes, int row_bytes,
+                         uint8_t* response, size_t response_cap, size_t* response_len);
 
 /* ----------------------------------------------------------------------------------------------
  * Tensor parallelism (NCCL over NVLink, loaded at run time). Replaces the host-mediated
@@ -320,6 +379,37 @@ int shd_model_read_tokens(shd_model* m, int count, int32_t* tokens_host);
  * full vocabulary on every rank). Synchronous. */
 int shd_model_forward_host(shd_model* m, int slot, const float* hc_host, const float* hs_host,
                            float* logits_c_host, float* logits_s_host);
+/* batched_prefill_gpu_v3 (secure_inference.rs:2299-2632) as the reference's route takes it: the
+ * client's hidden-state shares of n prompt positions (host [n][h] each, get_embeddings_direct's
+ * output) instead of token ids. Optional outputs (pairs, nullable): the last position's logit
+ * shares [vocab] and its final hidden state shares [h] (the residual stream after the last layer).
+ * The KV cache stays on the device; next_token_host (nullable) = greedy token. Synchronous. */
+int shd_model_prefill_hidden(shd_model* m, int slot, const float* hc_host, const float* hs_host, int n,
+                             float* logits_c_host, float* logits_s_host, float* final_c_host,
+                             float* final_s_host, int32_t* next_token_host);
+/* The reconstructed K and V rows of positions [pos0, pos0 + n) of a slot, every layer, as the
+ * reference's prefill response carries them: host [n_layers][n][kv_dim] each (this rank's kv
+ * heads under tensor parallelism). Synchronous. */
+int shd_model_read_kv(shd_model* m, int slot, int pos0, int n, float* k_host, float* v_host);
+/* shd_model_forward_host that also returns the position's output hidden state shares [h]
+ * (BinaryDecodeResponse.hidden_*); hidden outputs nullable (as a pair). */
+int shd_model_forward_host_hidden(shd_model* m, int slot, const float* hc_host, const float* hs_host,
+                                  float* logits_c_host, float* logits_s_host, float* hidden_c_host,
+                                  float* hidden_s_host);
+/* The reference's binary wire format (crates/v2/server/src/routes/binary_protocol.rs:21-81; bincode
+ * 1.3.3 default encoding: little-endian fixed-width integers, Vec<f32> = u64 length + raw f32s,
+ * fields in declaration order). shd_bincode_prefill decodes a BinaryPrefillRequest, prefills it
+ * into `slot` and encodes the BinaryPrefillResponse (batched_prefill_gpu_v3_binary,
+ * secure_inference.rs:2635-2700); include_kv = 0 leaves k_cache and v_cache empty (the cache stays
+ * on the device for decode). shd_bincode_decode takes a BinaryDecodeRequest (position must equal
+ * the slot's length) and returns a BinaryDecodeResponse. *resp_len receives the response size;
+ * a NULL or too small `resp` fails with SHD_ERR_ARG before any work, naming the size needed.
+ * Malformed requests (truncated, trailing bytes, wrong dimensions) fail with SHD_ERR_ARG
+ * ("Invalid binary request: ..."), as the route's InvalidRequest. Single-GPU models only. */
+int shd_bincode_prefill(shd_model* m, int slot, const uint8_t* req, size_t req_len, int include_kv,
+                        uint8_t* resp, size_t resp_cap, size_t* resp_len);
+int shd_bincode_decode(shd_model* m, int slot, const uint8_t* req, size_t req_len, uint8_t* resp,
+                       size_t resp_cap, size_t* resp_len);
 /* Current length (positions held in the KV cache) of a slot. */
 int shd_model_seq_len(const shd_model* m, int slot);
 /* Kernels launched by one captured decode step (0 before the first decode). */
@@ -328,23 +418,9 @@ int64_t shd_model_step_launches(const shd_model* m);
  * and attention launch; shd_model_linear_times then returns, for the most recent step, the summed
  * device time (ms) and the summed weight bytes of the launches of each kind: [0] qkv, [1] o,
  * [2] gate/up, [3] down, [4] lm_head, [5] attention (bytes 0). Turning it on or off re-captures
- * the graph at the next decode. With the persistent step kernel (shd_model_set_engine) the times
- * are, per kind, the summed spans from the first CTA starting a job of that kind to the last one
- * finishing it (%globaltimer inside the kernel), averaged over the decode steps run since
- * profiling was turned on. */
+ * the graph at the next decode. */
 int shd_model_set_profiling(shd_model* m, int on);
 int shd_model_linear_times(shd_model* m, float* ms_out6, double* bytes_out6);
-/* Decode engine (no counterpart in the reference, whose decode is host-driven). 0 (default): one
- * kernel per operation, chained by programmatic dependent launch in a captured graph (always used
- * under tensor parallelism, for prefill and for shd_model_forward_host). 1: on a single GPU
- * (tp_world == 1) each decode step is ONE persistent kernel (one or two CTAs per SM, all resident)
- * running the embedding, every layer, the head and the token update as a job list with grid
- * barriers between jobs, its weight stream running ahead across them; same results within the f32
- * tolerance. On B200 the per-job barriers currently cost more than the overlap gains (7B decode
- * ~260 vs ~330 tok/s), hence the default. Switching re-captures the graph at the next decode. */
-int shd_model_set_engine(shd_model* m, int engine);
-/* 1 when the last decode used the persistent step kernel, else 0. */
-int shd_model_engine(const shd_model* m);
 
 #ifdef __cplusplus
 }

@@ -164,7 +164,8 @@ ORC_API int orc_fixed_from_f64(double v, int scale, int32_t* out) {
   const double scaled = v * (double)(1ull << scale);
   if (scaled > 2147483647.0) return 1;
   if (scaled < -2147483648.0) return 2;
-  *out = (int32_t)std::round(scaled);
+  // Rust's `f64 as i32` saturates and maps NaN to 0
+  *out = std::isnan(scaled) ? 0 : (int32_t)std::round(scaled);
   return 0;
 }
 
@@ -344,4 +345,125 @@ ORC_API void orc_embed_shares(const uint16_t* table, int hidden, int token, uint
     hs[k] = s;
     hc[k] = e - s;
   }
+}
+
+// ------------------------------------------------------------------------------------------------
+// ChaCha20Rng (rand_chacha 0.3.1, a dependency pinned in the reference's Cargo.lock and absent
+// here), restated from its published algorithm: the ChaCha20 block function (D. J. Bernstein,
+// "ChaCha, a variant of Salsa20", 2008; 20 rounds = 10 column + diagonal double rounds) with the
+// 32-byte seed as the key, a 64-bit block counter in words 12-13 starting at 0 and a 64-bit stream
+// id (0) in words 14-15; next_u32 returns the keystream's little-endian 32-bit words in order.
+// seed_from_u64 (rand_core 0.6.4, SeedableRng's default) expands a u64 into the 32-byte seed with
+// eight PCG32 (XSH-RR, O'Neill 2014) outputs, advancing the state before each output.
+// Used by Share::random_seeded (crates/sharing/src/share.rs:44-54) and get_embeddings_direct
+// (crates/v2/server/src/routes/secure_inference.rs:387-460).
+// ------------------------------------------------------------------------------------------------
+static inline uint32_t rotl32(uint32_t v, int c) { return (v << c) | (v >> (32 - c)); }
+
+static void chacha20_block(const uint32_t key[8], uint64_t counter, uint64_t stream, uint32_t out[16]) {
+  uint32_t x[16] = {0x61707865u, 0x3320646eu, 0x79622d32u, 0x6b206574u,
+                    key[0], key[1], key[2], key[3], key[4], key[5], key[6], key[7],
+                    (uint32_t)counter, (uint32_t)(counter >> 32), (uint32_t)stream, (uint32_t)(stream >> 32)};
+  uint32_t in[16];
+  std::memcpy(in, x, sizeof(in));
+  auto qr = [&](int a, int b, int c, int d) {
+    x[a] += x[b]; x[d] = rotl32(x[d] ^ x[a], 16);
+    x[c] += x[d]; x[b] = rotl32(x[b] ^ x[c], 12);
+    x[a] += x[b]; x[d] = rotl32(x[d] ^ x[a], 8);
+    x[c] += x[d]; x[b] = rotl32(x[b] ^ x[c], 7);
+  };
+  for (int r = 0; r < 10; ++r) {
+    qr(0, 4, 8, 12); qr(1, 5, 9, 13); qr(2, 6, 10, 14); qr(3, 7, 11, 15);
+    qr(0, 5, 10, 15); qr(1, 6, 11, 12); qr(2, 7, 8, 13); qr(3, 4, 9, 14);
+  }
+  for (int i = 0; i < 16; ++i) out[i] = x[i] + in[i];
+}
+
+static void key_words(const uint8_t seed[32], uint32_t key[8]) {
+  for (int i = 0; i < 8; ++i)
+    key[i] = (uint32_t)seed[4 * i] | ((uint32_t)seed[4 * i + 1] << 8) | ((uint32_t)seed[4 * i + 2] << 16) |
+             ((uint32_t)seed[4 * i + 3] << 24);
+}
+
+ORC_API void orc_chacha20_words(const uint8_t seed[32], uint64_t word_offset, uint32_t* out, int64_t n) {
+  uint32_t key[8], blk[16];
+  key_words(seed, key);
+  uint64_t cur = ~0ull;
+  for (int64_t i = 0; i < n; ++i) {
+    const uint64_t w = word_offset + (uint64_t)i;
+    if (w / 16 != cur) {
+      cur = w / 16;
+      chacha20_block(key, cur, 0, blk);
+    }
+    out[i] = blk[w % 16];
+  }
+}
+
+ORC_API void orc_seed_from_u64(uint64_t state, uint8_t seed[32]) {
+  const uint64_t MUL = 6364136223846793005ull, INC = 11634580027462260723ull;
+  for (int c = 0; c < 8; ++c) {
+    state = state * MUL + INC;
+    const uint32_t xorshifted = (uint32_t)(((state >> 18) ^ state) >> 27);
+    const uint32_t rot = (uint32_t)(state >> 59);
+    const uint32_t x = (xorshifted >> rot) | (xorshifted << ((32 - rot) & 31));
+    for (int b = 0; b < 4; ++b) seed[4 * c + b] = (uint8_t)(x >> (8 * b));
+  }
+}
+
+// Share::random_seeded + SharePair::from_plaintext_seeded (crates/sharing/src/share.rs:44-54,
+// 116-135): server share = next_u32() as i32 from ChaCha20Rng::seed_from_u64(seed), client share =
+// x wrapping_sub server.
+ORC_API void orc_ring_share_seeded(const int32_t* x, int64_t n, uint64_t seed, int32_t* xc, int32_t* xs) {
+  uint8_t key[32];
+  orc_seed_from_u64(seed, key);
+  std::vector<uint32_t> w((size_t)n);
+  orc_chacha20_words(key, 0, w.data(), n);
+  for (int64_t i = 0; i < n; ++i) {
+    xs[i] = (int32_t)w[i];
+    xc[i] = (int32_t)((uint32_t)x[i] - w[i]);
+  }
+}
+
+// get_embeddings_direct (crates/v2/server/src/routes/secure_inference.rs:387-460): one ChaCha20Rng
+// per request from seed = session id bytes || 16 zero bytes; for each token in order and each of
+// its `hidden` elements, s = rng.gen::<f32>() (rand 0.8.5 Standard: (next_u32 >> 8) * 2^-24) and
+// c = e - s with e the bf16 table value.
+ORC_API void orc_embed_shares_chacha(const uint16_t* table, int hidden, const int32_t* tokens, int n_tokens,
+                                     const uint8_t seed[32], float* hc, float* hs) {
+  std::vector<uint32_t> w((size_t)n_tokens * hidden);
+  orc_chacha20_words(seed, 0, w.data(), (int64_t)w.size());
+  for (int t = 0; t < n_tokens; ++t)
+    for (int k = 0; k < hidden; ++k) {
+      const size_t i = (size_t)t * hidden + k;
+      const float s = unit_f32(w[i]);
+      hs[i] = s;
+      hc[i] = bf16_to_f32(table[(size_t)tokens[t] * hidden + k]) - s;
+    }
+}
+
+// OtFunctionTable::new (crates/v2/sharing/src/secure_nonlinear_ot.rs:44-72) for the functions of
+// StandardOtTables::new (:554-575): kind 0 SiLU x * (1 / (1 + exp(-x))), 1 exp, 2 1/sqrt, 3 1/x;
+// x_i = lo + i * step with step = (hi - lo) / (size - 1), all f32 as the Rust code.
+ORC_API void orc_ot_table(int kind, float lo, float hi, int size, float* out) {
+  const float step = (hi - lo) / (float)(size - 1);
+  for (int i = 0; i < size; ++i) {
+    const float x = lo + (float)i * step;
+    float v;
+    if (kind == 0) v = x * (1.0f / (1.0f + expf(-x)));
+    else if (kind == 1) v = expf(x);
+    else if (kind == 2) v = 1.0f / sqrtf(x);
+    else v = 1.0f / x;
+    out[i] = v;
+  }
+}
+
+// OtFunctionTable::input_to_index: clamp, (x - min) / step rounded half away from zero, capped at
+// size - 1; NaN -> 0 (Rust's saturating float-to-int cast).
+ORC_API uint32_t orc_ot_input_to_index(float x, float lo, float hi, int size) {
+  const float step = (hi - lo) / (float)(size - 1);
+  if (std::isnan(x)) return 0;
+  const float c = x < lo ? lo : (x > hi ? hi : x);
+  const float r = std::round((c - lo) / step);
+  long long idx = r < 0 ? 0 : (long long)r;
+  return (uint32_t)(idx > size - 1 ? size - 1 : idx);
 }

@@ -38,6 +38,10 @@ _SIGS = {
     "orc_philox_words": (None, [U64, U64, U64, P, I64]),
     "orc_fill_uniform": (None, [U64, U64, F32, F32, P, I64]),
     "orc_fill_normal_bf16": (None, [U64, U64, F32, P, I64]),
+    "orc_chacha20_words": (None, [P, U64, P, I64]),
+    "orc_seed_from_u64": (None, [U64, P]),
+    "orc_ring_share_seeded": (None, [P, I64, U64, P, P]),
+    "orc_embed_shares_chacha": (None, [P, I32, P, I32, P, P, P]),
     "orc_triples_f32": (None, [U64, U64, I64] + [P] * 9),
     "orc_triples_ring": (None, [U64, U64, I64] + [P] * 6),
     "orc_embed_shares": (None, [P, I32, I32, U64, U64, P, P]),
@@ -54,6 +58,9 @@ _SIGS = {
     "orc_model_set_layer": (None, [P, I32] + [P] * 12),
     "orc_model_set_head": (None, [P, P, P]),
     "orc_model_reset": (None, [P]),
+    "orc_ot_table": (None, [I32, F32, F32, I32, P]),
+    "orc_ot_input_to_index": (C.c_uint32, [F32, F32, F32, I32]),
+    "orc_model_get_kv": (I32, [P, I32, I32, P, P]),
     "orc_model_set_len": (None, [P, I32]),
     "orc_model_forward": (I32, [P, P, P, I32, I32, P, I64, I32, P, P, P, P]),
 }
@@ -301,6 +308,14 @@ class Model:
     def reset(self):
         lib().orc_model_reset(self.ptr)
 
+    def get_kv(self, pos0: int, n: int):
+        """Cached reconstructed K and V rows [L][n][Hkv*d] of positions [pos0, pos0 + n)."""
+        k = np.empty((self.L, n, self.Hkv * self.d), np.float32)
+        v = np.empty_like(k)
+        if lib().orc_model_get_kv(self.ptr, pos0, n, _p(k), _p(v)) != 0:
+            raise RuntimeError("oracle model: positions beyond the cache")
+        return k, v
+
     def set_len(self, n: int):
         lib().orc_model_set_len(self.ptr, int(n))
 
@@ -323,3 +338,110 @@ class Model:
             lib().orc_model_destroy(self.ptr)
         except Exception:
             pass
+
+
+def chacha20_words(seed32: bytes, offset: int, n: int) -> np.ndarray:
+    """ChaCha20Rng::from_seed(seed32) next_u32 words [offset, offset + n)."""
+    k = np.frombuffer(bytes(seed32), np.uint8).copy()
+    assert k.size == 32
+    out = np.empty(n, np.uint32)
+    lib().orc_chacha20_words(_p(k), offset, _p(out), n)
+    return out
+
+
+def seed_from_u64(seed: int) -> bytes:
+    """rand_core 0.6 SeedableRng::seed_from_u64 expansion (PCG32) to a 32-byte seed."""
+    out = np.empty(32, np.uint8)
+    lib().orc_seed_from_u64(seed, _p(out))
+    return out.tobytes()
+
+
+def ring_share_seeded(x_i32, seed: int):
+    """SharePair::from_plaintext_seeded: (client, server) i32 shares."""
+    x = _c(x_i32, np.int32).reshape(-1)
+    xc, xs = np.empty_like(x), np.empty_like(x)
+    lib().orc_ring_share_seeded(_p(x), x.size, seed, _p(xc), _p(xs))
+    return xc, xs
+
+
+def embed_shares_chacha(table_u16, hidden, tokens, seed32: bytes):
+    """get_embeddings_direct: [n][hidden] client and server shares of one request."""
+    t = _c(table_u16, np.uint16)
+    tok = _c(tokens, np.int32).reshape(-1)
+    k = np.frombuffer(bytes(seed32), np.uint8).copy()
+    hc = np.empty((tok.size, hidden), np.float32)
+    hs = np.empty((tok.size, hidden), np.float32)
+    lib().orc_embed_shares_chacha(_p(t), hidden, _p(tok), tok.size, _p(k), _p(hc), _p(hs))
+    return hc, hs
+
+
+OT_TABLE_RANGES = ((-8.0, 8.0), (-10.0, 0.0), (0.01, 10.0), (0.01, 100.0))  # silu, exp, rsqrt, reciprocal
+
+
+def ot_standard_tables(size: int = 4096) -> np.ndarray:
+    """StandardOtTables::new(size) values, [4][size] f32 (silu, exp, rsqrt, reciprocal)."""
+    out = np.empty((4, size), np.float32)
+    for k, (lo, hi) in enumerate(OT_TABLE_RANGES):
+        lib().orc_ot_table(k, lo, hi, size, _p(out[k]))
+    return out
+
+
+def ot_input_to_index(x: float, kind: int, size: int = 4096) -> int:
+    lo, hi = OT_TABLE_RANGES[kind]
+    return int(lib().orc_ot_input_to_index(float(x), lo, hi, size))
+
+
+# IknpOtExtension's commitment-based query protocol (crates/ot/src/iknp.rs:414-620), restated in
+# Python over hashlib's SHA-256 and the `cryptography` package's AES-128: the client's
+# generate_query / decode_response and the server's process_query, for checking the device's
+# process_query on small batches.
+def _ot_prf(key: bytes, ctr: int, n: int) -> bytes:
+    from cryptography.hazmat.primitives.ciphers import Cipher, algorithms, modes
+
+    enc = Cipher(algorithms.AES(key), modes.ECB()).encryptor()
+    blocks = b"".join(ctr.to_bytes(8, "little") + i.to_bytes(8, "little") for i in range((n + 15) // 16))
+    return (enc.update(blocks) + enc.finalize())[:n]
+
+
+def _ot_item_key(commitment: bytes, batch_seed: bytes, j: int, ctr: int) -> bytes:
+    import hashlib
+
+    h = hashlib.sha256(b"IKNP-Item-Key-v2" + commitment + batch_seed + j.to_bytes(4, "little") + ctr.to_bytes(8, "little"))
+    return h.digest()[:16]
+
+
+def ot_generate_query(commitment: bytes, ctr: int, indices, batch_seed: bytes, row_keys):
+    """The client's query for `indices` with the given batch seed and per-item row keys."""
+    q = len(indices).to_bytes(2, "little") + batch_seed
+    for j, idx in enumerate(indices):
+        k = _ot_item_key(commitment, batch_seed, j, ctr)
+        idx_enc = int(idx) ^ int.from_bytes(_ot_prf(k, 0, 4), "little")
+        rk = bytes(a ^ b for a, b in zip(row_keys[j], _ot_prf(k, 1, 16)))
+        q += idx_enc.to_bytes(4, "little") + rk
+    return q
+
+
+def ot_process_query(commitment: bytes, ctr: int, query: bytes, table: bytes, row_bytes: int) -> bytes:
+    m = int.from_bytes(query[:2], "little")
+    seed = query[2:34]
+    assert len(query) == 34 + 20 * m
+    rows = len(table) // row_bytes
+    out = b""
+    for j in range(m):
+        e = query[34 + 20 * j: 54 + 20 * j]
+        k = _ot_item_key(commitment, seed, j, ctr)
+        idx = int.from_bytes(e[:4], "little") ^ int.from_bytes(_ot_prf(k, 0, 4), "little")
+        if idx >= rows:
+            raise ValueError(f"InvalidIndex {{ index: {idx}, max: {rows} }}")
+        rk = bytes(a ^ b for a, b in zip(e[4:], _ot_prf(k, 1, 16)))
+        mask = _ot_prf(rk, ctr * 1000 + j, row_bytes)
+        out += bytes(a ^ b for a, b in zip(table[idx * row_bytes:(idx + 1) * row_bytes], mask))
+    return out
+
+
+def ot_decode_response(response: bytes, ctr: int, row_keys, row_bytes: int) -> bytes:
+    out = b""
+    for j, rk in enumerate(row_keys):
+        mask = _ot_prf(rk, ctr * 1000 + j, row_bytes)
+        out += bytes(a ^ b for a, b in zip(response[j * row_bytes:(j + 1) * row_bytes], mask))
+    return out

@@ -297,6 +297,18 @@ ORC_API void orc_model_set_len(void* p, int len) {
   m->len = len;
 }
 
+// The cached (reconstructed) K and V rows [L][n][Hkv*d] of positions [pos0, pos0 + n).
+ORC_API int orc_model_get_kv(void* p, int pos0, int n, float* k_out, float* v_out) {
+  OrcModel* m = static_cast<OrcModel*>(p);
+  if (pos0 < 0 || n < 0 || pos0 + n > m->len) return -1;
+  const size_t kvd = (size_t)m->Hkv * m->d;
+  for (int l = 0; l < m->L; ++l) {
+    std::memcpy(k_out + (size_t)l * n * kvd, m->kcache[l].data() + (size_t)pos0 * kvd, (size_t)n * kvd * 4);
+    std::memcpy(v_out + (size_t)l * n * kvd, m->vcache[l].data() + (size_t)pos0 * kvd, (size_t)n * kvd * 4);
+  }
+  return 0;
+}
+
 ORC_API void orc_model_reset(void* p) {
   OrcModel* m = static_cast<OrcModel*>(p);
   for (auto& k : m->kcache) k.clear();

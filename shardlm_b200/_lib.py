@@ -70,6 +70,17 @@ SIGNATURES: dict[str, tuple] = {
     "shd_rope_shares": (I32, [P, P, P, I32, I32, I32, I32]),
     "shd_attn_decode": (I32, [P, P, P, P, I32, I32, I32, I32, P, I32, I32, P, P, P]),
     "shd_embed_shares": (I32, [P, P, I32, I32, P, I32, U64, U64, P, P]),
+    "shd_attn_prefill": (I32, [P, P, P, P, I32, I32, I32, I32, I32, I32, I32, P, P, P]),
+    "shd_model_prefill_hidden": (I32, [P, I32, P, P, I32, P, P, P, P, P]),
+    "shd_model_read_kv": (I32, [P, I32, I32, I32, P, P]),
+    "shd_model_forward_host_hidden": (I32, [P, I32, P, P, P, P, P, P]),
+    "shd_bincode_prefill": (I32, [P, I32, P, C.c_size_t, I32, P, C.c_size_t, P]),
+    "shd_bincode_decode": (I32, [P, I32, P, C.c_size_t, P, C.c_size_t, P]),
+    "shd_ot_standard_tables": (I32, [P, I32, P]),
+    "shd_ot_process_query": (I32, [P, P, U64, P, C.c_size_t, P, C.c_size_t, I32, P, C.c_size_t, P]),
+    "shd_embed_shares_session": (I32, [P, P, I32, I32, P, I32, P, P, P]),
+    "shd_fixed_from_f64": (I32, [P, P, I64, I32, P]),
+    "shd_ring_share_seeded": (I32, [P, P, I64, U64, P, P]),
     "shd_argmax_reconstruct": (I32, [P, P, P, I32, I32, P]),
     "shd_tp_unique_id": (I32, [P]),
     "shd_tp_init": (I32, [P, I32, I32, P]),
@@ -93,8 +104,6 @@ SIGNATURES: dict[str, tuple] = {
     "shd_model_step_launches": (I64, [P]),
     "shd_model_set_profiling": (I32, [P, I32]),
     "shd_model_linear_times": (I32, [P, P, P]),
-    "shd_model_set_engine": (I32, [P, I32]),
-    "shd_model_engine": (I32, [P]),
 }
 
 

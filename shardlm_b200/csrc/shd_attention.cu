@@ -392,3 +392,51 @@ extern "C" int shd_attn_decode(shd_ctx* ctx, const float* q, const float* k_cach
   if (e != cudaSuccess) return shd_cuda_fail(ctx, e, "shd_attn_decode");
   return rc;
 }
+
+extern "C" int shd_attn_prefill(shd_ctx* ctx, const float* q, const float* k_cache, const float* v_cache,
+                                int kv_capacity, int H, int Hkv, int head_dim, int pos0, int M, int variant,
+                                const float* mask, float* out_c, float* out_s) {
+  if (!ctx) return SHD_ERR_ARG;
+  SHD_REQUIRE(ctx, q && k_cache && v_cache && out_c && out_s, "shd_attn_prefill: null pointer");
+  SHD_REQUIRE(ctx, H > 0 && Hkv > 0 && H % Hkv == 0, "shd_attn_prefill: num_heads must be a multiple of num_kv_heads");
+  SHD_REQUIRE(ctx, head_dim == 128, "shd_attn_prefill: head_dim must be 128");
+  SHD_REQUIRE(ctx, variant >= 0 && variant <= 2, "shd_attn_prefill: unknown variant");
+  SHD_REQUIRE(ctx, M > 0 && pos0 >= 0 && pos0 + M <= kv_capacity, "shd_attn_prefill: positions outside the cache");
+  SHD_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
+  const std::vector<int4> groups = attn_groups(0, H, 0, H / Hkv, 8);
+  const int ng = (int)groups.size();
+  int* d_meta = nullptr;
+  const size_t meta_bytes = (size_t)ng * 16 + 16;
+  SHD_CHECK_CUDA(ctx, cudaMallocAsync(&d_meta, meta_bytes, ctx->stream));
+  std::vector<int> meta(meta_bytes / 4, 0);
+  std::memcpy(meta.data(), groups.data(), (size_t)ng * 16);
+  meta[4 * ng] = pos0;
+  SHD_CHECK_CUDA(ctx, cudaMemcpyAsync(d_meta, meta.data(), meta_bytes, cudaMemcpyHostToDevice, ctx->stream));
+  AttnArgs a{};
+  a.Q = q;
+  a.ldq = H * head_dim;
+  a.Kcache = k_cache;
+  a.Vcache = v_cache;
+  a.kvd = Hkv * head_dim;
+  a.kv_seq_stride = (int64_t)kv_capacity * a.kvd;
+  a.groups = reinterpret_cast<const int4*>(d_meta);
+  a.n_groups = ng;
+  a.head_dim = head_dim;
+  a.pos = d_meta + 4 * ng;
+  a.seq = nullptr;
+  a.variant = variant;
+  a.scale = 1.0f / sqrtf((float)head_dim);
+  a.mask = mask;
+  a.ldmask = H * head_dim;
+  a.Oc = out_c;
+  a.Os = out_s;
+  a.ldo = H * head_dim;
+  a.group_cap = 8;
+  a.err = ctx->d_err;
+  int rc = flash_prefill_supported(a, M) ? launch_flash_prefill(ctx, a, M)
+                                         : shd_fail(ctx, SHD_ERR_ARG, "shd_attn_prefill: rows must be 16-byte aligned");
+  cudaFreeAsync(d_meta, ctx->stream);
+  cudaError_t e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) return shd_cuda_fail(ctx, e, "shd_attn_prefill");
+  return rc;
+}

@@ -30,6 +30,7 @@ struct shd_ctx {
   size_t partial_floats = 0;
   int* d_counters = nullptr;     // per-tile arrival counters, left zero by every kernel
   int n_counters = 0;
+  unsigned long long* d_scratch64 = nullptr;  // one word for synchronous result checks (encoders)
   int num_sms = 148;
   int64_t launches = 0;
   // RoPE table (host-built with libm, as the reference's RopeFrequencies::new)

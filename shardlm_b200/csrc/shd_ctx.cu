@@ -63,6 +63,7 @@ extern "C" int shd_destroy(shd_ctx* ctx) {
   cudaFree(ctx->d_err);
   cudaFree(ctx->d_partials);
   cudaFree(ctx->d_counters);
+  cudaFree(ctx->d_scratch64);
   cudaFree(ctx->d_rope_cos);
   cudaFree(ctx->d_rope_sin);
   cudaFree(ctx->d_xpad);
@@ -258,6 +259,9 @@ extern "C" int shd_weight_from_bf16(shd_ctx* ctx, const uint16_t* w_out_in_dev, 
   e = cudaGetLastError();
   if (e != cudaSuccess) { shd_weight_destroy(w); return shd_cuda_fail(ctx, e, "tile_bf16_kernel"); }
   ctx->launches++;
+  // the tiles are complete when the call returns, so any stream may use the weight afterwards
+  e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) { shd_weight_destroy(w); return shd_cuda_fail(ctx, e, "tile_bf16_kernel"); }
   *out = w;
   return SHD_OK;
 }

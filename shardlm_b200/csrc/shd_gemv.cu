@@ -490,7 +490,7 @@ int gemv_prepare(shd_ctx* ctx, const shd_weight* w, GemvArgs& a, bool norm) {
   a.counters = ctx->d_counters;
   a.err = ctx->d_err;
   if (w->kind != WK_BF16) return shd_fail(ctx, SHD_ERR_ARG, "gemv: need a bf16 weight");
-  if (w->nT > ctx->n_counters - 8192) return shd_fail(ctx, SHD_ERR_ARG, "gemv: too many row tiles");
+  if (w->nT > ctx->n_counters) return shd_fail(ctx, SHD_ERR_ARG, "gemv: too many row tiles");
   if (norm) {
     if (w->K % 4 != 0) return shd_fail(ctx, SHD_ERR_ARG, "gemv: fused norm needs in_features % 4 == 0");
     a.K = w->K;
@@ -543,7 +543,7 @@ int launch_gemv_ring(shd_ctx* ctx, const shd_weight* w, int M, RingArgs a) {
   a.partials = reinterpret_cast<long long*>(ctx->d_partials);
   a.counters = ctx->d_counters;
   a.err = ctx->d_err;
-  if (w->nT > ctx->n_counters - 8192) return shd_fail(ctx, SHD_ERR_ARG, "gemv: too many row tiles");
+  if (w->nT > ctx->n_counters) return shd_fail(ctx, SHD_ERR_ARG, "gemv: too many row tiles");
   switch (M) {
     case 1: return launch_ring_t<1>(ctx, w, a);
     case 2: return launch_ring_t<2>(ctx, w, a);

@@ -1,8 +1,7 @@
-// Device building blocks of the dual-share GEMV, shared by the per-layer GEMV kernels
-// (shd_gemv.cu) and the persistent decode-step kernel (shd_step.cu): stream-K bookkeeping, the
+// Device building blocks of the dual-share GEMV kernels (shd_gemv.cu): stream-K bookkeeping, the
 // consumer-group barrier, the split-tile fixup, the f32 epilogues, the fused RMSNorm prologue and
 // the per-block multiply-accumulate. Activations written by other CTAs of the same grid are read
-// with L2-coherent loads (__ldcg), so a persistent grid never sees a stale L1 line.
+// with L2-coherent loads (__ldcg), so no CTA sees a stale L1 line.
 #pragma once
 
 #include <algorithm>

@@ -32,8 +32,9 @@ using namespace shd;
 namespace {
 
 constexpr int kMaxRows = 8;        // decode batch (sequence slots stepped together)
-constexpr int kPrefillRows = 128;
-constexpr int kAttnWideRows = 4;   // from this many rows, attention groups of up to 8 q heads  // prompt positions per prefill chunk (tensor-core linears)
+constexpr int kPrefillRows = 128;  // prompt positions per prefill chunk
+constexpr int kAttnWideRows = 4;   // from this many rows, attention groups of up to 8 q heads
+constexpr int kFlashRows = 16;     // prompt blocks of this many rows and more: tensor-core attention
 
 // Decode bookkeeping after the logits: tokens = keys, history row, position advance. It does not
 // release its dependents early: the next step's kernels all start after it has completed, so the
@@ -232,7 +233,6 @@ extern "C" int shd_model_create(shd_ctx* ctx, const shd_model_config* cfg, shd_m
 
 shd_model::~shd_model() {
   if (graph) cudaGraphExecDestroy(graph);
-  shd::step_plan_free(step_plan);
   for (cudaEvent_t ev : prof_events) cudaEventDestroy(ev);
   for (auto& L : layers) {
     shd_weight_destroy(L.qkv);
@@ -414,9 +414,9 @@ int shd_model::norm_into(GemvArgs& g, const shd_weight* w, int M, const float* H
                          int variant, const float* mask, bool& fused) {
   const int h = cfg.hidden;
   has_pend_norm = false;
-  // fused into the GEMV when its activations fit the CTA; the tensor-core path (per-kernel engine)
-  // computes it in its plane split
-  fused = (size_t)M * 2 * w->nKC * kChunkBf16 * 4 <= 120 * 1024 && (rec != nullptr || !tc_preferred(w, M));
+  // fused into the GEMV when its activations fit the CTA; the tensor-core path computes it in its
+  // plane split
+  fused = (size_t)M * 2 * w->nKC * kChunkBf16 * 4 <= 120 * 1024 && !tc_preferred(w, M);
   if (fused) {
     g.nHc = Hc; g.nHs = Hs; g.nDc = Dc; g.nDs = Ds; g.nHout_c = Oc; g.nHout_s = Os; g.n_ldh = h;
     g.gamma = gamma; g.eps = cfg.rms_eps; g.nvariant = variant; g.nmask = mask; g.n_ldmask = 0;
@@ -427,86 +427,27 @@ int shd_model::norm_into(GemvArgs& g, const shd_weight* w, int M, const float* H
   na.gamma = gamma; na.eps = cfg.rms_eps; na.variant = variant; na.mask = mask; na.ldmask = 0;
   na.Xc = Xbuf; na.Xs = Xbuf + (size_t)M * h; na.ldx = h; na.n = h;
   g.Xc = Xbuf; g.Xs = Xbuf + (size_t)M * h; g.ldx = h;
-  if (!rec && tc_preferred(w, M)) {
+  if (tc_preferred(w, M)) {
     // the tensor-core linear computes the norm itself while it splits the bf16 planes (op_gemv)
     pend_norm = na;
     has_pend_norm = true;
     return SHD_OK;
   }
-  return op_norm(na, M);
+  return launch_norm(ctx, na, M);
 }
 
-int shd_model::op_gemv(const shd_weight* w, int M, int epi, const GemvArgs& g, bool norm, int kind,
+int shd_model::op_gemv(const shd_weight* w, int M, int epi, const GemvArgs& g, bool norm,
                        const PlaneOut* out_planes, bool* wrote_out) {
   if (wrote_out) *wrote_out = false;
-  if (!rec) {
-    const bool pend = has_pend_norm;
-    has_pend_norm = false;
-    if (!norm && tc_preferred(w, M))
-      return launch_linear_tc(ctx, w, M, epi, g, pend ? &pend_norm : nullptr, false, out_planes, wrote_out);
-    if (pend) {
-      const int rc = op_norm(pend_norm, M);
-      if (rc) return rc;
-    }
-    return launch_gemv_f32(ctx, w, M, epi, g, norm);
+  const bool pend = has_pend_norm;
+  has_pend_norm = false;
+  if (!norm && tc_preferred(w, M))
+    return launch_linear_tc(ctx, w, M, epi, g, pend ? &pend_norm : nullptr, false, out_planes, wrote_out);
+  if (pend) {
+    const int rc = launch_norm(ctx, pend_norm, M);
+    if (rc) return rc;
   }
-  StepJob j{};
-  j.type = JOB_GEMV;
-  j.epi = epi;
-  j.norm = norm ? 1 : 0;
-  j.kind = kind;
-  j.bytes = (double)w->N * (double)w->K * 2.0;
-  j.g = g;
-  const int rc = gemv_prepare(ctx, w, j.g, norm);
-  if (rc) return rc;
-  rec->push_back(j);
-  return SHD_OK;
-}
-
-int shd_model::op_attn(const AttnArgs& at, int M) {
-  if (!rec) return launch_attention(ctx, at, M);
-  StepJob j{};
-  j.type = JOB_ATTN;
-  j.kind = KIND_ATTN;
-  j.at = at;
-  rec->push_back(j);
-  return SHD_OK;
-}
-
-int shd_model::op_norm(const NormArgs& na, int M) {
-  if (!rec) return launch_norm(ctx, na, M);
-  StepJob j{};
-  j.type = JOB_NORM;
-  j.kind = KIND_OTHER;
-  j.na = na;
-  rec->push_back(j);
-  return SHD_OK;
-}
-
-int shd_model::op_embed(const EmbedArgs& ea, int M) {
-  if (!rec) return launch_embed(ctx, ea, M);
-  StepJob j{};
-  j.type = JOB_EMBED;
-  j.kind = KIND_OTHER;
-  j.ea = ea;
-  rec->push_back(j);
-  return SHD_OK;
-}
-
-// Record the decode step of M rows as a job list and upload it for the persistent kernel.
-// SHD_ERR_UNSUPPORTED leaves the per-kernel path in use.
-int shd_model::build_step(int M) {
-  std::vector<StepJob> jobs;
-  rec = &jobs;
-  int rc = enqueue_decode_step(M);
-  rec = nullptr;
-  if (rc) return rc;
-  rc = shd::step_plan_build(ctx, step_plan, jobs, M);
-  if (rc == SHD_ERR_UNSUPPORTED) {
-    ctx->last_error.clear();
-    return SHD_OK;
-  }
-  return rc;
+  return launch_gemv_f32(ctx, w, M, epi, g, norm);
 }
 
 int shd_model::enqueue_layers(int M, const int* d_pos, const int* d_seq, int variant, int& cur, bool decode) {
@@ -535,7 +476,7 @@ int shd_model::enqueue_layers(int M, const int* d_pos, const int* d_seq, int var
     g.Kcache = kcache + (size_t)l * kv_layer; g.Vcache = vcache + (size_t)l * kv_layer;
     g.kv_seq_stride = (int64_t)c.max_seq * kvd;
     if ((rc = prof_mark(0, Lw.qkv, true))) return rc;
-    if ((rc = op_gemv(Lw.qkv, M, EPI_QKV, g, fused, KIND_QKV))) return rc;
+    if ((rc = op_gemv(Lw.qkv, M, EPI_QKV, g, fused))) return rc;
     if ((rc = prof_mark(0, Lw.qkv, false))) return rc;
     // attention -> A shares
     AttnArgs at{};
@@ -548,13 +489,17 @@ int shd_model::enqueue_layers(int M, const int* d_pos, const int* d_seq, int var
     at.Oc = Abuf; at.Os = Abuf + (size_t)M * qd; at.ldo = qd;
     at.err = ctx->d_err;
     at.early_kv = decode ? 1 : 0;
-    if (!rec && M >= kAttnWideRows && attn_groups8_dev) {
+    if (M >= kAttnWideRows && attn_groups8_dev) {
       at.groups = attn_groups8_dev;
       at.n_groups = n_groups8;
       at.group_cap = 8;
     }
     if ((rc = prof_mark(5, nullptr, true))) return rc;
-    if ((rc = op_attn(at, M))) return rc;
+    if (!decode && M >= kFlashRows && flash_prefill_supported(at, M))
+      rc = launch_flash_prefill(ctx, at, M);  // a prompt block: consecutive positions of one slot
+    else
+      rc = launch_attention(ctx, at, M);
+    if (rc) return rc;
     if ((rc = prof_mark(5, nullptr, false))) return rc;
     // o projection -> D (partial under TP)
     GemvArgs go{};
@@ -562,7 +507,7 @@ int shd_model::enqueue_layers(int M, const int* d_pos, const int* d_seq, int var
     go.Yc = Dbuf; go.Ys = Dbuf + (size_t)M * h; go.ldy = h;
     const bool push_o = tp_push(go, Lw.o, M, (size_t)2 * M * h);
     if ((rc = prof_mark(1, Lw.o, true))) return rc;
-    if ((rc = op_gemv(Lw.o, M, EPI_STORE, go, false, KIND_O))) return rc;
+    if ((rc = op_gemv(Lw.o, M, EPI_STORE, go, false))) return rc;
     if ((rc = prof_mark(1, Lw.o, false))) return rc;
     if ((rc = push_o ? allreduce_recv(Dbuf, (size_t)2 * M * h) : allreduce_sum(Dbuf, (size_t)2 * M * h))) return rc;
     // post-attention norm (h = D + Ho -> Hc) + gate/up + SwiGLU reshare -> ACT
@@ -575,9 +520,9 @@ int shd_model::enqueue_layers(int M, const int* d_pos, const int* d_seq, int var
     gu.mask = lm ? lm + 3 * (size_t)h + sh.inter_begin : nullptr; gu.ldmask = 0;
     if ((rc = prof_mark(2, Lw.gateup, true))) return rc;
     // gate/up with split K writes its output as the down linear's planes from the reduce kernel
-    const PlaneOut d_planes = (rec || fused) ? PlaneOut{} : tc_input_planes(ctx, Lw.down, M);
+    const PlaneOut d_planes = fused ? PlaneOut{} : tc_input_planes(ctx, Lw.down, M);
     bool down_ready = false;
-    if ((rc = op_gemv(Lw.gateup, M, EPI_GATEUP, gu, fused, KIND_GATEUP, d_planes.p ? &d_planes : nullptr,
+    if ((rc = op_gemv(Lw.gateup, M, EPI_GATEUP, gu, fused, d_planes.p ? &d_planes : nullptr,
                       &down_ready)))
       return rc;
     if ((rc = prof_mark(2, Lw.gateup, false))) return rc;
@@ -588,7 +533,7 @@ int shd_model::enqueue_layers(int M, const int* d_pos, const int* d_seq, int var
     const bool push_d = tp_push(gd, Lw.down, M, (size_t)2 * M * h);
     if ((rc = prof_mark(3, Lw.down, true))) return rc;
     if ((rc = down_ready ? launch_linear_tc(ctx, Lw.down, M, EPI_STORE, gd, nullptr, true)
-                         : op_gemv(Lw.down, M, EPI_STORE, gd, false, KIND_DOWN)))
+                         : op_gemv(Lw.down, M, EPI_STORE, gd, false)))
       return rc;
     if ((rc = prof_mark(3, Lw.down, false))) return rc;
     if ((rc = push_d ? allreduce_recv(Dbuf, (size_t)2 * M * h) : allreduce_sum(Dbuf, (size_t)2 * M * h))) return rc;
@@ -629,7 +574,7 @@ int shd_model::enqueue_head_rows(int M, int cur, int variant) {
   g.amax = amax;
   g.idx_offset = sh.vocab_begin;
   if ((rc = prof_mark(4, lm_head, true))) return rc;
-  if ((rc = op_gemv(lm_head, M, EPI_LOGITS, g, fused, KIND_HEAD))) return rc;
+  if ((rc = op_gemv(lm_head, M, EPI_LOGITS, g, fused))) return rc;
   return prof_mark(4, lm_head, false);
 }
 
@@ -637,6 +582,94 @@ int shd_model::check_ready() {
   SHD_REQUIRE(ctx, embed && lm_head, "model: embedding and head must be set");
   for (auto& L : layers) SHD_REQUIRE(ctx, L.qkv && L.o && L.gateup && L.down, "model: a layer has no weights");
   return SHD_OK;
+}
+
+// Prefill of n positions of `slot` in chunks of kPrefillRows, from token ids (embedding shares
+// generated on the device) or from hidden-state shares given by the caller (hc/hs host [n][h]).
+// Optional outputs of the last position: the whole logit shares, and the final hidden state
+// (the residual stream after the last layer, per share: H + D, as secure_add_gpu leaves it).
+int shd_model::prefill_impl(int slot, int n, const int32_t* tokens_host, const float* hc_host, const float* hs_host,
+                            float* logits_c_host, float* logits_s_host, float* final_c_host, float* final_s_host,
+                            int32_t* next_token_host) {
+  const int h = cfg.hidden;
+  std::vector<int> hp(3 * kPrefillRows);
+  int cur = 0, rc = SHD_OK, M_last = 0;
+  for (int p0 = 0; p0 < n && rc == SHD_OK; p0 += kPrefillRows) {
+    const int M = std::min(kPrefillRows, n - p0);
+    M_last = M;
+    // the staging vector is reused: finish the previous chunk's copies first
+    if (cudaStreamSynchronize(stream) != cudaSuccess) { rc = shd_fail(ctx, SHD_ERR_CUDA, "prefill sync"); break; }
+    for (int i = 0; i < M; ++i) {
+      hp[i] = tokens_host ? tokens_host[p0 + i] : 0;
+      hp[kPrefillRows + i] = len[slot] + p0 + i;
+      hp[2 * kPrefillRows + i] = slot;
+    }
+    cudaError_t e = cudaMemcpyAsync(p_pos, hp.data() + kPrefillRows, M * 4, cudaMemcpyHostToDevice, stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(p_seq, hp.data() + 2 * kPrefillRows, M * 4, cudaMemcpyHostToDevice, stream);
+    if (tokens_host) {
+      if (e == cudaSuccess) e = cudaMemcpyAsync(p_tokens, hp.data(), M * 4, cudaMemcpyHostToDevice, stream);
+    } else {
+      // the caller's hidden-state shares (get_embeddings_direct output) stand in for the embedding
+      if (e == cudaSuccess)
+        e = cudaMemcpyAsync(Hbuf[0], hc_host + (size_t)p0 * h, (size_t)M * h * 4, cudaMemcpyHostToDevice, stream);
+      if (e == cudaSuccess)
+        e = cudaMemcpyAsync(Hbuf[0] + (size_t)M * h, hs_host + (size_t)p0 * h, (size_t)M * h * 4,
+                            cudaMemcpyHostToDevice, stream);
+      if (e == cudaSuccess) e = cudaMemsetAsync(Dbuf, 0, (size_t)2 * M * h * 4, stream);
+      if (e == cudaSuccess) e = cudaMemsetAsync(amax, 0, 8, stream);
+    }
+    if (e != cudaSuccess) { rc = shd_cuda_fail(ctx, e, "prefill staging"); break; }
+    if (tokens_host) {
+      EmbedArgs ea{};
+      ea.table = embed; ea.vocab = cfg.vocab; ea.hidden = h; ea.tokens = p_tokens;
+      ea.pos = p_pos; ea.seed = cfg.share_seed; ea.counter_base = (uint64_t)slot << 32;
+      ea.Hc = Hbuf[0]; ea.Hs = Hbuf[0] + (size_t)M * h; ea.ldh = h;
+      ea.Dc = Dbuf; ea.Ds = Dbuf + (size_t)M * h; ea.amax = amax; ea.err = ctx->d_err;
+      if ((rc = launch_embed(ctx, ea, M))) break;
+    }
+    if ((rc = enqueue_layers(M, p_pos, p_seq, cfg.variant_prefill, cur, false))) break;
+    if (p0 + M == n) {
+      if ((rc = enqueue_head(M, M - 1, cur, cfg.variant_prefill, logits_c_host != nullptr, 0))) break;
+      if ((rc = allreduce_max_keys(1))) break;
+      if (logits_c_host && (rc = gather_logits(logits_c_host, logits_s_host))) break;
+    }
+  }
+  std::vector<float> fin;
+  if (rc == SHD_OK && final_c_host) {
+    // row M_last - 1 of (H, D), both shares
+    fin.resize((size_t)4 * h);
+    const size_t off_c = (size_t)(M_last - 1) * h, off_s = (size_t)M_last * h + off_c;
+    cudaError_t e = cudaMemcpyAsync(fin.data(), Hbuf[cur] + off_c, (size_t)h * 4, cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(fin.data() + h, Hbuf[cur] + off_s, (size_t)h * 4, cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(fin.data() + 2 * h, Dbuf + off_c, (size_t)h * 4, cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(fin.data() + 3 * h, Dbuf + off_s, (size_t)h * 4, cudaMemcpyDeviceToHost, stream);
+    if (e != cudaSuccess) rc = shd_cuda_fail(ctx, e, "prefill: final hidden");
+  }
+  if (rc == SHD_OK) {
+    unsigned long long key = 0;
+    cudaError_t e = cudaMemcpyAsync(&key, amax, 8, cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) rc = shd_cuda_fail(ctx, e, "shd_model_prefill");
+    if (rc == SHD_OK) {
+      const int tok = (int)(key & 0xffffffffu);
+      const int next_pos = len[slot] + n;
+      // decode state of the slot: input token and its position
+      e = cudaMemcpyAsync(tokens + slot, &tok, 4, cudaMemcpyHostToDevice, stream);
+      if (e == cudaSuccess) e = cudaMemcpyAsync(pos + slot, &next_pos, 4, cudaMemcpyHostToDevice, stream);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+      if (e != cudaSuccess) rc = shd_cuda_fail(ctx, e, "shd_model_prefill: state");
+      len[slot] = next_pos;
+      n_active = std::max(n_active, slot + 1);
+      if (next_token_host) *next_token_host = tok;
+      if (final_c_host) {
+        for (int i = 0; i < h; ++i) {
+          final_c_host[i] = fin[i] + fin[2 * h + i];  // secure_add_gpu: per-share add
+          final_s_host[i] = fin[h + i] + fin[3 * h + i];
+        }
+      }
+    }
+  }
+  return rc;
 }
 
 extern "C" int shd_model_prefill(shd_model* m, int slot, const int32_t* tokens_host, int n,
@@ -651,55 +684,49 @@ extern "C" int shd_model_prefill(shd_model* m, int slot, const int32_t* tokens_h
   int rc = m->check_ready();
   if (rc) return rc;
   if ((rc = m->enter())) return rc;
-  const int h = m->cfg.hidden;
-  std::vector<int> hp(3 * kPrefillRows);
-  int cur = 0;
-  for (int p0 = 0; p0 < n && rc == SHD_OK; p0 += kPrefillRows) {
-    const int M = std::min(kPrefillRows, n - p0);
-    for (int i = 0; i < M; ++i) {
-      hp[i] = tokens_host[p0 + i];
-      hp[kPrefillRows + i] = m->len[slot] + p0 + i;
-      hp[2 * kPrefillRows + i] = slot;
-    }
-    // the staging vector is reused: finish the previous chunk's copies first
-    if (cudaStreamSynchronize(m->stream) != cudaSuccess) { rc = shd_fail(ctx, SHD_ERR_CUDA, "prefill sync"); break; }
-    cudaError_t e = cudaMemcpyAsync(m->p_tokens, hp.data(), M * 4, cudaMemcpyHostToDevice, m->stream);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(m->p_pos, hp.data() + kPrefillRows, M * 4, cudaMemcpyHostToDevice, m->stream);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(m->p_seq, hp.data() + 2 * kPrefillRows, M * 4, cudaMemcpyHostToDevice, m->stream);
-    if (e != cudaSuccess) { rc = shd_cuda_fail(ctx, e, "prefill staging"); break; }
-    EmbedArgs ea{};
-    ea.table = m->embed; ea.vocab = m->cfg.vocab; ea.hidden = h; ea.tokens = m->p_tokens;
-    ea.pos = m->p_pos; ea.seed = m->cfg.share_seed; ea.counter_base = (uint64_t)slot << 32;
-    ea.Hc = m->Hbuf[0]; ea.Hs = m->Hbuf[0] + (size_t)M * h; ea.ldh = h;
-    ea.Dc = m->Dbuf; ea.Ds = m->Dbuf + (size_t)M * h; ea.amax = m->amax; ea.err = ctx->d_err;
-    if ((rc = launch_embed(ctx, ea, M))) break;
-    if ((rc = m->enqueue_layers(M, m->p_pos, m->p_seq, m->cfg.variant_prefill, cur, false))) break;
-    if (p0 + M == n) {
-      if ((rc = m->enqueue_head(M, M - 1, cur, m->cfg.variant_prefill, false, 0))) break;
-      if ((rc = m->allreduce_max_keys(1))) break;
-    }
-  }
-  if (rc == SHD_OK) {
-    unsigned long long key = 0;
-    cudaError_t e = cudaMemcpyAsync(&key, m->amax, 8, cudaMemcpyDeviceToHost, m->stream);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
-    if (e != cudaSuccess) rc = shd_cuda_fail(ctx, e, "shd_model_prefill");
-    if (rc == SHD_OK) {
-      const int tok = (int)(key & 0xffffffffu);
-      const int next_pos = m->len[slot] + n;
-      // decode state of the slot: input token and its position
-      e = cudaMemcpyAsync(m->tokens + slot, &tok, 4, cudaMemcpyHostToDevice, m->stream);
-      if (e == cudaSuccess) e = cudaMemcpyAsync(m->pos + slot, &next_pos, 4, cudaMemcpyHostToDevice, m->stream);
-      if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
-      if (e != cudaSuccess) rc = shd_cuda_fail(ctx, e, "shd_model_prefill: state");
-      m->len[slot] = next_pos;
-      m->n_active = std::max(m->n_active, slot + 1);
-      if (next_token_host) *next_token_host = tok;
-    }
-  }
+  rc = m->prefill_impl(slot, n, tokens_host, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, next_token_host);
   rc = m->leave(rc);
   if (rc == SHD_OK) rc = shd_sync(ctx);
   return rc;
+}
+
+extern "C" int shd_model_prefill_hidden(shd_model* m, int slot, const float* hc_host, const float* hs_host, int n,
+                                        float* logits_c_host, float* logits_s_host, float* final_c_host,
+                                        float* final_s_host, int32_t* next_token_host) {
+  if (!m) return SHD_ERR_ARG;
+  shd_ctx* ctx = m->ctx;
+  SHD_REQUIRE(ctx, slot >= 0 && slot < m->cfg.max_batch, "shd_model_prefill_hidden: slot out of range");
+  SHD_REQUIRE(ctx, hc_host && hs_host && n > 0, "shd_model_prefill_hidden: empty prompt (the reference rejects it)");
+  SHD_REQUIRE(ctx, (logits_c_host == nullptr) == (logits_s_host == nullptr) &&
+                   (final_c_host == nullptr) == (final_s_host == nullptr),
+              "shd_model_prefill_hidden: output shares come in pairs");
+  SHD_REQUIRE(ctx, m->len[slot] + n <= m->cfg.max_seq, "shd_model_prefill_hidden: prompt exceeds max_seq");
+  int rc = m->check_ready();
+  if (rc) return rc;
+  if ((rc = m->enter())) return rc;
+  rc = m->prefill_impl(slot, n, nullptr, hc_host, hs_host, logits_c_host, logits_s_host, final_c_host, final_s_host,
+                       next_token_host);
+  rc = m->leave(rc);
+  if (rc == SHD_OK) rc = shd_sync(ctx);
+  return rc;
+}
+
+extern "C" int shd_model_read_kv(shd_model* m, int slot, int pos0, int n, float* k_host, float* v_host) {
+  if (!m) return SHD_ERR_ARG;
+  shd_ctx* ctx = m->ctx;
+  SHD_REQUIRE(ctx, slot >= 0 && slot < m->cfg.max_batch, "shd_model_read_kv: slot out of range");
+  SHD_REQUIRE(ctx, k_host && v_host && n >= 0 && pos0 >= 0 && pos0 + n <= m->len[slot],
+              "shd_model_read_kv: positions beyond the slot's length");
+  SHD_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
+  const size_t kvd = (size_t)m->kvd, row = kvd * 4;
+  const size_t layer = (size_t)m->cfg.max_batch * m->cfg.max_seq * kvd;
+  for (int l = 0; l < m->cfg.n_layers; ++l) {
+    const size_t src = (size_t)l * layer + ((size_t)slot * m->cfg.max_seq + pos0) * kvd;
+    SHD_CHECK_CUDA(ctx, cudaMemcpyAsync(k_host + (size_t)l * n * kvd, m->kcache + src, n * row, cudaMemcpyDeviceToHost, m->stream));
+    SHD_CHECK_CUDA(ctx, cudaMemcpyAsync(v_host + (size_t)l * n * kvd, m->vcache + src, n * row, cudaMemcpyDeviceToHost, m->stream));
+  }
+  SHD_CHECK_CUDA(ctx, cudaStreamSynchronize(m->stream));
+  return SHD_OK;
 }
 
 // One decode step for slots [0, M): embed the current tokens at pos, all layers, head, tokens.
@@ -712,13 +739,10 @@ int shd_model::enqueue_decode_step(int M) {
   ea.Dc = Dbuf; ea.Ds = Dbuf + (size_t)M * h; ea.amax = amax; ea.err = ctx->d_err;
   ea.slot_counter = 1;
   int rc;
-  if (!rec && step_usable(M))
-    return shd::step_launch(ctx, step_plan, stream, amax, tokens, pos, hist, hist_cap, step, profiling != 0);
-  if ((rc = op_embed(ea, M))) return rc;
+  if ((rc = launch_embed(ctx, ea, M))) return rc;
   int cur = 0;
   if ((rc = enqueue_layers(M, pos, seq, cfg.variant_decode, cur, true))) return rc;
   if ((rc = enqueue_head_rows(M, cur, cfg.variant_decode))) return rc;
-  if (rec) return SHD_OK;  // the step kernel does the token update itself
   if ((rc = allreduce_max_keys(M))) return rc;
   SHD_CHECK_CUDA(ctx, launch_pdl(finish_step_kernel, dim3(1), dim3(32), 0, stream, (const unsigned long long*)amax,
                                  tokens, pos, hist, hist_cap, step, M));
@@ -746,10 +770,8 @@ extern "C" int shd_model_decode_async(shd_model* m, int n_steps) {
       cudaGraphExecDestroy(m->graph);
       m->graph = nullptr;
     }
-    // the persistent step for this batch size (single GPU), then one eager step (sets kernel
-    // attributes, real work), then capture the step
-    if (m->engine == 1 && ctx->tp_world <= 1 && m->step_plan.M != M) rc = m->build_step(M);
-    if (rc == SHD_OK) rc = m->enqueue_decode_step(M);
+    // one eager step (sets kernel attributes, real work), then capture the step
+    rc = m->enqueue_decode_step(M);
     done = 1;
     if (rc == SHD_OK && m->profiling) {
       const size_t need = (size_t)2 * (5 * m->cfg.n_layers + 1);
@@ -814,12 +836,15 @@ extern "C" int shd_model_read_tokens(shd_model* m, int count, int32_t* tokens_ho
   return shd_sync(ctx);
 }
 
-extern "C" int shd_model_forward_host(shd_model* m, int slot, const float* hc_host, const float* hs_host,
-                                      float* logits_c_host, float* logits_s_host) {
+extern "C" int shd_model_forward_host_hidden(shd_model* m, int slot, const float* hc_host, const float* hs_host,
+                                             float* logits_c_host, float* logits_s_host, float* hidden_c_host,
+                                             float* hidden_s_host) {
   if (!m) return SHD_ERR_ARG;
   shd_ctx* ctx = m->ctx;
   SHD_REQUIRE(ctx, slot >= 0 && slot < m->cfg.max_batch, "shd_model_forward_host: slot out of range");
   SHD_REQUIRE(ctx, hc_host && hs_host && logits_c_host && logits_s_host, "shd_model_forward_host: null buffer");
+  SHD_REQUIRE(ctx, (hidden_c_host == nullptr) == (hidden_s_host == nullptr),
+              "shd_model_forward_host: output shares come in pairs");
   SHD_REQUIRE(ctx, m->len[slot] < m->cfg.max_seq, "shd_model_forward_host: sequence full");
   int rc = m->check_ready();
   if (rc) return rc;
@@ -827,6 +852,7 @@ extern "C" int shd_model_forward_host(shd_model* m, int slot, const float* hc_ho
   const int h = m->cfg.hidden;
   const int p = m->len[slot];
   int meta[2] = {p, slot};
+  std::vector<float> fin(hidden_c_host ? (size_t)4 * h : 0);
   cudaError_t e = cudaMemcpyAsync(m->Hbuf[0], hc_host, (size_t)h * 4, cudaMemcpyHostToDevice, m->stream);
   if (e == cudaSuccess) e = cudaMemcpyAsync(m->Hbuf[0] + h, hs_host, (size_t)h * 4, cudaMemcpyHostToDevice, m->stream);
   if (e == cudaSuccess) e = cudaMemcpyAsync(m->p_pos, &meta[0], 4, cudaMemcpyHostToDevice, m->stream);
@@ -838,18 +864,37 @@ extern "C" int shd_model_forward_host(shd_model* m, int slot, const float* hc_ho
   if (rc == SHD_OK) rc = m->enqueue_layers(1, m->p_pos, m->p_seq, m->cfg.variant_decode, cur, true);
   if (rc == SHD_OK) rc = m->enqueue_head(1, 0, cur, m->cfg.variant_decode, true, 0);
   if (rc == SHD_OK) rc = m->gather_logits(logits_c_host, logits_s_host);
+  if (rc == SHD_OK && hidden_c_host) {
+    // the residual stream after the last layer: (H, D) of row 0, both shares
+    e = cudaMemcpyAsync(fin.data(), m->Hbuf[cur], (size_t)2 * h * 4, cudaMemcpyDeviceToHost, m->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(fin.data() + 2 * h, m->Dbuf, (size_t)2 * h * 4, cudaMemcpyDeviceToHost, m->stream);
+    if (e != cudaSuccess) rc = shd_cuda_fail(ctx, e, "shd_model_forward_host: hidden");
+  }
   if (rc == SHD_OK) {
     e = cudaStreamSynchronize(m->stream);
-    if (e != cudaSuccess) rc = shd_cuda_fail(ctx, e, "shd_model_forward_host");
-    else m->len[slot] = p + 1;
+    if (e != cudaSuccess) {
+      rc = shd_cuda_fail(ctx, e, "shd_model_forward_host");
+    } else {
+      m->len[slot] = p + 1;
+      if (hidden_c_host)
+        for (int i = 0; i < h; ++i) {
+          hidden_c_host[i] = fin[i] + fin[2 * h + i];  // secure_add_gpu: per-share add
+          hidden_s_host[i] = fin[h + i] + fin[3 * h + i];
+        }
+    }
   }
   rc = m->leave(rc);
   if (rc == SHD_OK) rc = shd_sync(ctx);
   return rc;
 }
 
+extern "C" int shd_model_forward_host(shd_model* m, int slot, const float* hc_host, const float* hs_host,
+                                      float* logits_c_host, float* logits_s_host) {
+  return shd_model_forward_host_hidden(m, slot, hc_host, hs_host, logits_c_host, logits_s_host, nullptr, nullptr);
+}
+
 int shd_model::prof_mark(int kind, const shd_weight* w, bool begin) {
-  if (!prof_active || rec) return SHD_OK;
+  if (!prof_active) return SHD_OK;
   if (prof_next + 1 >= prof_events.size()) return SHD_OK;
   if (begin) {
     prof_kind.push_back(kind);
@@ -871,32 +916,7 @@ extern "C" int shd_model_set_profiling(shd_model* m, int on) {
     m->graph = nullptr;
   }
   m->profiling = on != 0;
-  if (m->profiling && m->step_plan.d_prof) {
-    SHD_CHECK_CUDA(m->ctx, cudaSetDevice(m->ctx->device));
-    const int rc = shd::step_prof_reset(m->ctx, m->step_plan, m->stream);
-    if (rc) return rc;
-    SHD_CHECK_CUDA(m->ctx, cudaStreamSynchronize(m->stream));
-  }
   return SHD_OK;
-}
-
-extern "C" int shd_model_set_engine(shd_model* m, int engine) {
-  if (!m) return SHD_ERR_ARG;
-  SHD_REQUIRE(m->ctx, engine == 0 || engine == 1, "shd_model_set_engine: engine must be 0 or 1");
-  if (engine != m->engine) {
-    if (m->graph) {
-      cudaGraphExecDestroy(m->graph);
-      m->graph = nullptr;
-    }
-    shd::step_plan_free(m->step_plan);
-    m->engine = engine;
-  }
-  return SHD_OK;
-}
-
-extern "C" int shd_model_engine(const shd_model* m) {
-  if (!m) return SHD_ERR_ARG;
-  return (m->engine == 1 && m->step_plan.M > 0) ? 1 : 0;
 }
 
 extern "C" int shd_model_linear_times(shd_model* m, float* ms_out6, double* bytes_out6) {
@@ -904,7 +924,6 @@ extern "C" int shd_model_linear_times(shd_model* m, float* ms_out6, double* byte
   shd_ctx* ctx = m->ctx;
   SHD_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
   SHD_CHECK_CUDA(ctx, cudaStreamSynchronize(m->stream));
-  if (m->step_usable(m->graph_rows)) return shd::step_prof_read(ctx, m->step_plan, ms_out6, bytes_out6);
   SHD_REQUIRE(ctx, m->prof_count > 0, "shd_model_linear_times: no profiled decode step yet");
   for (int k = 0; k < 6; ++k) {
     ms_out6[k] = 0.f;

@@ -4,8 +4,8 @@
 #include <vector>
 
 #include "shd_gemv.cuh"
+#include "shd_nonlinear.cuh"
 #include "shd_planes.cuh"
-#include "shd_step.cuh"
 
 struct LayerW {
   shd_weight* qkv = nullptr;     // fused q|k|v, SHD_ROWS_QKV
@@ -63,19 +63,10 @@ struct shd_model {
   std::vector<double> prof_bytes;
   size_t prof_next = 0, prof_count = 0;
   int prof_mark(int kind, const shd_weight* w, bool begin);
-  // persistent decode step (one kernel per token; single-GPU models)
-  int engine = 0;                           // 0: one kernel per operation, 1: persistent step kernel
-  shd::StepPlan step_plan;                  // plan for step_plan.M rows (0: none)
-  std::vector<shd::StepJob>* rec = nullptr;  // when set, the enqueue functions record jobs
-  bool step_usable(int M) const { return engine == 1 && ctx->tp_world <= 1 && step_plan.M == M; }
-  int build_step(int M);
-  // launch (or record) one operation of the layer loop
+  // launch one linear of the layer loop (tensor cores or the GEMV, with a pending norm)
   // out_planes / wrote_out: see launch_linear_tc (tensor-core path only)
-  int op_gemv(const shd_weight* w, int M, int epi, const shd::GemvArgs& g, bool norm, int kind,
+  int op_gemv(const shd_weight* w, int M, int epi, const shd::GemvArgs& g, bool norm,
               const shd::PlaneOut* out_planes = nullptr, bool* wrote_out = nullptr);
-  int op_attn(const shd::AttnArgs& at, int M);
-  int op_norm(const shd::NormArgs& na, int M);
-  int op_embed(const shd::EmbedArgs& ea, int M);
 
   ~shd_model();
   int use_stream();
@@ -91,6 +82,9 @@ struct shd_model {
   int enqueue_head(int M, int row, int cur, int variant, bool want_logits, int key_row);
   int enqueue_head_rows(int M, int cur, int variant);
   int enqueue_decode_step(int M);
+  int prefill_impl(int slot, int n, const int32_t* tokens_host, const float* hc_host, const float* hs_host,
+                   float* logits_c_host, float* logits_s_host, float* final_c_host, float* final_s_host,
+                   int32_t* next_token_host);
   // tensor parallel collectives (no-ops at tp_world == 1)
   int allreduce_sum(float* buf, size_t n);
   bool tp_push(shd::GemvArgs& g, const shd_weight* w, int M, size_t n);

@@ -13,6 +13,13 @@
 // exits. Every call shares it and it keeps the last call's contents; the tile counters, which must
 // start at zero, are cleared on the caller's stream at the start of each call. Calls that overlap
 // on the GPU (different streams, or different host threads without ordering) race on it.
+//
+// Set-up: the first call on a device, with that device current, looks up the array's device
+// address (cudaGetSymbolAddress; the host-side name is only a stand-in). With lazy module loading
+// that lookup or the first launch may load the library's module and place the array in device
+// memory, so make one call per device before the host framework freezes device memory and before
+// any stream capture. Device-side wait timeouts set the array's error word, which this entry point
+// does not read back: they are not reported.
 #include <mutex>
 
 #include "shd_gemv.cuh"
@@ -26,8 +33,12 @@ constexpr size_t kNaPartialFloats =
     (size_t)kNaMaxCtas * 2 * shd::kTileRows * 2 * kNaMaxRowsPerLaunch;  // 2 slots per CTA
 constexpr size_t kNaScratchFloats = kNaPartialFloats + kNaMaxTiles + 64;
 
+}  // namespace
+
 // [partials: kNaPartialFloats][counters: kNaMaxTiles ints][error word + padding: 64]
-__device__ __align__(256) float g_noalloc_scratch[kNaScratchFloats];
+static __device__ __align__(256) float g_noalloc_scratch[kNaScratchFloats];
+
+namespace {
 
 struct DeviceScratch {
   float* base = nullptr;  // device address of g_noalloc_scratch on that device
@@ -90,7 +101,7 @@ extern "C" int shd_linear_dual_f32_noalloc(const shd_weight* w, const float* bia
   tmp.d_partials = partials;
   tmp.partial_floats = kNaPartialFloats;
   tmp.d_counters = counters;
-  tmp.n_counters = kNaMaxTiles + 8192;  // the GEMV launcher keeps the top 8192 counters out of its tiles
+  tmp.n_counters = kNaMaxTiles;
   tmp.d_err = err;
   for (int m0 = 0; m0 < M;) {
     const int mm = (M - m0) >= kNaMaxRowsPerLaunch ? kNaMaxRowsPerLaunch : (M - m0);
@@ -106,7 +117,10 @@ extern "C" int shd_linear_dual_f32_noalloc(const shd_weight* w, const float* bia
     a.Ys = ys + (size_t)m0 * w->N;
     a.ldy = w->N;
     const int rc = launch_gemv_f32(&tmp, w, mm, EPI_STORE, a);
-    if (rc) return rc;
+    if (rc) {
+      w->ctx->last_error = tmp.last_error;  // readable through shd_last_error(weight's context)
+      return rc;
+    }
     m0 += mm;
   }
   return SHD_OK;

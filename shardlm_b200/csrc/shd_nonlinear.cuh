@@ -69,18 +69,19 @@ struct AttnArgs {
   float* Oc;               // attention output shares [M][ldo]
   float* Os;
   int ldo;
-  int nsplit;              // position splits: set by the persistent step engine for its own attention
   // Decode launches: every K/V row before pos[m] of row m's slot, and pos/seq themselves, were
   // written before the previous step ended (only row pos[m] comes from the q/k/v kernel right
   // before), so they may be read before the wait on that kernel. 0 for prefill chunks.
   int early_kv;
   int group_cap;           // 8: `groups` hold up to 8 q heads each; otherwise up to 4
-  float* partials;         // step engine: [M][n_groups][nsplit][kAttnGroupMax][head_dim + 2]
-  int* counters;           // step engine: [M][n_groups]
   int* err;
 };
 
 int launch_attention(shd_ctx* ctx, const AttnArgs& a, int M);
+// Prompt blocks on the tensor cores (shd_flash.cu): rows m are positions pos[0] + m of slot seq[0]
+// and attend to [0, pos[0] + m]. Supported: head_dim 128, 16-byte aligned rows.
+bool flash_prefill_supported(const AttnArgs& a, int M);
+int launch_flash_prefill(shd_ctx* ctx, const AttnArgs& a, int M);
 // Groups of at most `cap` (4 or 8) consecutive local q heads sharing one kv head. Local q heads are
 // [q_begin, q_begin + q_count) of the model, local kv heads start at kv_begin; group = H / Hkv.
 std::vector<int4> attn_groups(int q_begin, int q_count, int kv_begin, int group, int cap = 4);

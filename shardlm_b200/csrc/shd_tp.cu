@@ -429,10 +429,10 @@ int shd_model::allreduce_sum(float* buf, size_t n) {
 }
 
 // A row-parallel GEMV of M rows of w pushes its tiles to the peers itself when the peer path is up,
-// the n-value message fits a slot, the GEMV (not the tensor-core linear) runs it and kernels are
-// launched one by one (engine 0); then fill g's push fields. allreduce_recv completes the sum.
+// the n-value message fits a slot and the GEMV (not the tensor-core linear) runs it; then fill g's
+// push fields. allreduce_recv completes the sum.
 bool shd_model::tp_push(shd::GemvArgs& g, const shd_weight* w, int M, size_t n) {
-  if (ctx->tp_world <= 1 || !ctx->p2p_local || ctx->tp_world > kP2pMaxWorld || n > kP2pCapacity || rec ||
+  if (ctx->tp_world <= 1 || !ctx->p2p_local || ctx->tp_world > kP2pMaxWorld || n > kP2pCapacity ||
       shd::tc_preferred(w, M))
     return false;
   for (int q = 0; q < ctx->tp_world; ++q) g.tp_peer[q] = static_cast<uint8_t*>(ctx->p2p_peer[q]);

@@ -5,6 +5,7 @@
   python -m shardlm_b200.microbench beaver [--n 9699328] [--iters 20]
   python -m shardlm_b200.microbench ring   [--copies 16] [--iters 20]
   python -m shardlm_b200.microbench attn   [--model qwen2.5-7b] [--kv-len 577] [--iters 20]
+  python -m shardlm_b200.microbench prefill [--model qwen2.5-7b] [--prompt 512] [--layers 28]
 
 --graph times a captured CUDA graph of the launches instead of host-issued launches.
 Each weight kind is instantiated in enough copies to exceed the 126 MB L2, and launches rotate over
@@ -149,9 +150,37 @@ def attn(args, ctx: Context):
                                "kv_bytes": kv_bytes}}))
 
 
+def prefill(args, ctx: Context):
+    """Whole-model prefill of a seeded prompt: one untimed prefill, then a timed one inside a
+    profiler window (cudaProfilerStart/Stop), so `ncu --profile-from-start off` lists exactly the
+    timed prefill's launches."""
+    from .model import SecureModel
+
+    sh = SHAPES[args.model].replace(n_layers=args.layers) if args.layers else SHAPES[args.model]
+    m = SecureModel(ctx, sh, max_seq=args.prompt + 8)
+    m.load_random_weights(seed=0)
+    toks = np.random.default_rng(0).integers(0, sh.vocab, args.prompt).astype(np.int32)
+    m.prefill(toks)
+    m.reset()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    m.prefill(toks)
+    e.record()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    ms = s.elapsed_time(e)
+    print(json.dumps({"prefill": {"model": sh.name, "layers": sh.n_layers, "tokens": args.prompt,
+                                  "ms": round(ms, 3), "tok_s": round(args.prompt / ms * 1e3, 1)}}))
+    m.close()
+
+
 def main():
     p = argparse.ArgumentParser()
-    p.add_argument("what", choices=["linear", "beaver", "ring", "attn"])
+    p.add_argument("what", choices=["linear", "beaver", "ring", "attn", "prefill"])
+    p.add_argument("--prompt", type=int, default=512)
+    p.add_argument("--layers", type=int, default=0)
     p.add_argument("--kv-len", type=int, default=577)
     p.add_argument("--model", default="qwen2.5-7b")
     p.add_argument("--kind", default="all")
@@ -164,7 +193,7 @@ def main():
     global GRAPH
     GRAPH = args.graph
     ctx = Context(0)
-    {"linear": linear, "beaver": beaver, "ring": ring, "attn": attn}[args.what](args, ctx)
+    {"linear": linear, "beaver": beaver, "ring": ring, "attn": attn, "prefill": prefill}[args.what](args, ctx)
 
 
 if __name__ == "__main__":

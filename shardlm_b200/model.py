@@ -177,16 +177,6 @@ class SecureModel:
     def reset(self) -> None:
         check(lib().shd_model_reset(self.handle), self.ctx.ptr)
 
-    def set_engine(self, engine: int) -> None:
-        """Decode engine: 0 = one kernel per operation (default), 1 = one persistent kernel per step
-        (single GPU)."""
-        check(lib().shd_model_set_engine(self.handle, engine), self.ctx.ptr)
-
-    @property
-    def engine(self) -> int:
-        """1 when the last decode ran the persistent step kernel."""
-        return int(lib().shd_model_engine(self.handle))
-
     def prefill(self, tokens, slot: int = 0) -> int:
         t = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
         out = C.c_int32()
@@ -217,6 +207,62 @@ class SecureModel:
         check(lib().shd_model_forward_host(self.handle, slot, hc.ctypes.data, hs.ctypes.data,
                                            out[0].ctypes.data, out[1].ctypes.data), self.ctx.ptr)
         return out
+
+    def forward_host_hidden(self, hc: np.ndarray, hs: np.ndarray, slot: int = 0):
+        """forward_host that also returns the position's output hidden shares:
+        (logits_c, logits_s, hidden_c, hidden_s)."""
+        hc = np.ascontiguousarray(hc, dtype=np.float32)
+        hs = np.ascontiguousarray(hs, dtype=np.float32)
+        V, h = self.shape.vocab, self.shape.hidden
+        lc, ls = np.empty(V, np.float32), np.empty(V, np.float32)
+        oc, os_ = np.empty(h, np.float32), np.empty(h, np.float32)
+        self.ctx.bind_stream()
+        check(lib().shd_model_forward_host_hidden(self.handle, slot, hc.ctypes.data, hs.ctypes.data, lc.ctypes.data,
+                                                  ls.ctypes.data, oc.ctypes.data, os_.ctypes.data), self.ctx.ptr)
+        return lc, ls, oc, os_
+
+    def prefill_hidden(self, hc: np.ndarray, hs: np.ndarray, slot: int = 0):
+        """batched_prefill_gpu_v3: hidden-state shares [n][h] in; returns (next token, logits_c,
+        logits_s, final_hidden_c, final_hidden_s) of the last position."""
+        hc = np.ascontiguousarray(hc, dtype=np.float32).reshape(-1, self.shape.hidden)
+        hs = np.ascontiguousarray(hs, dtype=np.float32).reshape(-1, self.shape.hidden)
+        V, h = self.shape.vocab, self.shape.hidden
+        lc, ls = np.empty(V, np.float32), np.empty(V, np.float32)
+        fc, fs = np.empty(h, np.float32), np.empty(h, np.float32)
+        tok = C.c_int32()
+        self.ctx.bind_stream()
+        check(lib().shd_model_prefill_hidden(self.handle, slot, hc.ctypes.data, hs.ctypes.data, hc.shape[0],
+                                             lc.ctypes.data, ls.ctypes.data, fc.ctypes.data, fs.ctypes.data,
+                                             C.byref(tok)), self.ctx.ptr)
+        return int(tok.value), lc, ls, fc, fs
+
+    def read_kv(self, pos0: int, n: int, slot: int = 0):
+        """Reconstructed K and V rows [n_layers][n][kv_dim] of positions [pos0, pos0 + n)."""
+        kvd = self.shard.kv_head_count * self.shape.head_dim
+        k = np.empty((self.shape.n_layers, n, kvd), np.float32)
+        v = np.empty_like(k)
+        check(lib().shd_model_read_kv(self.handle, slot, pos0, n, k.ctypes.data, v.ctypes.data), self.ctx.ptr)
+        return k, v
+
+    def _bincode(self, fn: str, req: bytes, *extra) -> bytes:
+        buf = np.frombuffer(bytes(req), np.uint8).copy()
+        n = C.c_size_t(0)
+        self.ctx.bind_stream()
+        args = (self.handle,) + extra[:1] + (buf.ctypes.data, buf.size) + extra[1:]
+        rc = getattr(lib(), fn)(*args, None, 0, C.byref(n))  # size query (no work is done)
+        if rc != _lib.SHD_ERR_ARG or n.value == 0:
+            check(rc, self.ctx.ptr)
+        out = np.empty(n.value, np.uint8)
+        check(getattr(lib(), fn)(*args, out.ctypes.data, out.size, C.byref(n)), self.ctx.ptr)
+        return out[: n.value].tobytes()
+
+    def prefill_binary(self, request: bytes, slot: int = 0, include_kv: bool = True) -> bytes:
+        """POST /v3/secure/gpu/prefill: a bincode BinaryPrefillRequest in, BinaryPrefillResponse out."""
+        return self._bincode("shd_bincode_prefill", request, slot, int(include_kv))
+
+    def decode_binary(self, request: bytes, slot: int = 0) -> bytes:
+        """A bincode BinaryDecodeRequest in, BinaryDecodeResponse out."""
+        return self._bincode("shd_bincode_decode", request, slot)
 
     def seq_len(self, slot: int = 0) -> int:
         return int(lib().shd_model_seq_len(self.handle, slot))

@@ -3,11 +3,15 @@
 Names, argument meaning and error behaviour follow the Rust crates this path replaces:
   * GpuSecureLinear      -- crates/v2/sharing/src/secure_linear.rs:148-405
   * LinearServer & co.   -- crates/sharing/src/linear.rs:186-274 (v1 Z_2^32 ring shares)
+  * Fixed / FixedVector  -- crates/fixed_point/src/fixed.rs:30-49, vector.rs:22-29
+  * SharePair / Share    -- crates/sharing/src/share.rs:44-135 (seeded server shares)
+  * get_embeddings_direct -- crates/v2/server/src/routes/secure_inference.rs:387-460
   * secure_multiply_*    -- crates/v2/sharing/src/beaver.rs:167-233
   * BeaverTriple(Store)  -- crates/v2/sharing/src/beaver.rs:21-156
 """
 from __future__ import annotations
 
+import ctypes as C
 from dataclasses import dataclass
 
 import numpy as np
@@ -111,6 +115,72 @@ class LinearResponseMsg:
     client_output_share: np.ndarray
     server_output_share: np.ndarray
     scale: int
+
+
+class FixedPointError(ValueError):
+    """Overflow / Underflow / InvalidScale of crates/fixed_point/src/error.rs."""
+
+
+def fixed_from_f64_slice(ctx: Context, values, scale: int = 16) -> torch.Tensor:
+    """FixedVector::from_f64_slice on the device: raw = round(v * 2^scale), half away from zero.
+    Raises FixedPointError for the first element outside i32 (as the reference's `?` does)."""
+    from ._lib import ShdError
+
+    v = values if isinstance(values, torch.Tensor) else torch.as_tensor(np.asarray(values, np.float64))
+    v = v.to(device=ctx.torch_device, dtype=torch.float64).contiguous().reshape(-1)
+    out = ctx.empty(v.numel(), dtype=torch.int32)
+    try:
+        ctx.call("shd_fixed_from_f64", ptr(v), v.numel(), scale, ptr(out))
+    except ShdError as e:
+        raise FixedPointError(str(e)) from None
+    return out
+
+
+def random_share_seeded(ctx: Context, x: torch.Tensor, seed: int):
+    """SharePair::from_plaintext_seeded on device i32 plaintext: (client, server) shares with the
+    server share = ChaCha20Rng::seed_from_u64(seed) words, client = x wrapping_sub server."""
+    x = x.to(device=ctx.torch_device, dtype=torch.int32).contiguous().reshape(-1)
+    xc, xs = torch.empty_like(x), torch.empty_like(x)
+    ctx.call("shd_ring_share_seeded", ptr(x), x.numel(), seed & 0xFFFFFFFFFFFFFFFF, ptr(xc), ptr(xs))
+    return xc, xs
+
+
+class SharePair:
+    """SharePair::from_plaintext_seeded (crates/sharing/src/share.rs:116-135) for host callers."""
+
+    def __init__(self, client: Share, server: Share):
+        self.client, self.server = client, server
+
+    @classmethod
+    def from_plaintext_seeded(cls, ctx: Context, plaintext_raw, scale: int, seed: int) -> "SharePair":
+        xc, xs = random_share_seeded(ctx, torch.as_tensor(np.asarray(plaintext_raw, np.int32)), seed)
+        return cls(Share(xc.cpu().numpy(), scale), Share(xs.cpu().numpy(), scale))
+
+    def reconstruct(self) -> np.ndarray:
+        if self.client.scale != self.server.scale:
+            raise SharingError(f"ScaleMismatch: expected {self.client.scale}, got {self.server.scale}")
+        if len(self.client) != len(self.server):
+            raise SharingError(f"DimensionMismatch: expected {len(self.client)}, got {len(self.server)}")
+        return (self.client.data.astype(np.int64) + self.server.data.astype(np.int64)).astype(np.int32)
+
+
+def get_embeddings_direct(ctx: Context, table: torch.Tensor, token_ids, session_id: bytes):
+    """get_embeddings_direct: shares of the bf16 embedding rows of one request, the server share
+    drawn from ChaCha20Rng::from_seed(session id || 16 zero bytes), bit-exact with the reference.
+    table: device bf16 [vocab][hidden]; session_id: the 16 UUID bytes."""
+    if len(session_id) != 16:
+        raise SharingError("InvalidRequest: session id must be 16 bytes")
+    vocab, hidden = table.shape
+    tok = np.asarray(token_ids, np.int64).reshape(-1)
+    bad = tok[(tok < 0) | (tok >= vocab)]
+    if bad.size:
+        raise SharingError(f"InvalidRequest: Token ID {int(bad[0])} out of range (vocab_size={vocab})")
+    t = ctx.to_device(tok.astype(np.int32))
+    hc, hs = ctx.empty(tok.size, hidden), ctx.empty(tok.size, hidden)
+    sid = np.frombuffer(bytes(session_id), np.uint8).copy()
+    ctx.call("shd_embed_shares_session", ptr(table.contiguous()), vocab, hidden, ptr(t), tok.size,
+             sid.ctypes.data, ptr(hc), ptr(hs))
+    return hc, hs
 
 
 class LinearServer:
@@ -286,3 +356,49 @@ __all__ = [
     "beaver_triples_f32", "secure_multiply_batch", "secure_multiply_mpc", "beaver_mul_ring",
     "beaver_triples_ring", "fill_uniform", "reconstruct", "reshare", "secure_add_gpu", "NL_APPROX",
 ]
+
+
+# ------------------------------------------------------------------------------------------------
+# V3-OT function tables and the server's OT query processing
+# ------------------------------------------------------------------------------------------------
+class StandardOtTables:
+    """StandardOtTables::new(table_size) (crates/v2/sharing/src/secure_nonlinear_ot.rs:554-575) on
+    the device: silu, exp, rsqrt, reciprocal tables of f32 (4 bytes per row, as the reference's
+    as_bytes())."""
+
+    RANGES = {"silu": (-8.0, 8.0), "exp": (-10.0, 0.0), "rsqrt": (0.01, 10.0), "reciprocal": (0.01, 100.0)}
+
+    def __init__(self, ctx: Context, table_size: int = 4096):
+        self.ctx, self.size = ctx, table_size
+        self.values = ctx.empty(4, table_size)
+        ctx.call("shd_ot_standard_tables", table_size, ptr(self.values))
+        self.index = {k: i for i, k in enumerate(self.RANGES)}
+
+    def table(self, name: str) -> torch.Tensor:
+        """The table of an operation name as the route maps them (rmsnorm/rsqrt, silu/swiglu,
+        softmax/exp, reciprocal)."""
+        alias = {"rmsnorm": "rsqrt", "swiglu": "silu", "softmax": "exp"}
+        return self.values[self.index[alias.get(name, name)]]
+
+
+class OtFunctionServer:
+    """OtFunctionServer (crates/v2/sharing/src/secure_nonlinear_ot.rs:173-235) answering queries on
+    the GPU: the session commitment comes from the base-OT handshake (out of scope here), the
+    session counter advances by one per query as the reference's does."""
+
+    def __init__(self, ctx: Context, commitment: bytes):
+        if len(commitment) != 32:
+            raise SharingError("session commitment must be 32 bytes")
+        self.ctx, self.commitment, self.session_ctr = ctx, bytes(commitment), 0
+
+    def process_query(self, query: bytes, table: torch.Tensor) -> bytes:
+        self.session_ctr += 1
+        q = np.frombuffer(bytes(query), np.uint8).copy()
+        com = np.frombuffer(self.commitment, np.uint8).copy()
+        m = int(q[0]) | (int(q[1]) << 8) if q.size >= 2 else 0
+        out = np.empty(max(1, m * 4), np.uint8)
+        n = C.c_size_t(0)
+        t = table.contiguous()
+        self.ctx.call("shd_ot_process_query", com.ctypes.data, self.session_ctr, q.ctypes.data, q.size, ptr(t),
+                      t.numel() * t.element_size(), 4, out.ctypes.data, out.size, C.byref(n))
+        return out[: n.value].tobytes()

@@ -43,17 +43,15 @@ def _check_token(gpu_tok, lc, ls, orc):
     return True
 
 
-@pytest.mark.parametrize("engine", [1, 0])
 @pytest.mark.parametrize("shape_name,n_layers,prompt,steps,max_seq",
                          [("tiny", 2, 11, 12, 64), ("qwen2.5-1.5b", 2, 9, 6, 64), ("tiny", 1, 2450, 3, 2460)])
-def test_prefill_decode_tokens_match_oracle(ctx, orc, shape_name, n_layers, prompt, steps, max_seq, engine):
-    """engine 1: the persistent step kernel; engine 0: one kernel per operation. The long prompt
-    gives every attention split of the step kernel several 32-position tiles."""
+def test_prefill_decode_tokens_match_oracle(ctx, orc, shape_name, n_layers, prompt, steps, max_seq):
+    """Prefill then greedy decode; the long prompt gives the attention kernel many K/V tiles per
+    cluster CTA."""
     from shardlm_b200.model import SHAPES, SecureModel
 
     shape = SHAPES[shape_name].replace(n_layers=n_layers)
     m = SecureModel(ctx, shape, max_seq=max_seq, share_seed=123)
-    m.set_engine(engine)
     host = m.load_random_weights(seed=5, host_copy=True)
     om = _oracle_for(orc, shape, host, max_seq)
     rng = np.random.default_rng(0)
@@ -71,7 +69,48 @@ def test_prefill_decode_tokens_match_oracle(ctx, orc, shape_name, n_layers, prom
         inp = int(gpu[i])  # teacher-force the GPU's choice so one near-tie cannot cascade
     assert exact >= steps - 1
     assert m.seq_len() == prompt + steps
-    assert m.engine == engine
+
+
+@pytest.mark.parametrize("variant", ["v3", "mpc"])
+def test_long_prompt_tensor_core_attention(ctx, orc, variant):
+    """A 700-token prompt through a one-layer 7B-shaped model: every 128-position block's attention
+    runs on the tensor cores (flash prefill), the last block ragged; the next token and three decode
+    steps are checked against the oracle (V3-MPC: with reshare masks)."""
+    from shardlm_b200._lib import NL_MPC
+    from shardlm_b200.model import QWEN2_5_7B, SecureModel
+    from shardlm_b200.sharing import beaver_triples_f32
+
+    orc.set_threads(orc.max_threads())
+    shape = QWEN2_5_7B.replace(n_layers=1, vocab=4096)
+    prompt, steps, max_seq = 700, 3, 712
+    mpc = variant == "mpc"
+    kw = dict(variant_decode=NL_MPC, variant_prefill=NL_MPC, variant_attn=NL_MPC) if mpc else {}
+    m = SecureModel(ctx, shape, max_seq=max_seq, share_seed=31, **kw)
+    host = m.load_random_weights(seed=17, host_copy=True)
+    masks = None
+    if mpc:
+        P = 10 * shape.hidden + 20 + 5 * 32
+        a = torch.stack([beaver_triples_f32(ctx, P, seed=4, offset=l * P).a for l in range(shape.n_layers)])
+        m.set_masks(a)
+        masks = a.cpu().numpy()
+    om = _oracle_for(orc, shape, host, max_seq)
+    toks = np.random.default_rng(3).integers(0, shape.vocab, prompt).astype(np.int32)
+    nxt = m.prefill(toks)
+    pv = orc.NL_MPC if mpc else orc.NL_GPU
+    av = orc.NL_MPC if mpc else orc.NL_APPROX
+    for p, t in enumerate(toks):
+        hc, hs = orc.embed_shares(host["embed"], shape.hidden, int(t), 31, p)
+        _, _, lc, ls = om.forward(hc, hs, variant=pv, attn_variant=av, masks=masks)
+    exact = int(_check_token(nxt, lc, ls, orc))
+    gpu = m.decode(steps)[:, 0]
+    inp = nxt
+    for i in range(steps):
+        hc, hs = orc.embed_shares(host["embed"], shape.hidden, int(inp), 31, prompt + i)
+        _, _, lc, ls = om.forward(hc, hs, variant=av, attn_variant=av, masks=masks)
+        exact += _check_token(int(gpu[i]), lc, ls, orc)
+        inp = int(gpu[i])
+    assert exact >= steps
+    m.close()
 
 
 def test_forward_host_logits_match_oracle(ctx, orc):
@@ -126,10 +165,9 @@ def test_mpc_masks_reshare(ctx, orc):
 
 
 @pytest.mark.parametrize("variant,slots", [("approx", 3), ("mpc", 3), ("approx", 6)])
-def test_batched_decode_engines_agree_with_oracle(ctx, orc, variant, slots):
-    """Slots decoded together (M rows per step) by both engines, each checked against the oracle slot
-    by slot (teacher-forced on the GPU's tokens). With 6 rows the per-kernel engine runs the layer
-    linears on the tensor cores."""
+def test_batched_decode_agrees_with_oracle(ctx, orc, variant, slots):
+    """Slots decoded together (M rows per step), each checked against the oracle slot by slot
+    (teacher-forced on the GPU's tokens). With 6 rows the layer linears run on the tensor cores."""
     from shardlm_b200._lib import NL_APPROX, NL_GPU, NL_MPC
     from shardlm_b200.model import TINY, SecureModel
     from shardlm_b200.sharing import beaver_triples_f32
@@ -140,35 +178,30 @@ def test_batched_decode_engines_agree_with_oracle(ctx, orc, variant, slots):
     prompts = [np.array(p, np.int32) for p in ([5, 17, 300], [9, 2, 44, 11, 7], [999], [1, 2], [640, 3, 3, 8],
                                                [77, 78, 79, 80, 81, 82])][:slots]
     steps = 5
-    results = {}
-    for engine in (1, 0):
-        m = SecureModel(ctx, shape, max_seq=32, max_batch=slots, share_seed=77, variant_decode=nl,
-                        variant_prefill=nl_pre, variant_attn=nl)
-        m.set_engine(engine)
-        host = m.load_random_weights(seed=12, host_copy=True)
-        masks = None
-        if variant == "mpc":
-            P = 10 * shape.hidden + 20 + 5 * 32
-            a = torch.stack([beaver_triples_f32(ctx, P, seed=8, offset=l * P).a for l in range(shape.n_layers)])
-            m.set_masks(a)
-            masks = a.cpu().numpy()
-        first = [m.prefill(p, slot=b) for b, p in enumerate(prompts)]
-        toks = m.decode(steps, n_active=slots)
-        assert m.engine == engine
-        results[engine] = toks
-        om = [_oracle_for(orc, shape, host, 32) for _ in prompts]
-        for b, p in enumerate(prompts):
-            for i, t in enumerate(p):
-                hc, hs = orc.embed_shares(host["embed"], shape.hidden, int(t), 77, (b << 32) + i)
-                om[b].forward(hc, hs, variant=nl_pre, attn_variant=nl, masks=masks)
-            inp = first[b]
-            for i in range(steps):
-                hc, hs = orc.embed_shares(host["embed"], shape.hidden, int(inp), 77, (b << 32) + len(p) + i)
-                _, _, lc, ls = om[b].forward(hc, hs, variant=nl, attn_variant=nl, masks=masks)
-                _check_token(int(toks[i, b]), lc, ls, orc)
-                inp = int(toks[i, b])
-    # both engines compute the same shares up to float reassociation: the tokens agree
-    assert np.mean(results[0] == results[1]) >= 0.9
+    m = SecureModel(ctx, shape, max_seq=32, max_batch=slots, share_seed=77, variant_decode=nl,
+                    variant_prefill=nl_pre, variant_attn=nl)
+    host = m.load_random_weights(seed=12, host_copy=True)
+    masks = None
+    if variant == "mpc":
+        P = 10 * shape.hidden + 20 + 5 * 32
+        a = torch.stack([beaver_triples_f32(ctx, P, seed=8, offset=l * P).a for l in range(shape.n_layers)])
+        m.set_masks(a)
+        masks = a.cpu().numpy()
+    first = [m.prefill(p, slot=b) for b, p in enumerate(prompts)]
+    toks = m.decode(steps, n_active=slots)
+    om = [_oracle_for(orc, shape, host, 32) for _ in prompts]
+    exact = 0
+    for b, p in enumerate(prompts):
+        for i, t in enumerate(p):
+            hc, hs = orc.embed_shares(host["embed"], shape.hidden, int(t), 77, (b << 32) + i)
+            om[b].forward(hc, hs, variant=nl_pre, attn_variant=nl, masks=masks)
+        inp = first[b]
+        for i in range(steps):
+            hc, hs = orc.embed_shares(host["embed"], shape.hidden, int(inp), 77, (b << 32) + len(p) + i)
+            _, _, lc, ls = om[b].forward(hc, hs, variant=nl, attn_variant=nl, masks=masks)
+            exact += _check_token(int(toks[i, b]), lc, ls, orc)
+            inp = int(toks[i, b])
+    assert exact >= slots * steps - 1
 
 
 def test_batched_decode_tensor_core_rows(ctx, orc):

@@ -173,6 +173,45 @@ def test_attention_decode_rows(ctx, orc, M, H, Hkv, d):
             assert np.array_equal(first, got)
 
 
+@pytest.mark.parametrize("variant", [0, 2])
+@pytest.mark.parametrize("H,Hkv,pos0,M", [(28, 4, 0, 512), (28, 4, 384, 128), (12, 2, 33, 100), (40, 8, 0, 2048),
+                                          (4, 1, 7, 17)])
+def test_attention_prefill_tensor_cores(ctx, orc, variant, H, Hkv, pos0, M):
+    """shd_attn_prefill (tcgen05 flash attention over a prompt block) vs the oracle's
+    secure_attention_approx / compute_mpc_attention_on_shares row by row: rows m are positions
+    pos0 + m attending to [0, pos0 + m]. Ragged blocks (M % 128 != 0), a block after earlier
+    positions, a 2048-position prompt, a tensor-parallel slice (4 q heads on 1 kv head); with MPC
+    masks the server share is the mask. A second launch repeats the first bit for bit."""
+    from shardlm_b200.runtime import ptr
+
+    d = 128
+    T = pos0 + M + 5
+    rng = np.random.default_rng(H * M + pos0 + variant)
+    q = rng.standard_normal((M, H * d)).astype(np.float32)
+    k = rng.standard_normal((T, Hkv * d)).astype(np.float32)
+    v = rng.standard_normal((T, Hkv * d)).astype(np.float32)
+    mask = rng.uniform(-1, 1, (M, H * d)).astype(np.float32) if variant == 2 else None
+    oc, os_ = ctx.empty(M, H * d), ctx.empty(M, H * d)
+    qd, kd, vd = _dev(ctx, q), _dev(ctx, k), _dev(ctx, v)
+    md = None if mask is None else _dev(ctx, mask)
+    outs = []
+    for rep in range(2):
+        ctx.call("shd_attn_prefill", ptr(qd), ptr(kd), ptr(vd), T, H, Hkv, d, pos0, M, variant,
+                 None if md is None else ptr(md), ptr(oc), ptr(os_))
+        ctx.sync()
+        outs.append((oc.cpu().numpy().copy(), os_.cpu().numpy().copy()))
+    assert np.array_equal(outs[0][0], outs[1][0])
+    got_c, got_s = outs[0]
+    rows = sorted(set(list(range(0, M, max(1, M // 24))) + [M - 1, min(M - 1, 127), min(M - 1, 128)]))
+    for m in rows:
+        L = pos0 + m + 1
+        rc, rs = orc.attention(q[m], k[:L], v[:L], H, Hkv, d, variant, None if mask is None else mask[m])
+        assert np.array_equal(got_s[m], rs)
+        err = np.max(np.abs(got_c[m] - rc))
+        # f32-accurate products (three-term bf16 split), reassociated sums: 2e-5 of the value scale
+        assert err <= 2e-5 * max(1.0, np.max(np.abs(rc))), (m, err)
+
+
 def test_embed_shares_bit_exact(ctx, orc):
     from shardlm_b200.runtime import ptr
 

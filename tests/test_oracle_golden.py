@@ -164,6 +164,45 @@ def test_philox_against_independent_python(orc):
     assert _philox_py(0, 0, 0) == [0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8]
 
 
+def _pcg32_seed_py(state):
+    """rand_core 0.6.4 SeedableRng::seed_from_u64, written out independently in Python."""
+    m64 = (1 << 64) - 1
+    out = b""
+    for _ in range(8):
+        state = (state * 6364136223846793005 + 11634580027462260723) & m64
+        xs = (((state >> 18) ^ state) >> 27) & 0xFFFFFFFF
+        rot = state >> 59
+        out += (((xs >> rot) | (xs << ((32 - rot) & 31))) & 0xFFFFFFFF).to_bytes(4, "little")
+    return out
+
+
+def test_chacha20_against_independent_implementation(orc):
+    """ChaCha20Rng (rand_chacha 0.3.1) words = the ChaCha20 keystream with a zero nonce and the
+    block counter from 0; checked against the `cryptography` package's ChaCha20 (OpenSSL)."""
+    from cryptography.hazmat.primitives.ciphers import Cipher, algorithms
+
+    for key in (bytes(32), bytes(range(32)), _pcg32_seed_py(42)):
+        for off, n in ((0, 64), (7, 300), (1000, 129)):
+            ks = Cipher(algorithms.ChaCha20(key, bytes(16)), mode=None).encryptor().update(bytes(4 * (off + n)))
+            want = np.frombuffer(ks, "<u4")[off:off + n]
+            assert np.array_equal(orc.chacha20_words(key, off, n), want)
+    # rand_chacha's own test vector for the all-zero seed starts with this word
+    assert int(orc.chacha20_words(bytes(32), 0, 1)[0]) == 0xADE0B876
+
+
+def test_seed_from_u64_and_seeded_shares(orc):
+    for seed in (0, 1, 42, 12345, 2**64 - 1):
+        assert orc.seed_from_u64(seed) == _pcg32_seed_py(seed)
+    x = np.random.default_rng(0).integers(-2**31, 2**31, 1000, dtype=np.int64).astype(np.int32)
+    xc, xs = orc.ring_share_seeded(x, 12345)
+    assert np.array_equal(xs.view(np.uint32), orc.chacha20_words(orc.seed_from_u64(12345), 0, 1000))
+    # SharePair::reconstruct: x_c wrapping_add x_s == x
+    assert np.array_equal((xc.astype(np.int64) + xs.astype(np.int64)).astype(np.int32), x)
+    # determinism and seed sensitivity, as share.rs:238-250 tests
+    assert np.array_equal(orc.ring_share_seeded(x, 12345)[1], xs)
+    assert not np.array_equal(orc.ring_share_seeded(x, 12346)[1], xs)
+
+
 def test_rope_table_matches_reference_formula(orc):
     c, s = orc.rope_table(128, 16, 1e6)
     inv = (1.0 / np.power(np.float32(1e6), np.arange(0, 64, dtype=np.float32) * 2 / np.float32(128))).astype(np.float32)
