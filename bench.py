@@ -248,8 +248,29 @@ def run_ours(args, shape):
         t = torch.tensor([pf_s], device="cuda", dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         pf_s = float(t.item())
+    # tensor-pipe work of the timed prefill: the seven layer linears at 12 FLOPs per weight and token
+    # (2 shares x 3 bf16 terms x multiply-add) and the prompt attention at 24 FLOPs per score and
+    # per weighted value (6 bf16 term products x multiply-add), per rank
+    h, d = shape.hidden, shape.head_dim
+    per_layer = (h * shape.n_heads * d + 2 * h * shape.n_kv_heads * d + shape.n_heads * d * h
+                 + 3 * h * shape.intermediate)
+    n_prompts = max(1, B - 1) if B > 1 else 1
+    P = args.prompt
+    tc_flops = (12.0 * per_layer * shape.n_layers * n_pf
+                + 24.0 * shape.n_heads * d * shape.n_layers * n_prompts * P * (P + 1) / 2) / world
+    sustained = None
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            sustained = float(json.load(f)["bf16_tflops_sustained"])
+    except Exception:
+        sustained = 1400.0
+    tc_tflops = tc_flops / pf_s / 1e12
     prefill = {"tokens": n_pf, "seconds": round(pf_s, 4), "tok_s": round(n_pf / pf_s, 1),
-               "path": "shd_model_prefill, 128-position chunks through the tcgen05 linears (host-synchronous)"}
+               "tensor_tflops": round(tc_tflops, 1), "tensor_flops_per_gpu": tc_flops,
+               "tensor_frac_of_sustained_bf16": round(tc_tflops / sustained, 4),
+               "sustained_bf16_tflops": sustained,
+               "path": "shd_model_prefill: prompt chunks through the tcgen05 linears and the tcgen05 "
+                       "prefill attention (host-synchronous, wall time around the call)"}
     lib = _lib.lib()
     model.decode_async(args.warmup)
     torch.cuda.synchronize()
@@ -312,8 +333,11 @@ def run_ours(args, shape):
             hrng.random(out=s_buf, dtype=np.float32)
             np.subtract(embed_host[tok], s_buf, out=c_buf)
             lc, ls = model.forward_host(c_buf, s_buf, slot=slot, out=out)
+            # client reconstruct + greedy: the LAST index among equal maxima (Iterator::max_by)
             l = np.add(lc, ls, out=l_buf)
-            return int(len(l) - 1 - np.argmax(l[::-1]))  # last index among equal maxima
+            i = int(np.argmax(l))
+            ties = np.flatnonzero(l[i + 1:] == l[i])
+            return i + 1 + int(ties[-1]) if ties.size else i
 
         for _ in range(2):
             tok = one(tok)

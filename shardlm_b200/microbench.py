@@ -6,6 +6,7 @@
   python -m shardlm_b200.microbench ring   [--copies 16] [--iters 20]
   python -m shardlm_b200.microbench attn   [--model qwen2.5-7b] [--kv-len 577] [--iters 20]
   python -m shardlm_b200.microbench prefill [--model qwen2.5-7b] [--prompt 512] [--layers 28]
+  python -m shardlm_b200.microbench attn-prefill [--model qwen2.5-7b] [--rows 512] [--kv-len 512]
 
 --graph times a captured CUDA graph of the launches instead of host-issued launches.
 Each weight kind is instantiated in enough copies to exceed the 126 MB L2, and launches rotate over
@@ -150,6 +151,31 @@ def attn(args, ctx: Context):
                                "kv_bytes": kv_bytes}}))
 
 
+def attn_prefill(args, ctx: Context):
+    """Prompt-block attention on the tensor cores (shd_attn_prefill): --rows query rows ending at
+    position kv_len - 1, every head of the model; reports tensor TFLOP/s (6 bf16 term products per
+    f32 multiply-add of QK^T and PV, causal)."""
+    sh = SHAPES[args.model]
+    H, Hkv, d = sh.n_heads, sh.n_kv_heads, sh.head_dim
+    M, L = args.rows, max(args.kv_len, args.rows)
+    pos0 = L - M
+    q = torch.randn(M, H * d, device="cuda")
+    k = torch.randn(L, Hkv * d, device="cuda")
+    v = torch.randn(L, Hkv * d, device="cuda")
+    oc, os_ = torch.empty(M, H * d, device="cuda"), torch.empty(M, H * d, device="cuda")
+
+    def run(i):
+        ctx.call("shd_attn_prefill", ptr(q), ptr(k), ptr(v), L, H, Hkv, d, pos0, M, 0, None, ptr(oc), ptr(os_))
+
+    ms = _time(run, args.iters)
+    ctx.sync()
+    pairs = M * pos0 + M * (M + 1) // 2  # (query, position) pairs attended
+    flops = 24.0 * H * d * pairs
+    print(json.dumps({"attn_prefill": {"H": H, "Hkv": Hkv, "rows": M, "kv_len": L,
+                                       "us_per_call_incl_host": round(ms * 1e3, 2),
+                                       "tensor_TFLOPs": round(flops / ms / 1e9, 1)}}))
+
+
 def prefill(args, ctx: Context):
     """Whole-model prefill of a seeded prompt: one untimed prefill, then a timed one inside a
     profiler window (cudaProfilerStart/Stop), so `ncu --profile-from-start off` lists exactly the
@@ -178,7 +204,7 @@ def prefill(args, ctx: Context):
 
 def main():
     p = argparse.ArgumentParser()
-    p.add_argument("what", choices=["linear", "beaver", "ring", "attn", "prefill"])
+    p.add_argument("what", choices=["linear", "beaver", "ring", "attn", "attn-prefill", "prefill"])
     p.add_argument("--prompt", type=int, default=512)
     p.add_argument("--layers", type=int, default=0)
     p.add_argument("--kv-len", type=int, default=577)
@@ -193,7 +219,8 @@ def main():
     global GRAPH
     GRAPH = args.graph
     ctx = Context(0)
-    {"linear": linear, "beaver": beaver, "ring": ring, "attn": attn, "prefill": prefill}[args.what](args, ctx)
+    {"linear": linear, "beaver": beaver, "ring": ring, "attn": attn, "attn-prefill": attn_prefill,
+     "prefill": prefill}[args.what](args, ctx)
 
 
 if __name__ == "__main__":
