@@ -12,13 +12,15 @@
 // the tensor core accumulates in f32, so scores and weighted sums keep f32 accuracy:
 //   S = sum_(i+j<=2) Q_i K_j^T      M = 128 queries, N = 64 positions, K = 128 head dims
 //   O_tile = sum_(i+j<=2) P_i V_j   M = 128 queries, N = 128 head dims, K = 64 positions
-// Warps 0-3 (thread = query row = tensor-memory lane) load and split the K and V tiles into
-// 128-byte-swizzled K-major shared-memory planes (V transposed so that positions are K), read the
-// scores from tensor memory, run the online softmax (running max and sum, the reference's +-40
-// clamp applied to s - max for the approximate variant; masked positions weigh exactly 0), write
-// the weights' planes, and keep the output row in registers (O = O * alpha + O_tile). Warp 4 owns
-// tensor memory (S: 64 columns, O_tile: 128 columns) and one lane issues the MMAs, each group
-// committed to an mbarrier the other warps wait on (bounded, as every wait in this library).
+// Eight worker warps load and split the K and V tiles into 128-byte-swizzled K-major shared-memory
+// planes (V transposed so that positions are K); warps w and w + 4 share query rows 32 (w % 4) ..
+// + 31 (their tensor-memory lanes) and split each row's columns in halves: they read the scores
+// from tensor memory, run the online softmax (running max exchanged through shared memory, the
+// reference's +-40 clamp applied to s - max for the approximate variant, masked positions weigh
+// exactly 0), write the weights' planes, and keep half the output row in registers (O = O * alpha
+// + O_tile). Warp 0 also owns tensor memory (S: 64 columns, O_tile: 128 columns) and thread 0
+// issues the MMAs, each group committed to an mbarrier the warps wait on (bounded, as every wait in
+// this library).
 #include <cuda_bf16.h>
 
 #include <cmath>
@@ -33,7 +35,9 @@ namespace {
 constexpr int kFQ = 128;          // query rows per CTA
 constexpr int kFKV = 64;          // positions per K/V tile
 constexpr int kFHD = 128;         // head_dim
-constexpr int kFThreads = 160;    // warps 0-3 workers, warp 4 tensor memory + MMA issue
+constexpr int kFWorkers = 8;      // worker warps: warp w serves query rows 32 (w % 4) .. + 31 (its
+                                  // tensor-memory lanes) and half w / 4 of the columns
+constexpr int kFThreads = 32 * kFWorkers;  // warp 0 also owns tensor memory, thread 0 issues the MMAs
 constexpr uint32_t kFCols = 256;  // S at columns [0, 64), O_tile at [64, 192)
 constexpr uint32_t kFColO = 64;
 
@@ -41,7 +45,8 @@ constexpr uint32_t kFColO = 64;
 constexpr uint32_t kQOff = 0;                          // Q   [3 terms][2 K blocks][128 rows][128 B]
 constexpr uint32_t kKVOff = 3 * 2 * kFQ * 128;         // K   [3][2][64 rows][128 B]  (or)  V^T [3][128 rows][128 B]
 constexpr uint32_t kPOff = kKVOff + 3 * kFHD * 128;    // P   [3][128 rows][128 B]
-constexpr uint32_t kBarOff = kPOff + 3 * kFQ * 128;    // s_full, pv_full, done, tmem base, abort
+constexpr uint32_t kRedOff = kPOff + 3 * kFQ * 128;    // [2 halves][128 rows] f32: row maxima / sums
+constexpr uint32_t kBarOff = kRedOff + 2 * kFQ * 4;    // s_full, pv_full, done, tmem base, abort
 constexpr size_t kFSmem = kBarOff + 64 + 1024;         // + alignment slack
 
 // the six kept term pairs (i, j), i + j <= 2
@@ -63,48 +68,70 @@ __device__ __forceinline__ bool flash_wait(uint64_t* bar, uint32_t parity, int* 
   return ok;
 }
 
+// The two worker warps of one lane quarter (warps q and q + 4) exchange row values through shared
+// memory: named barrier 1 + q over their 64 threads.
+__device__ __forceinline__ void pair_sync(int quarter) {
+  asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
+}
+
 // rows [0, nrows) x 128 f32 columns of `src` (row stride ld) -> three K-major 128-byte-swizzled bf16
 // planes at dst + t * plane_bytes, K blocks of 64 columns nrows * 128 bytes apart. Rows at or past
-// `valid` are zero. Warp w takes rows w, w + 4, ...; lane l columns 4l .. 4l + 3.
+// `valid` are zero. Worker warp w takes rows w, w + 8, ...; lane l columns 4l .. 4l + 3. The loads
+// of 4 rows are issued before any is used (one memory latency per 4 rows, not per row).
 __device__ __forceinline__ void split_rows_kmajor(uint8_t* dst, uint32_t plane_bytes, const float* src,
                                                   size_t ld, int nrows, int valid, int warp, int lane) {
+  constexpr int G = 4;
   const int kb = lane >> 4, e = (4 * lane) & 63;
-  for (int r = warp; r < nrows; r += 4) {
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (r < valid) v = *reinterpret_cast<const float4*>(src + (size_t)r * ld + 4 * lane);
-    uint16_t b[4][3];
-    split3(v.x, b[0]);
-    split3(v.y, b[1]);
-    split3(v.z, b[2]);
-    split3(v.w, b[3]);
-    const uint32_t off = (uint32_t)kb * (uint32_t)nrows * 128u + sw128_offset(r, e);
+  for (int r0 = warp; r0 < nrows; r0 += kFWorkers * G) {
+    float4 v[G];
 #pragma unroll
-    for (int t = 0; t < 3; ++t) {
-      uint2 pk;
-      pk.x = (uint32_t)b[0][t] | ((uint32_t)b[1][t] << 16);
-      pk.y = (uint32_t)b[2][t] | ((uint32_t)b[3][t] << 16);
-      *reinterpret_cast<uint2*>(dst + (size_t)t * plane_bytes + off) = pk;
+    for (int g = 0; g < G; ++g) {
+      const int r = r0 + g * kFWorkers;
+      v[g] = (r < valid && r < nrows) ? *reinterpret_cast<const float4*>(src + (size_t)r * ld + 4 * lane)
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const int r = r0 + g * kFWorkers;
+      if (r >= nrows) continue;
+      uint16_t b[4][3];
+      split3(v[g].x, b[0]);
+      split3(v[g].y, b[1]);
+      split3(v[g].z, b[2]);
+      split3(v[g].w, b[3]);
+      const uint32_t off = (uint32_t)kb * (uint32_t)nrows * 128u + sw128_offset(r, e);
+#pragma unroll
+      for (int t = 0; t < 3; ++t) {
+        uint2 pk;
+        pk.x = (uint32_t)b[0][t] | ((uint32_t)b[1][t] << 16);
+        pk.y = (uint32_t)b[2][t] | ((uint32_t)b[3][t] << 16);
+        *reinterpret_cast<uint2*>(dst + (size_t)t * plane_bytes + off) = pk;
+      }
     }
   }
 }
 
 // V rows [0, 64) (positions) x 128 dims -> three planes of V^T: [128 dims][64 positions] K-major,
 // 128-byte swizzle. Lane l takes positions 2l, 2l + 1 (one 4-byte store per dim and term, the 32
-// lanes of a warp filling one 128-byte row); warp w takes dims 32w .. 32w + 31.
+// lanes of a warp filling one 128-byte row); worker warp w takes dims 16w .. 16w + 15.
 __device__ __forceinline__ void split_v_transposed(uint8_t* dst, const float* V, size_t ld, int valid, int warp,
                                                    int lane) {
   const int p0 = 2 * lane;
-  const float* r0 = V + (size_t)p0 * ld + 32 * warp;
+  const float* r0 = V + (size_t)p0 * ld + 16 * warp;
   const float* r1 = r0 + ld;
   const bool v0ok = p0 < valid, v1ok = p0 + 1 < valid;
-#pragma unroll 2
-  for (int q = 0; q < 8; ++q) {
-    const float4 a = v0ok ? *reinterpret_cast<const float4*>(r0 + 4 * q) : make_float4(0.f, 0.f, 0.f, 0.f);
-    const float4 b = v1ok ? *reinterpret_cast<const float4*>(r1 + 4 * q) : make_float4(0.f, 0.f, 0.f, 0.f);
-    const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+  float4 a[4], b[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    a[q] = v0ok ? *reinterpret_cast<const float4*>(r0 + 4 * q) : make_float4(0.f, 0.f, 0.f, 0.f);
+    b[q] = v1ok ? *reinterpret_cast<const float4*>(r1 + 4 * q) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float av[4] = {a[q].x, a[q].y, a[q].z, a[q].w}, bv[4] = {b[q].x, b[q].y, b[q].z, b[q].w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const int d = 32 * warp + 4 * q + j;
+      const int d = 16 * warp + 4 * q + j;
       uint16_t sa[3], sb[3];
       split3(av[j], sa);
       split3(bv[j], sb);
@@ -120,12 +147,16 @@ __global__ void __launch_bounds__(kFThreads, 1) flash_prefill_kernel(const __gri
   const AttnArgs& a = fa.a;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* red = reinterpret_cast<float*>(smem + kRedOff);
   uint64_t* s_full = reinterpret_cast<uint64_t*>(smem + kBarOff);
   uint64_t* pv_full = s_full + 1;
   uint64_t* done = s_full + 2;
   uint32_t* tmem_base = reinterpret_cast<uint32_t*>(s_full + 3);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base + 1);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const bool worker = true;  // every warp works; thread 0 also issues the MMAs
+  const int quarter = warp & 3, half = (warp >> 2) & 1;
+  const int row = 32 * quarter + lane;  // query row of this worker thread (tensor-memory lane)
 
   if (tid == 0) {
     mbar_init(s_full, 1);
@@ -135,8 +166,8 @@ __global__ void __launch_bounds__(kFThreads, 1) flash_prefill_kernel(const __gri
     mbar_fence_init();
   }
   if (tid == 0) pdl_trigger();
-  pdl_wait();  // queries, the chunk's K/V rows and the positions come from the q/k/v kernel
-  if (warp == 4) tmem_alloc(tmem_base, kFCols);
+  pdl_wait();  // queries, the block's K/V rows and the positions come from the q/k/v kernel
+  if (warp == 0) tmem_alloc(tmem_base, kFCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -156,31 +187,33 @@ __global__ void __launch_bounds__(kFThreads, 1) flash_prefill_kernel(const __gri
   const float* K = a.Kcache + (size_t)sq * a.kv_seq_stride + (size_t)kvh * kFHD;
   const float* V = a.Vcache + (size_t)sq * a.kv_seq_stride + (size_t)kvh * kFHD;
   const bool mpc = a.variant == SHD_NL_MPC;
-  const int my_pos = pos0 + q0 + tid;                    // worker thread = query row
+  const int my_pos = pos0 + q0 + row;
   const int n_tiles = (kv_len + kFKV - 1) / kFKV;
+  const int sc0 = half * (kFKV / 2);   // this thread's score columns [sc0, sc0 + 32)
+  const int oc0 = half * (kFHD / 2);   // this thread's output columns [oc0, oc0 + 64)
 
   // Q planes, once
-  if (warp < 4)
+  if (worker)
     split_rows_kmajor(smem + kQOff, 2 * kFQ * 128, a.Q + (size_t)q0 * a.ldq + (size_t)hq * kFHD, (size_t)a.ldq,
                       kFQ, rows, warp, lane);
 
-  float o[kFHD];
+  float o[kFHD / 2];
 #pragma unroll
-  for (int d = 0; d < kFHD; ++d) o[d] = 0.0f;
-  float m_run = -INFINITY, l_run = 0.0f;
-  const uint32_t t_row = tbase + ((uint32_t)(warp * 32) << 16);  // this warp's tensor-memory lanes
+  for (int d = 0; d < kFHD / 2; ++d) o[d] = 0.0f;
+  float m_run = -INFINITY, l_half = 0.0f;  // running max (same in both halves), this half's sum
+  const uint32_t t_row = tbase + ((uint32_t)(quarter * 32) << 16);  // this warp's tensor-memory lanes
 
   for (int j = 0; j < n_tiles; ++j) {
     const int t0 = j * kFKV;
     const int nvalid = min(kFKV, kv_len - t0);
-    if (warp < 4) {
+    if (worker) {
       split_rows_kmajor(smem + kKVOff, 2 * kFKV * 128, K + (size_t)t0 * a.kvd, (size_t)a.kvd, kFKV, nvalid, warp,
                         lane);
       fence_proxy_async_smem();
     }
     __syncthreads();
     if (*abort_flag) break;
-    if (warp == 4 && lane == 0) {
+    if (tid == 0) {
       tc_fence_after();
       constexpr uint32_t idesc = idesc_bf16_f32_mn(kFQ, kFKV);
 #pragma unroll
@@ -198,34 +231,46 @@ __global__ void __launch_bounds__(kFThreads, 1) flash_prefill_kernel(const __gri
       tc_commit(s_full);
     }
     float alpha = 0.0f;
-    if (warp < 4) {
-      if (flash_wait(s_full, (uint32_t)(j & 1), a.err, abort_flag)) {
+    if (worker) {
+      // both warps of a pair meet at the exchange whatever their waits returned (no unbounded wait)
+      const bool ok = flash_wait(s_full, (uint32_t)(j & 1), a.err, abort_flag);
+      // this half's 32 scores of the row, loaded once (four loads, one wait); its maximum over the
+      // tile's valid positions, then the row's through the pair exchange
+      float sv[kFKV / 2];
+      float tmax = -INFINITY;
+      if (ok) {
         tc_fence_after();
-        // pass 1: this row's maximum over the tile's valid positions
-        float tmax = -INFINITY;
 #pragma unroll
-        for (int c0 = 0; c0 < kFKV; c0 += 8) {
-          float s[8];
-          tmem_ld8(t_row + (uint32_t)c0, s);
-          tmem_wait_ld();
+        for (int c0 = 0; c0 < kFKV / 2; c0 += 8) {
+          float s8[8];
+          tmem_ld8(t_row + (uint32_t)(sc0 + c0), s8);
 #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            if (t0 + c0 + i <= my_pos) tmax = fmaxf(tmax, __fmul_rn(s[i], a.scale));
+          for (int i = 0; i < 8; ++i) sv[c0 + i] = s8[i];
         }
+        tmem_wait_ld();
+#pragma unroll
+        for (int c0 = 0; c0 < kFKV / 2; c0 += 8) tmem_loaded(*reinterpret_cast<float(*)[8]>(&sv[c0]));
+#pragma unroll
+        for (int c = 0; c < kFKV / 2; ++c) {
+          sv[c] = __fmul_rn(sv[c], a.scale);
+          if (t0 + sc0 + c <= my_pos) tmax = fmaxf(tmax, sv[c]);
+        }
+      }
+      red[half * kFQ + row] = tmax;
+      pair_sync(quarter);
+      if (ok) {
+        tmax = fmaxf(tmax, red[(half ^ 1) * kFQ + row]);
         const float mnew = fmaxf(m_run, tmax);
-        // pass 2: weights, their sum, and their three bf16 planes (this thread's row of P)
+        // weights, this half's sum, and their three bf16 planes (columns sc0 .. of P's row)
         float tsum = 0.0f;
 #pragma unroll
-        for (int c0 = 0; c0 < kFKV; c0 += 8) {
-          float s[8];
-          tmem_ld8(t_row + (uint32_t)c0, s);
-          tmem_wait_ld();
+        for (int c0 = 0; c0 < kFKV / 2; c0 += 8) {
           uint16_t b[8][3];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             float pe = 0.0f;
-            if (t0 + c0 + i <= my_pos) {
-              float x = __fsub_rn(__fmul_rn(s[i], a.scale), mnew);
+            if (t0 + sc0 + c0 + i <= my_pos) {
+              float x = __fsub_rn(sv[c0 + i], mnew);
               if (!mpc) x = fminf(fmaxf(x, -40.0f), 40.0f);
               pe = expf(x);
             }
@@ -239,11 +284,11 @@ __global__ void __launch_bounds__(kFThreads, 1) flash_prefill_kernel(const __gri
             pk.y = (uint32_t)b[2][t] | ((uint32_t)b[3][t] << 16);
             pk.z = (uint32_t)b[4][t] | ((uint32_t)b[5][t] << 16);
             pk.w = (uint32_t)b[6][t] | ((uint32_t)b[7][t] << 16);
-            *reinterpret_cast<uint4*>(smem + kPOff + (size_t)t * kFQ * 128 + sw128_offset(tid, c0)) = pk;
+            *reinterpret_cast<uint4*>(smem + kPOff + (size_t)t * kFQ * 128 + sw128_offset(row, sc0 + c0)) = pk;
           }
         }
         alpha = (m_run == -INFINITY) ? 0.0f : expf(__fsub_rn(m_run, mnew));
-        l_run = __fmaf_rn(l_run, alpha, tsum);
+        l_half = __fmaf_rn(l_half, alpha, tsum);
         m_run = mnew;
         tc_fence_before();
         // the S MMAs have read the K planes: the same buffer takes V^T
@@ -253,7 +298,7 @@ __global__ void __launch_bounds__(kFThreads, 1) flash_prefill_kernel(const __gri
     }
     __syncthreads();
     if (*abort_flag) break;
-    if (warp == 4 && lane == 0) {
+    if (tid == 0) {
       tc_fence_after();
       constexpr uint32_t idesc = idesc_bf16_f32_mn(kFQ, kFHD);
 #pragma unroll
@@ -266,61 +311,72 @@ __global__ void __launch_bounds__(kFThreads, 1) flash_prefill_kernel(const __gri
       }
       tc_commit(pv_full);
     }
-    if (warp < 4) {
+    if (worker) {
       if (flash_wait(pv_full, (uint32_t)(j & 1), a.err, abort_flag)) {
         tc_fence_after();
 #pragma unroll
-        for (int c0 = 0; c0 < kFHD; c0 += 8) {
-          float pv[8];
-          tmem_ld8(t_row + kFColO + (uint32_t)c0, pv);
+        for (int c0 = 0; c0 < kFHD / 2; c0 += 32) {
+          float pv[4][8];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) tmem_ld8(t_row + kFColO + (uint32_t)(oc0 + c0 + 8 * u), pv[u]);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 8; ++i) o[c0 + i] = __fmaf_rn(o[c0 + i], alpha, pv[i]);
+          for (int u = 0; u < 4; ++u) tmem_loaded(pv[u]);
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[c0 + 8 * u + i] = __fmaf_rn(o[c0 + 8 * u + i], alpha, pv[u][i]);
         }
         tc_fence_before();
       }
     }
   }
 
-  // output row: O / L, reshared as (y - mask, mask)
-  if (warp < 4 && !*abort_flag && tid < rows) {
-    const int m = q0 + tid;
-    float* oc = a.Oc + (size_t)m * a.ldo + (size_t)hq * kFHD;
-    float* os = a.Os + (size_t)m * a.ldo + (size_t)hq * kFHD;
-    const float* mk = a.mask ? a.mask + (size_t)m * a.ldmask + (size_t)hq * kFHD : nullptr;
-    if (mpc && !(l_run > 1e-10f && isfinite(l_run))) {
-      // compute_mpc_attention_on_shares: weights 1/seq_len when the sum is not usable
-      const float invk = __fdiv_rn(1.0f, (float)(my_pos + 1));
-      for (int d = 0; d < kFHD; ++d) {
-        float u = 0.0f;
-        for (int t = 0; t <= my_pos; ++t) u = __fmaf_rn(invk, V[(size_t)t * a.kvd + d], u);
-        const float mv = mk ? mk[d] : 0.0f;
-        oc[d] = __fsub_rn(u, mv);
-        os[d] = mv;
-      }
-    } else {
+  // output row: O / L, reshared as (y - mask, mask); L = the two halves' sums
+  __syncthreads();  // every thread reads the same abort flag before the pair exchange
+  if (worker && !*abort_flag) {
+    red[half * kFQ + row] = l_half;
+    pair_sync(quarter);
+    const float l_run = __fadd_rn(red[row], red[kFQ + row]);
+    if (row < rows) {
+      const int m = q0 + row;
+      float* oc = a.Oc + (size_t)m * a.ldo + (size_t)hq * kFHD + oc0;
+      float* os = a.Os + (size_t)m * a.ldo + (size_t)hq * kFHD + oc0;
+      const float* mk = a.mask ? a.mask + (size_t)m * a.ldmask + (size_t)hq * kFHD + oc0 : nullptr;
+      if (mpc && !(l_run > 1e-10f && isfinite(l_run))) {
+        // compute_mpc_attention_on_shares: weights 1/seq_len when the sum is not usable
+        const float invk = __fdiv_rn(1.0f, (float)(my_pos + 1));
+        for (int d = 0; d < kFHD / 2; ++d) {
+          float u = 0.0f;
+          for (int t = 0; t <= my_pos; ++t) u = __fmaf_rn(invk, V[(size_t)t * a.kvd + oc0 + d], u);
+          const float mv = mk ? mk[d] : 0.0f;
+          oc[d] = __fsub_rn(u, mv);
+          os[d] = mv;
+        }
+      } else {
 #pragma unroll
-      for (int d = 0; d < kFHD; d += 4) {
-        float4 y, mv = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (mk) mv = *reinterpret_cast<const float4*>(mk + d);
-        y.x = __fsub_rn(__fdiv_rn(o[d], l_run), mv.x);
-        y.y = __fsub_rn(__fdiv_rn(o[d + 1], l_run), mv.y);
-        y.z = __fsub_rn(__fdiv_rn(o[d + 2], l_run), mv.z);
-        y.w = __fsub_rn(__fdiv_rn(o[d + 3], l_run), mv.w);
-        *reinterpret_cast<float4*>(oc + d) = y;
-        *reinterpret_cast<float4*>(os + d) = mv;
+        for (int d = 0; d < kFHD / 2; d += 4) {
+          float4 y, mv = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (mk) mv = *reinterpret_cast<const float4*>(mk + d);
+          y.x = __fsub_rn(__fdiv_rn(o[d], l_run), mv.x);
+          y.y = __fsub_rn(__fdiv_rn(o[d + 1], l_run), mv.y);
+          y.z = __fsub_rn(__fdiv_rn(o[d + 2], l_run), mv.z);
+          y.w = __fsub_rn(__fdiv_rn(o[d + 3], l_run), mv.w);
+          *reinterpret_cast<float4*>(oc + d) = y;
+          *reinterpret_cast<float4*>(os + d) = mv;
+        }
       }
     }
   }
   // every MMA issued has completed before tensor memory is released
-  if (warp == 4 && lane == 0) {
+  if (tid == 0) {
     tc_commit(done);
     if (!mbar_wait_bounded(done, 0)) atomicOr(a.err, SHD_DEVERR_TIMEOUT_DRAIN);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 4) tmem_dealloc(tbase, kFCols);
+  if (warp == 0) tmem_dealloc(tbase, kFCols);
 }
 
 }  // namespace

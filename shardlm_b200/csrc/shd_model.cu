@@ -32,7 +32,7 @@ using namespace shd;
 namespace {
 
 constexpr int kMaxRows = 8;        // decode batch (sequence slots stepped together)
-constexpr int kPrefillRows = 128;  // prompt positions per prefill chunk
+constexpr int kPrefillRows = 512;  // prompt positions per prefill chunk
 constexpr int kAttnWideRows = 4;   // from this many rows, attention groups of up to 8 q heads
 constexpr int kFlashRows = 16;     // prompt blocks of this many rows and more: tensor-core attention
 

@@ -76,6 +76,12 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// After tmem_wait_ld: ties 8 loaded values to a point after the wait, so that no use of them can be
+// scheduled between the asynchronous load and its wait.
+__device__ __forceinline__ void tmem_loaded(float (&v)[8]) {
+  asm volatile("" : "+f"(v[0]), "+f"(v[1]), "+f"(v[2]), "+f"(v[3]), "+f"(v[4]), "+f"(v[5]), "+f"(v[6]), "+f"(v[7]));
+}
+
 // Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, 8-row atoms 1024 bytes apart.
 // Within the 128-byte swizzle row, K step k (16 bf16) starts 32 bytes further: add 2 * k.
 __device__ __forceinline__ uint64_t smem_desc_sw128(const void* p) {
