@@ -356,10 +356,15 @@ extern "C" int shd_attn_decode(shd_ctx* ctx, const float* q, const float* k_cach
   const int cap = (M >= 4 && H / Hkv > kAttnGroup) ? 8 : kAttnGroup;
   const std::vector<int4> groups = attn_groups(0, H, 0, H / Hkv, cap);
   const int ng = (int)groups.size();
-  // per-call staging of groups and positions
+  // staging of groups and positions (the context's buffer: the call synchronizes before returning)
   int* d_meta = nullptr;
   const size_t meta_bytes = (size_t)ng * 16 + (size_t)M * 4;
-  SHD_CHECK_CUDA(ctx, cudaMallocAsync(&d_meta, meta_bytes, ctx->stream));
+  {
+    void* p = nullptr;
+    const int src = shd_stage(ctx, meta_bytes, &p);
+    if (src) return src;
+    d_meta = static_cast<int*>(p);
+  }
   std::vector<int> meta(meta_bytes / 4);
   std::memcpy(meta.data(), groups.data(), (size_t)ng * 16);
   for (int i = 0; i < M; ++i) meta[4 * ng + i] = pos_host[i];
@@ -386,7 +391,6 @@ extern "C" int shd_attn_decode(shd_ctx* ctx, const float* q, const float* k_cach
   a.group_cap = cap;
   a.err = ctx->d_err;
   int rc = launch_attention(ctx, a, M);
-  cudaFreeAsync(d_meta, ctx->stream);
   // the host staging vector must outlive the async copy
   cudaError_t e = cudaStreamSynchronize(ctx->stream);
   if (e != cudaSuccess) return shd_cuda_fail(ctx, e, "shd_attn_decode");
@@ -407,7 +411,12 @@ extern "C" int shd_attn_prefill(shd_ctx* ctx, const float* q, const float* k_cac
   const int ng = (int)groups.size();
   int* d_meta = nullptr;
   const size_t meta_bytes = (size_t)ng * 16 + 16;
-  SHD_CHECK_CUDA(ctx, cudaMallocAsync(&d_meta, meta_bytes, ctx->stream));
+  {
+    void* p = nullptr;
+    const int src = shd_stage(ctx, meta_bytes, &p);
+    if (src) return src;
+    d_meta = static_cast<int*>(p);
+  }
   std::vector<int> meta(meta_bytes / 4, 0);
   std::memcpy(meta.data(), groups.data(), (size_t)ng * 16);
   meta[4 * ng] = pos0;
@@ -435,7 +444,6 @@ extern "C" int shd_attn_prefill(shd_ctx* ctx, const float* q, const float* k_cac
   a.err = ctx->d_err;
   int rc = flash_prefill_supported(a, M) ? launch_flash_prefill(ctx, a, M)
                                          : shd_fail(ctx, SHD_ERR_ARG, "shd_attn_prefill: rows must be 16-byte aligned");
-  cudaFreeAsync(d_meta, ctx->stream);
   cudaError_t e = cudaStreamSynchronize(ctx->stream);
   if (e != cudaSuccess) return shd_cuda_fail(ctx, e, "shd_attn_prefill");
   return rc;

@@ -31,6 +31,8 @@ struct shd_ctx {
   int* d_counters = nullptr;     // per-tile arrival counters, left zero by every kernel
   int n_counters = 0;
   unsigned long long* d_scratch64 = nullptr;  // one word for synchronous result checks (encoders)
+  void* d_stage = nullptr;  // staging of the synchronous per-call entry points (metadata, OT queries)
+  size_t stage_bytes = 0;
   int num_sms = 148;
   int64_t launches = 0;
   // RoPE table (host-built with libm, as the reference's RopeFrequencies::new)
@@ -60,6 +62,9 @@ struct shd_ctx {
 
 int shd_fail(shd_ctx* ctx, int code, const std::string& msg);
 int shd_cuda_fail(shd_ctx* ctx, cudaError_t e, const char* what);
+// Device staging of at least `bytes` owned by the context, grown when needed (after the stream has
+// drained); for entry points that synchronize before returning, so calls never overlap on it.
+int shd_stage(shd_ctx* ctx, size_t bytes, void** out);
 
 #define SHD_CHECK_CUDA(ctx, call)                                    \
   do {                                                              \

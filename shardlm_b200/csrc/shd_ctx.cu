@@ -1,4 +1,5 @@
 // Context, error plumbing and weight tiling for libshardlm_cuda.
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <vector>
@@ -56,6 +57,20 @@ extern "C" int shd_init(int device, shd_ctx** out) {
   return SHD_OK;
 }
 
+int shd_stage(shd_ctx* ctx, size_t bytes, void** out) {
+  if (bytes > ctx->stage_bytes) {
+    SHD_CHECK_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    cudaFree(ctx->d_stage);
+    ctx->d_stage = nullptr;
+    ctx->stage_bytes = 0;
+    const size_t want = std::max<size_t>(bytes, 1 << 16);
+    SHD_CHECK_CUDA(ctx, cudaMalloc(&ctx->d_stage, want));
+    ctx->stage_bytes = want;
+  }
+  *out = ctx->d_stage;
+  return SHD_OK;
+}
+
 extern "C" int shd_destroy(shd_ctx* ctx) {
   if (!ctx) return SHD_OK;
   cudaSetDevice(ctx->device);
@@ -64,6 +79,7 @@ extern "C" int shd_destroy(shd_ctx* ctx) {
   cudaFree(ctx->d_partials);
   cudaFree(ctx->d_counters);
   cudaFree(ctx->d_scratch64);
+  cudaFree(ctx->d_stage);
   cudaFree(ctx->d_rope_cos);
   cudaFree(ctx->d_rope_sin);
   cudaFree(ctx->d_xpad);

@@ -403,7 +403,12 @@ extern "C" int shd_ot_process_query(shd_ctx* ctx, const uint8_t* commitment32, u
   uint8_t* d = nullptr;
   const size_t ent = (size_t)m * 20, outb = need, al = 256;
   const size_t bytes = (ent + al - 1) / al * al + (outb + al - 1) / al * al + al;
-  SHD_CHECK_CUDA(ctx, cudaMallocAsync(&d, bytes, ctx->stream));
+  {
+    void* p = nullptr;
+    const int src = shd_stage(ctx, bytes, &p);
+    if (src) return src;
+    d = static_cast<uint8_t*>(p);
+  }
   uint8_t* d_ent = d;
   uint8_t* d_out = d + (ent + al - 1) / al * al;
   unsigned int* d_bad = reinterpret_cast<unsigned int*>(d_out + (outb + al - 1) / al * al);
@@ -420,7 +425,6 @@ extern "C" int shd_ot_process_query(shd_ctx* ctx, const uint8_t* commitment32, u
   unsigned int bad = 0xffffffffu;
   if (e == cudaSuccess) e = cudaMemcpyAsync(response, d_out, outb, cudaMemcpyDeviceToHost, ctx->stream);
   if (e == cudaSuccess) e = cudaMemcpyAsync(&bad, d_bad, 4, cudaMemcpyDeviceToHost, ctx->stream);
-  cudaFreeAsync(d, ctx->stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
   if (e != cudaSuccess) return shd_cuda_fail(ctx, e, "shd_ot_process_query");
   if (bad != 0xffffffffu) {

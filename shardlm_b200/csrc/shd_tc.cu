@@ -63,12 +63,19 @@ struct TcArgs {
   PlaneOut out;  // EPI_GATEUP in the reduce kernel: the output as the next linear's planes
 };
 
+// Token tiles of up to 32 rows keep the three terms of a share side by side in tensor memory (one
+// MMA with N = 3 NT per share, terms summed in order by the epilogue). From 64 rows the terms
+// accumulate into one accumulator per share (three MMAs with N = NT): the weight tile is reused by
+// twice or four times the tokens per shared-memory fill, which is what limits this kernel at prompt
+// sizes (the operands stream from L2 at about 90 GB/s per SM); the sum then runs over 3 K products
+// per output instead of K, and its f32 rounding bound is that of 3 K terms.
 template <int NT>
 struct TcSmem {
+  static constexpr bool kFused = NT >= 64;
   static constexpr int kBBytes = 6 * NT * kTcBK * 2;
   static constexpr int kStage = kTcABytes + kBBytes;
-  static constexpr int kN = 3 * NT;      // MMA N per share: the three bf16 terms side by side
-  static constexpr int kBuf = 2 * kN;    // tensor-memory columns per accumulator buffer
+  static constexpr int kN = kFused ? NT : 3 * NT;  // MMA N per share
+  static constexpr int kBuf = 2 * kN;              // tensor-memory columns per accumulator buffer
 };
 
 __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag) {
@@ -186,27 +193,40 @@ __device__ __forceinline__ void tc_epi_value(const TcArgs& ta, int n, int m, boo
   }
 }
 
-// Epilogue of one accumulator buffer (columns: share, term, token): this thread owns weight row
-// r = 32 warp + lane of the tile. The three terms of a share are summed in order.
+// Epilogue of one accumulator buffer (columns: share, term, token; or share, token when the terms
+// accumulate together): this thread owns weight row r = 32 warp + lane of the tile. Side-by-side
+// terms of a share are summed in order.
 template <int NT>
 __device__ void tc_epilogue(const TcArgs& ta, uint32_t tacc, int row0, int tok0, int ks, int warp, int lane) {
   using L = TcSmem<NT>;
+  constexpr int Q = L::kFused ? 2 : 6;
   const int r = warp * 32 + lane;
   const int n = row0 + r;  // row in tile order
   const uint32_t tl = tacc + ((uint32_t)(warp * 32) << 16);
   const int ntok = min(NT, ta.M - tok0);
   const int rows_all = ta.n_row * kTcBM;
   for (int c0 = 0; c0 < NT; c0 += 8) {
-    float t[6][8];
+    float t[Q][8];
 #pragma unroll
-    for (int q = 0; q < 6; ++q) tmem_ld8(tl + (uint32_t)((q / 3) * L::kN + (q % 3) * NT + c0), t[q]);
+    for (int q = 0; q < Q; ++q) {
+      const uint32_t col = L::kFused ? (uint32_t)(q * L::kN + c0) : (uint32_t)((q / 3) * L::kN + (q % 3) * NT + c0);
+      tmem_ld8(tl + col, t[q]);
+    }
     tmem_wait_ld();
+#pragma unroll
+    for (int q = 0; q < Q; ++q) tmem_loaded(t[q]);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int m = tok0 + c0 + j;
       const bool live = (c0 + j < ntok);
-      const float yc = __fadd_rn(__fadd_rn(t[0][j], t[1][j]), t[2][j]);
-      const float ys = __fadd_rn(__fadd_rn(t[3][j], t[4][j]), t[5][j]);
+      float yc, ys;
+      if constexpr (L::kFused) {
+        yc = t[0][j];
+        ys = t[1][j];
+      } else {
+        yc = __fadd_rn(__fadd_rn(t[0][j], t[1][j]), t[2][j]);
+        ys = __fadd_rn(__fadd_rn(t[Q / 2][j], t[Q / 2 + 1][j]), t[Q / 2 + 2][j]);
+      }
       if (ta.ksplit > 1) {
         float* w = ta.ws + (((size_t)ks * ta.n_tok * NT + (size_t)(tok0 + c0 + j)) * rows_all + n) * 2;
         w[0] = yc;
@@ -314,7 +334,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const uint64_t ad = smem_desc_sw128(st);
 #pragma unroll
           for (int k = 0; k < kTcBK / 16; ++k) {
-            if constexpr (NT == 8) {
+            if constexpr (L::kFused) {
+              // three MMAs per share (one per term plane, N = NT) into the share's accumulator
+#pragma unroll
+              for (int sh = 0; sh < 2; ++sh)
+#pragma unroll
+                for (int t = 0; t < 3; ++t) {
+                  const uint64_t bd = smem_desc_sw128(st + kTcABytes + (size_t)(sh * 3 + t) * NT * kTcBK * 2);
+                  tc_mma(dacc + (uint32_t)(sh * L::kN), ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc,
+                         (kb > 0 || k > 0 || t > 0) ? 1u : 0u);
+                }
+            } else if constexpr (NT == 8) {
               // 3 NT = 24 is no valid N for M = 128: the six planes (48 consecutive rows) go through
               // ONE MMA with N = 48, whose columns sh * 3 NT + term * NT + token are the layout the
               // two per-share MMAs of wider tiles produce
@@ -382,7 +412,7 @@ constexpr int kTcReduceY = 4;
 template <int NT>
 __global__ void __launch_bounds__(kTcBM * kTcReduceY) tc_reduce_kernel(const __grid_constant__ TcArgs ta) {
   constexpr int JT = NT / kTcReduceY;
-  constexpr int KQ = 16 / JT;  // splits loaded together: 16 partial pairs in flight per thread
+  constexpr int KQ = JT >= 16 ? 1 : 16 / JT;  // splits loaded together: >= 16 partial pairs in flight
   pdl_wait();
   const int rt = blockIdx.x, tt = blockIdx.y;
   const int lane = threadIdx.x & 31;
@@ -670,7 +700,7 @@ int ensure_ws(shd_ctx* ctx, size_t floats) {
 
 }  // namespace
 
-int tc_token_tile(int M) { return M <= 8 ? 8 : (M <= 16 ? 16 : 32); }
+int tc_token_tile(int M) { return M <= 8 ? 8 : (M <= 16 ? 16 : (M <= 32 ? 32 : (M <= 64 ? 64 : 128))); }
 
 PlaneOut tc_input_planes(shd_ctx* ctx, const shd_weight* w, int M) {
   PlaneOut o{};
@@ -775,7 +805,9 @@ int launch_linear_tc(shd_ctx* ctx, const shd_weight* w, int M, int epi, GemvArgs
   const CUtensorMap& mw = *static_cast<const CUtensorMap*>(w->tmap);
   if (nt == 8) return launch_tc_t<8>(ctx, ta, mw, mx);
   if (nt == 16) return launch_tc_t<16>(ctx, ta, mw, mx);
-  return launch_tc_t<32>(ctx, ta, mw, mx);
+  if (nt == 32) return launch_tc_t<32>(ctx, ta, mw, mx);
+  if (nt == 64) return launch_tc_t<64>(ctx, ta, mw, mx);
+  return launch_tc_t<128>(ctx, ta, mw, mx);
 }
 
 void free_weight_map(shd_weight* w) {

@@ -2,7 +2,9 @@
 
 Tolerance: the GPU sums the K products of an output in a different order than the reference's
 sequential i-outer loop, so results agree within the f32 summation bound
-2 * gamma_K * sum_i |x_i||W_ij| (conftest.f32_sum_tolerance), per share, for every element.
+2 * gamma_K * sum_i |x_i||W_ij| (conftest.f32_sum_tolerance), per share, for every element. From 33
+rows the tensor-core linear accumulates the three bf16 terms of each activation in one f32
+accumulator, a sum of 3K exact products: the bound is then 2 * gamma_3K * sum_i |x_i||W_ij|.
 """
 import numpy as np
 import pytest
@@ -23,16 +25,22 @@ def _case(rng, K, N, M, with_bias):
     return w_u16, xc, xs, b
 
 
+def _terms(M):
+    """Products summed per output: K, or 3K when the tensor-core linear fuses the terms (M > 32)."""
+    return 3 if M > 32 else 1
+
+
 def _check(orc, w_u16, xc, xs, b, yc, ys, residual=None):
     N, K = w_u16.shape
+    KS = K * _terms(xc.shape[0])
     w_in_out = np.ascontiguousarray(w_u16.T)
     oc, os_ = orc.linear_bf16(w_in_out, b, xc, xs)
     if residual is not None:
         oc = (oc + residual[0]).astype(np.float32)
         os_ = (os_ + residual[1]).astype(np.float32)
     for m in range(xc.shape[0]):
-        tc = f32_sum_tolerance(K, orc.linear_abs_bf16(w_in_out, xc[m]))
-        ts = f32_sum_tolerance(K, orc.linear_abs_bf16(w_in_out, xs[m]))
+        tc = f32_sum_tolerance(KS, orc.linear_abs_bf16(w_in_out, xc[m]))
+        ts = f32_sum_tolerance(KS, orc.linear_abs_bf16(w_in_out, xs[m]))
         if b is not None:
             ts = ts + np.abs(b) * 2 ** -23
         if residual is not None:
@@ -54,10 +62,11 @@ def _check(orc, w_u16, xc, xs, b, yc, ys, residual=None):
     (520, 4100, 5, False),     # 5 rows, ragged K
     (3584, 3584, 8, True),     # 8 rows, 7B o shape
     (18944, 3584, 6, False),   # 6 rows, 7B down shape: split K and the reduce kernel
-    (3584, 4608, 64, True),    # 7B q/k/v shape, one 64-row token tile
+    (3584, 4608, 64, True),    # 7B q/k/v shape, one 64-row token tile (terms fused)
     (1000, 77, 9, True),       # ragged N and K, 16-row token tile
     (18944, 3584, 33, False),  # 7B down shape
-    (1536, 1536, 130, True),   # three 64-row token tiles, ragged last
+    (1536, 1536, 130, True),   # two 128-row token tiles (terms fused), ragged last
+    (1000, 700, 200, True),    # 128-row token tiles, ragged N, K and M
     (4, 2, 17, True),          # tiny
 ])
 def test_linear_dual_f32_matches_oracle(ctx, orc, K, N, M, bias):
