@@ -48,6 +48,8 @@ struct shd_ctx {
   // bf16 activation planes of the tensor-core linear
   void* d_tc_planes = nullptr;
   size_t tc_planes_elems = 0;
+  void* d_tc_planes_next = nullptr;  // planes a producer writes for the next linear while this one reads
+  size_t tc_planes_next_elems = 0;
   float* d_tc_ws = nullptr;  // split-K partial sums of the tensor-core linear
   size_t tc_ws_floats = 0;
   // NCCL (tensor parallelism), loaded at run time

@@ -84,6 +84,7 @@ extern "C" int shd_destroy(shd_ctx* ctx) {
   cudaFree(ctx->d_rope_sin);
   cudaFree(ctx->d_xpad);
   cudaFree(ctx->d_tc_planes);
+  cudaFree(ctx->d_tc_planes_next);
   cudaFree(ctx->d_tc_ws);
   delete ctx;
   return SHD_OK;

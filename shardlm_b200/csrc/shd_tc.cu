@@ -482,6 +482,49 @@ __global__ void split_planes_kernel(const float* __restrict__ xc, const float* _
   }
 }
 
+// The same with 8 physical columns per thread (two float4 loads per share, one 16-byte store per
+// plane): rows 16-byte aligned (ldx % 4 == 0, aligned bases) and K a multiple of 256.
+__global__ void split_planes_vec_kernel(const float* __restrict__ xc, const float* __restrict__ xs, int ldx, int M,
+                                        int Mp, int KP, uint16_t* __restrict__ out) {
+  pdl_wait();  // the shares come from the previous kernel
+  const size_t plane = (size_t)Mp * KP;
+  const long long groups = (long long)Mp * (KP / 8);
+  for (long long g = blockIdx.x * (long long)blockDim.x + threadIdx.x; g < groups;
+       g += (long long)gridDim.x * blockDim.x) {
+    const int m = (int)(g / (KP / 8)), j = (int)(g % (KP / 8)) * 8;
+    const int c = j >> 8, l = (j & 255) >> 3;
+    const int col0 = c * 256 + 4 * l, col1 = col0 + 128;  // physical j..j+3 <- col0.., j+4..j+7 <- col1..
+    float v[2][8];
+#pragma unroll
+    for (int sh = 0; sh < 2; ++sh) {
+      const float* x = sh ? xs : xc;
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+      if (m < M) {
+        a = *reinterpret_cast<const float4*>(x + (size_t)m * ldx + col0);
+        b = *reinterpret_cast<const float4*>(x + (size_t)m * ldx + col1);
+      }
+      v[sh][0] = a.x; v[sh][1] = a.y; v[sh][2] = a.z; v[sh][3] = a.w;
+      v[sh][4] = b.x; v[sh][5] = b.y; v[sh][6] = b.z; v[sh][7] = b.w;
+    }
+    const size_t at = (size_t)m * KP + j;
+#pragma unroll
+    for (int sh = 0; sh < 2; ++sh) {
+      uint16_t t[8][3];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) split3(v[sh][i], t[i]);
+#pragma unroll
+      for (int q = 0; q < 3; ++q) {
+        uint4 pk;
+        pk.x = (uint32_t)t[0][q] | ((uint32_t)t[1][q] << 16);
+        pk.y = (uint32_t)t[2][q] | ((uint32_t)t[3][q] << 16);
+        pk.z = (uint32_t)t[4][q] | ((uint32_t)t[5][q] << 16);
+        pk.w = (uint32_t)t[6][q] | ((uint32_t)t[7][q] << 16);
+        *reinterpret_cast<uint4*>(out + (size_t)(sh * 3 + q) * plane + at) = pk;
+      }
+    }
+  }
+}
+
 // Logical column of physical plane column j (the weight blocks' column permutation).
 __device__ __forceinline__ int plane_col(int j) {
   const int c = j >> 8, jj = j & 255;
@@ -653,14 +696,26 @@ int planes_map(shd_ctx* ctx, const uint16_t* planes, int Mp, int KP, int nt, CUt
   return SHD_OK;
 }
 
-int ensure_planes(shd_ctx* ctx, size_t elems) {
-  if (ctx->tc_planes_elems >= elems) return SHD_OK;
-  if (ctx->d_tc_planes) cudaFree(ctx->d_tc_planes);
-  ctx->d_tc_planes = nullptr;
-  ctx->tc_planes_elems = 0;
-  SHD_CHECK_CUDA(ctx, cudaMalloc(&ctx->d_tc_planes, elems * 2));
-  ctx->tc_planes_elems = elems;
+int ensure_buffer(shd_ctx* ctx, void** buf, size_t* have, size_t elems) {
+  if (*have >= elems) return SHD_OK;
+  if (*buf) {
+    SHD_CHECK_CUDA(ctx, cudaStreamSynchronize(ctx->stream));  // earlier launches may still read it
+    cudaFree(*buf);
+  }
+  *buf = nullptr;
+  *have = 0;
+  SHD_CHECK_CUDA(ctx, cudaMalloc(buf, elems * 2));
+  *have = elems;
   return SHD_OK;
+}
+
+// The planes this linear computes and reads; and the planes a producer writes for the linear after
+// it (tc_input_planes), in a second buffer so that the producer's writes never meet its own reads.
+int ensure_planes(shd_ctx* ctx, size_t elems) {
+  return ensure_buffer(ctx, &ctx->d_tc_planes, &ctx->tc_planes_elems, elems);
+}
+int ensure_next_planes(shd_ctx* ctx, size_t elems) {
+  return ensure_buffer(ctx, &ctx->d_tc_planes_next, &ctx->tc_planes_next_elems, elems);
 }
 
 template <int NT>
@@ -707,8 +762,8 @@ PlaneOut tc_input_planes(shd_ctx* ctx, const shd_weight* w, int M) {
   if (M <= 0 || w->kind != WK_BF16 || !tc_preferred(w, M)) return o;
   if (M % tc_token_tile(M) != 0 || w->K % kChunkBf16 != 0) return o;
   const int KP = w->nKC * kChunkBf16;
-  if (ensure_planes(ctx, (size_t)6 * M * KP) != SHD_OK) return o;
-  o.p = reinterpret_cast<uint16_t*>(ctx->d_tc_planes);
+  if (ensure_next_planes(ctx, (size_t)6 * M * KP) != SHD_OK) return o;
+  o.p = reinterpret_cast<uint16_t*>(ctx->d_tc_planes_next);
   o.Mp = M;
   o.KP = KP;
   return o;
@@ -725,17 +780,21 @@ int launch_linear_tc(shd_ctx* ctx, const shd_weight* w, int M, int epi, GemvArgs
   const int n_tok = (M + nt - 1) / nt;
   const int Mp = n_tok * nt;
   const int KP = w->nKC * kChunkBf16;
-  if ((rc = ensure_planes(ctx, (size_t)6 * Mp * KP))) return rc;
-  uint16_t* planes = reinterpret_cast<uint16_t*>(ctx->d_tc_planes);
+  // planes written by the producer of this linear's input (tc_input_planes) are read where it wrote
+  // them; otherwise this launch computes its planes into the context's own buffer
+  if (!planes_ready && (rc = ensure_planes(ctx, (size_t)6 * Mp * KP))) return rc;
+  uint16_t* planes = reinterpret_cast<uint16_t*>(planes_ready ? ctx->d_tc_planes_next : ctx->d_tc_planes);
   if (planes_ready) {
-    if (Mp != M || KP != w->K) return shd_fail(ctx, SHD_ERR_ARG, "tensor-core linear: planes written for another shape");
+    if (Mp != M || KP != w->K || ctx->tc_planes_next_elems < (size_t)6 * Mp * KP)
+      return shd_fail(ctx, SHD_ERR_ARG, "tensor-core linear: planes written for another shape");
   } else if (norm) {
     if (norm->n != w->K) return shd_fail(ctx, SHD_ERR_ARG, "tensor-core linear: norm width != in_features");
-    // every CTA of a row reloads the whole row for its sum: slices of one column per thread (at
-    // least one 256-column chunk), so the planes pass keeps all threads busy
+    // every CTA of a row reloads the whole row for its sum: with few rows, slices of one column per
+    // thread (at least one 256-column chunk) keep the SMs busy; with a row per SM or more (prompt
+    // chunks), one CTA per row writes all its planes and the row is read once
     const int n_chunks = w->nKC;
     const int threads = norm->n >= 4096 ? 1024 : (norm->n >= 1024 ? 512 : 128);  // as launch_norm
-    const int cps = std::max(1, threads / 256);
+    const int cps = Mp >= ctx->num_sms ? n_chunks : std::max(1, threads / 256);
     const int slices = (n_chunks + cps - 1) / cps;
     const size_t smem = (size_t)norm->n * 4;
     static unsigned attr_devices = 0;
@@ -746,6 +805,12 @@ int launch_linear_tc(shd_ctx* ctx, const shd_weight* w, int M, int epi, GemvArgs
     if (smem > 200 * 1024) return shd_fail(ctx, SHD_ERR_ARG, "tensor-core linear: norm row too long");
     SHD_CHECK_CUDA(ctx, launch_pdl(norm_planes_kernel, dim3(Mp, slices), dim3(threads), smem, ctx->stream, *norm, M, Mp,
                                    KP, cps, planes));
+    ctx->launches++;
+  } else if (g.ldx % 4 == 0 && w->K % kChunkBf16 == 0 && shd_aligned16(g.Xc) && shd_aligned16(g.Xs)) {
+    const long long groups = (long long)Mp * (KP / 8);
+    const int blocks = (int)std::min<long long>((groups + 255) / 256, 8LL * ctx->num_sms);
+    SHD_CHECK_CUDA(ctx, launch_pdl(split_planes_vec_kernel, dim3(blocks), dim3(256), 0, ctx->stream, g.Xc, g.Xs,
+                                   g.ldx, M, Mp, KP, planes));
     ctx->launches++;
   } else {
     const long long total = (long long)Mp * KP;
@@ -796,11 +861,12 @@ int launch_linear_tc(shd_ctx* ctx, const shd_weight* w, int M, int epi, GemvArgs
   if (ta.ksplit > 1) {
     if ((rc = ensure_ws(ctx, (size_t)ta.ksplit * n_tok * nt * ta.n_row * kTcBM * 2))) return rc;
     ta.ws = ctx->d_tc_ws;
-    // the epilogue runs in the reduce kernel, after this linear has read its planes
-    if (out_planes && out_planes->p && epi == EPI_GATEUP) {
-      ta.out = *out_planes;
-      if (wrote_out) *wrote_out = true;
-    }
+  }
+  // the SwiGLU output as the next linear's planes, from the epilogue (in the reduce kernel when K is
+  // split); they go to the second plane buffer, so this launch's own planes stay intact
+  if (out_planes && out_planes->p && epi == EPI_GATEUP && out_planes->p != planes) {
+    ta.out = *out_planes;
+    if (wrote_out) *wrote_out = true;
   }
   const CUtensorMap& mw = *static_cast<const CUtensorMap*>(w->tmap);
   if (nt == 8) return launch_tc_t<8>(ctx, ta, mw, mx);
