@@ -104,6 +104,7 @@ SIGNATURES: dict[str, tuple] = {
     "shd_model_step_launches": (I64, [P]),
     "shd_model_set_profiling": (I32, [P, I32]),
     "shd_model_linear_times": (I32, [P, P, P]),
+    "shd_model_timeline": (I32, [P, I32, P, P, P]),
 }
 
 

@@ -191,6 +191,27 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// Launch timeline (a diagnostic of the captured decode step): each traced launch owns 8 u64 of a
+// buffer preset to all ones; every field is an atomic minimum of %globaltimer, the "last" fields of
+// its complement, so one launch records its first and last CTA at each point:
+//   0 first CTA entry, 1 last CTA entry, 2 first return from the wait on the previous kernel,
+//   3 last end of the prologue (the wait, plus the fused norm where there is one), 4 first exit,
+//   5 last exit.
+enum TraceField { TR_ENTRY = 0, TR_WAIT = 2, TR_READY = 3, TR_EXIT = 4 };
+__device__ __forceinline__ void trace_first(unsigned long long* tr, int f) {
+  if (tr) atomicMin(tr + f, (unsigned long long)globaltimer_ns());
+}
+__device__ __forceinline__ void trace_last(unsigned long long* tr, int f) {
+  if (tr) atomicMin(tr + f, ~(unsigned long long)globaltimer_ns());
+}
+__device__ __forceinline__ void trace_both(unsigned long long* tr, int f) {
+  if (tr) {
+    const unsigned long long t = globaltimer_ns();
+    atomicMin(tr + f, t);
+    atomicMin(tr + f + 1, ~t);
+  }
+}
+
 #ifdef __CUDACC__
 template <typename... KArgs, typename... Args>
 static inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,

@@ -146,7 +146,10 @@ __global__ void __launch_bounds__(kGemvThreads, MINB) gemv_f32_kernel(const __gr
     mbar_fence_init();
   }
   __syncthreads();
-  if (threadIdx.x == 0) pdl_trigger();
+  if (threadIdx.x == 0) {
+    pdl_trigger();
+    trace_both(a.trace, TR_ENTRY);
+  }
 
   if (warp == kConsumerWarps) {
     gemv_producer<M, kChunkBf16, float>(sm, a.W, a.Xc, a.Xs, a.ldx, a.K, a.nKC, u0, u1, !NORM, a.err, lane);
@@ -158,6 +161,7 @@ __global__ void __launch_bounds__(kGemvThreads, MINB) gemv_f32_kernel(const __gr
   NormGamma ngam;
   if constexpr (NORM) norm_gamma_preload(a, ctid, ngam);
   pdl_wait();  // activations, positions and scratch come from earlier kernels
+  if (ctid == 0) trace_first(a.trace, TR_WAIT);
   if constexpr (NORM) {
     if (!norm_prologue<M>(a, sm, cphase, xres, KP, ctid, lane, warp, g == 0, &ngam)) {
       if (lane == 0) atomicOr(a.err, SHD_DEVERR_TIMEOUT_FULL);
@@ -165,6 +169,7 @@ __global__ void __launch_bounds__(kGemvThreads, MINB) gemv_f32_kernel(const __gr
       return;
     }
   }
+  if (ctid == 0) trace_last(a.trace, TR_READY);
 
   const int first_tile = (int)(u0 / a.nKC);
   unsigned long long acc2[USE2 ? V : 1];
@@ -242,6 +247,7 @@ __global__ void __launch_bounds__(kGemvThreads, MINB) gemv_f32_kernel(const __gr
       return;
     }
   }
+  if (ctid == 0) trace_both(a.trace, TR_EXIT);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -403,9 +409,6 @@ static int set_smem_attr(shd_ctx* ctx, Kern kernel, unsigned& devices) {
   return SHD_OK;
 }
 
-// Two CTAs per SM (one streams while the other is in its prologue, split-tile exchange or
-// epilogue) when at least 4 stages fit in half the shared memory and M <= 2 keeps the registers
-// under the two-CTA limit; otherwise one CTA per SM.
 // Grid of a GEMV launch. Stream-K over min(U, per_sm * SMs) CTAs in general; when the weight has at
 // most per_sm * SMs row tiles of at most 16 chunks (256 KB), one CTA per tile instead: every CTA
 // then streams whole tiles and no tile is split, which removes the split-tile exchange from the
@@ -416,34 +419,60 @@ static int gemv_grid(const shd_ctx* ctx, const shd_weight* w, long long U, int p
   return (int)std::min<long long>(U, cap);
 }
 
-template <int M, int EPI, bool NORM>
-static int launch_f32_t(shd_ctx* ctx, const shd_weight* w, GemvArgs a) {
-  static unsigned attr1 = 0, attr2 = 0;
-  const int stage = kBlockBytes + (NORM ? 0 : M * 2 * kChunkBf16 * 4);
-  const size_t xres = NORM ? (size_t)M * 2 * w->nKC * kChunkBf16 * 4 : 0;
+// Launch shape of the f32-share GEMV for M rows of `w` (with or without the fused norm).
+// Two CTAs per SM (one streams while the other is in its prologue, split-tile exchange or
+// epilogue) when at least 4 stages fit in half the shared memory and M <= 2 keeps the registers
+// under the two-CTA limit; otherwise one CTA per SM.
+// At most one tile per SM: one CTA per SM, with as many stages as the tile has chunks (or as fit
+// in shared memory). The whole tile is then in flight at once and most of it loads before the
+// wait on the previous kernel, instead of paying one memory latency per 6 chunks after it.
+// (Loading the activations whole after the wait, instead of with every block, measured slower:
+// the first block then waits for the whole vector.)
+// Fewer row tiles than half the SMs (the q/k/v slice of a tensor-parallel rank): one tile per CTA
+// would leave most SMs idle and stream a whole tile through each busy one, so the (tile, chunk)
+// units are spread over one CTA per SM instead, every unit of a CTA in flight at once, and the
+// split tiles are finished by their owners.
+GemvPlan gemv_plan(const shd_ctx* ctx, const shd_weight* w, int M, bool norm) {
+  GemvPlan p{};
+  const int stage = kBlockBytes + (norm ? 0 : M * 2 * kChunkBf16 * 4);
+  const size_t xres = norm ? (size_t)M * 2 * w->nKC * kChunkBf16 * 4 : 0;
   const long long U = (long long)w->nT * w->nKC;
   const long long s2 = ((long long)kSmemPerCta2 - kTailBytes - (long long)xres) / stage;
   const long long s1 = ((long long)kSmemLimit - kTailBytes - (long long)xres) / stage;
-  // At most one tile per SM: one CTA per SM, with as many stages as the tile has chunks (or as fit
-  // in shared memory). The whole tile is then in flight at once and most of it loads before the
-  // wait on the previous kernel, instead of paying one memory latency per 6 chunks after it.
-  // (Loading the activations whole after the wait, instead of with every block, measured slower:
-  // the first block then waits for the whole vector.)
-  // Fewer row tiles than half the SMs (the q/k/v slice of a tensor-parallel rank): one tile per CTA
-  // would leave most SMs idle and stream a whole tile through each busy one, so the (tile, chunk)
-  // units are spread over one CTA per SM instead, every unit of a CTA in flight at once, and the
-  // split tiles are finished by their owners.
   const bool few_tiles = 2 * (long long)w->nT < ctx->num_sms && w->nKC >= 4 && s1 >= 2;
   const bool deep_tiles = !few_tiles && w->nT <= ctx->num_sms && w->nKC <= 16 &&
                           s1 >= std::min<long long>(w->nKC, 8);
+  p.U = U;
+  if (M <= 2 && s2 >= 4 && !deep_tiles && !few_tiles) {
+    p.per_sm = 2;
+    p.nstages = (int)std::min<long long>(kMaxStages, s2);
+    p.G = gemv_grid(ctx, w, U, 2);
+  } else {
+    p.per_sm = 1;
+    p.G = gemv_grid(ctx, w, U, 1);
+    long long want = deep_tiles ? std::max(w->nKC, 2) : kMaxStages;
+    if (few_tiles) {
+      p.G = (int)std::min<long long>(U, ctx->num_sms);
+      want = std::max<long long>((U + p.G - 1) / p.G, 2);
+    }
+    p.nstages = (int)std::min<long long>(want, s1);
+  }
+  p.smem = (size_t)p.nstages * stage + xres + kTailBytes;
+  return p;
+}
+
+template <int M, int EPI, bool NORM>
+static int launch_f32_t(shd_ctx* ctx, const shd_weight* w, GemvArgs a) {
+  static unsigned attr1 = 0, attr2 = 0;
+  const GemvPlan p = gemv_plan(ctx, w, M, NORM);
+  if (p.nstages < 2) return shd_fail(ctx, SHD_ERR_ARG, "gemv: activation vector too long for the fused norm");
+  a.nstages = p.nstages;
   if constexpr (M <= 2) {
-    if (s2 >= 4 && !deep_tiles && !few_tiles) {
+    if (p.per_sm == 2) {
       const int rc = set_smem_attr(ctx, gemv_f32_kernel<M, EPI, NORM, 2>, attr2);
       if (rc) return rc;
-      a.nstages = (int)std::min<long long>(kMaxStages, s2);
-      const size_t smem = (size_t)a.nstages * stage + xres + kTailBytes;
-      const int G = gemv_grid(ctx, w, U, 2);
-      SHD_CHECK_CUDA(ctx, launch_pdl(gemv_f32_kernel<M, EPI, NORM, 2>, dim3(G), dim3(kGemvThreads), smem, ctx->stream, a));
+      SHD_CHECK_CUDA(ctx, launch_pdl(gemv_f32_kernel<M, EPI, NORM, 2>, dim3(p.G), dim3(kGemvThreads), p.smem,
+                                     ctx->stream, a));
       ctx->launches++;
       return SHD_OK;
     }
@@ -451,16 +480,8 @@ static int launch_f32_t(shd_ctx* ctx, const shd_weight* w, GemvArgs a) {
   (void)attr2;
   const int rc = set_smem_attr(ctx, gemv_f32_kernel<M, EPI, NORM, 1>, attr1);
   if (rc) return rc;
-  int G = gemv_grid(ctx, w, U, 1);
-  long long want = deep_tiles ? std::max(w->nKC, 2) : kMaxStages;
-  if (few_tiles) {
-    G = (int)std::min<long long>(U, ctx->num_sms);
-    want = std::max<long long>((U + G - 1) / G, 2);
-  }
-  a.nstages = (int)std::min<long long>(want, s1);
-  if (a.nstages < 2) return shd_fail(ctx, SHD_ERR_ARG, "gemv: activation vector too long for the fused norm");
-  const size_t smem = (size_t)a.nstages * stage + xres + kTailBytes;
-  SHD_CHECK_CUDA(ctx, launch_pdl(gemv_f32_kernel<M, EPI, NORM, 1>, dim3(G), dim3(kGemvThreads), smem, ctx->stream, a));
+  SHD_CHECK_CUDA(ctx, launch_pdl(gemv_f32_kernel<M, EPI, NORM, 1>, dim3(p.G), dim3(kGemvThreads), p.smem,
+                                 ctx->stream, a));
   ctx->launches++;
   return SHD_OK;
 }

@@ -99,13 +99,24 @@ struct GemvArgs {
   // receive kernel of the same call sums the sources.
   uint8_t* tp_peer[8];
   int tp_me, tp_world;
+  unsigned long long* trace;  // launch timeline slot (nullable; TraceField in shd_common.cuh)
 };
+
+// Launch shape of the f32-share GEMV (what launch_gemv_f32 will launch for these rows).
+struct GemvPlan {
+  int per_sm;     // CTAs per SM (1 or 2)
+  int G;          // CTAs
+  int nstages;    // pipeline stages of 16 KB weight blocks
+  long long U;    // (tile, chunk) units, CTA g taking [U g / G, U (g + 1) / G)
+  size_t smem;
+};
+GemvPlan gemv_plan(const shd_ctx* ctx, const shd_weight* w, int M, bool norm);
 
 // Launch the f32-share GEMV for M rows with the given epilogue; `norm` selects the fused RMSNorm
 // prologue (x from nHc/nHs/...) instead of staged activations (Xc/Xs).
 int launch_gemv_f32(shd_ctx* ctx, const shd_weight* w, int M, int epi, GemvArgs a, bool norm = false);
 // Fill the weight, shape and scratch fields of `a` for `w` (what launch_gemv_f32 adds before a
-// launch); the persistent step kernel records jobs with it.
+// launch; the tensor-core linear uses it for its split-K scratch too).
 int gemv_prepare(shd_ctx* ctx, const shd_weight* w, GemvArgs& a, bool norm);
 
 struct RingArgs {

@@ -234,6 +234,7 @@ extern "C" int shd_model_create(shd_ctx* ctx, const shd_model_config* cfg, shd_m
 shd_model::~shd_model() {
   if (graph) cudaGraphExecDestroy(graph);
   for (cudaEvent_t ev : prof_events) cudaEventDestroy(ev);
+  cudaFree(d_trace);
   for (auto& L : layers) {
     shd_weight_destroy(L.qkv);
     shd_weight_destroy(L.o);
@@ -408,15 +409,18 @@ extern "C" int shd_model_reset(shd_model* m) {
 // Hbuf[0] and a zero D. Leaves the final residual in (Hbuf[cur], D) for the head.
 // ------------------------------------------------------------------------------------------------
 // RMSNorm of (D + H) feeding a GEMV: fused into the GEMV prologue when the M normalized rows fit in
-// shared memory next to the weight pipeline, else a separate norm kernel writes Xbuf.
+// shared memory next to the weight pipeline, else a separate norm kernel writes Xbuf (the
+// tensor-core path computes it in its plane split).
+static bool norm_fusable(const shd_weight* w, int M) {
+  return (size_t)M * 2 * w->nKC * kChunkBf16 * 4 <= 120 * 1024 && !tc_preferred(w, M);
+}
+
 int shd_model::norm_into(GemvArgs& g, const shd_weight* w, int M, const float* Hc, const float* Hs,
                          const float* Dc, const float* Ds, float* Oc, float* Os, const float* gamma,
                          int variant, const float* mask, bool& fused) {
   const int h = cfg.hidden;
   has_pend_norm = false;
-  // fused into the GEMV when its activations fit the CTA; the tensor-core path computes it in its
-  // plane split
-  fused = (size_t)M * 2 * w->nKC * kChunkBf16 * 4 <= 120 * 1024 && !tc_preferred(w, M);
+  fused = norm_fusable(w, M);
   if (fused) {
     g.nHc = Hc; g.nHs = Hs; g.nDc = Dc; g.nDs = Ds; g.nHout_c = Oc; g.nHout_s = Os; g.n_ldh = h;
     g.gamma = gamma; g.eps = cfg.rms_eps; g.nvariant = variant; g.nmask = mask; g.n_ldmask = 0;
@@ -475,6 +479,7 @@ int shd_model::enqueue_layers(int M, const int* d_pos, const int* d_seq, int var
     g.Q = Qbuf; g.ldq = qd;
     g.Kcache = kcache + (size_t)l * kv_layer; g.Vcache = vcache + (size_t)l * kv_layer;
     g.kv_seq_stride = (int64_t)c.max_seq * kvd;
+    g.trace = trace_slot(0);
     if ((rc = prof_mark(0, Lw.qkv, true))) return rc;
     if ((rc = op_gemv(Lw.qkv, M, EPI_QKV, g, fused))) return rc;
     if ((rc = prof_mark(0, Lw.qkv, false))) return rc;
@@ -494,6 +499,7 @@ int shd_model::enqueue_layers(int M, const int* d_pos, const int* d_seq, int var
       at.n_groups = n_groups8;
       at.group_cap = 8;
     }
+    at.trace = trace_slot(5);
     if ((rc = prof_mark(5, nullptr, true))) return rc;
     if (!decode && M >= kFlashRows && flash_prefill_supported(at, M))
       rc = launch_flash_prefill(ctx, at, M);  // a prompt block: consecutive positions of one slot
@@ -506,6 +512,7 @@ int shd_model::enqueue_layers(int M, const int* d_pos, const int* d_seq, int var
     go.Xc = Abuf; go.Xs = Abuf + (size_t)M * qd; go.ldx = qd;
     go.Yc = Dbuf; go.Ys = Dbuf + (size_t)M * h; go.ldy = h;
     const bool push_o = tp_push(go, Lw.o, M, (size_t)2 * M * h);
+    go.trace = trace_slot(1);
     if ((rc = prof_mark(1, Lw.o, true))) return rc;
     if ((rc = op_gemv(Lw.o, M, EPI_STORE, go, false))) return rc;
     if ((rc = prof_mark(1, Lw.o, false))) return rc;
@@ -518,6 +525,7 @@ int shd_model::enqueue_layers(int M, const int* d_pos, const int* d_seq, int var
     gu.Yc = ACTbuf; gu.Ys = ACTbuf + (size_t)M * I; gu.ldy = I;
     gu.variant = variant;
     gu.mask = lm ? lm + 3 * (size_t)h + sh.inter_begin : nullptr; gu.ldmask = 0;
+    gu.trace = trace_slot(2);
     if ((rc = prof_mark(2, Lw.gateup, true))) return rc;
     // gate/up with split K writes its output as the down linear's planes from the reduce kernel
     const PlaneOut d_planes = fused ? PlaneOut{} : tc_input_planes(ctx, Lw.down, M);
@@ -531,6 +539,7 @@ int shd_model::enqueue_layers(int M, const int* d_pos, const int* d_seq, int var
     gd.Xc = ACTbuf; gd.Xs = ACTbuf + (size_t)M * I; gd.ldx = I;
     gd.Yc = Dbuf; gd.Ys = Dbuf + (size_t)M * h; gd.ldy = h;
     const bool push_d = tp_push(gd, Lw.down, M, (size_t)2 * M * h);
+    gd.trace = trace_slot(3);
     if ((rc = prof_mark(3, Lw.down, true))) return rc;
     if ((rc = down_ready ? launch_linear_tc(ctx, Lw.down, M, EPI_STORE, gd, nullptr, true)
                          : op_gemv(Lw.down, M, EPI_STORE, gd, false)))
@@ -573,6 +582,7 @@ int shd_model::enqueue_head_rows(int M, int cur, int variant) {
   if (rc) return rc;
   g.amax = amax;
   g.idx_offset = sh.vocab_begin;
+  g.trace = trace_slot(4);
   if ((rc = prof_mark(4, lm_head, true))) return rc;
   if ((rc = op_gemv(lm_head, M, EPI_LOGITS, g, fused))) return rc;
   return prof_mark(4, lm_head, false);
@@ -781,6 +791,13 @@ extern "C" int shd_model_decode_async(shd_model* m, int n_steps) {
         m->prof_events.push_back(ev);
       }
     }
+    if (rc == SHD_OK && m->profiling == 2 && !m->d_trace) {
+      const int cap = 8 * m->cfg.n_layers + 8;
+      if (cudaMalloc(&m->d_trace, (size_t)cap * 8 * sizeof(uint64_t)) != cudaSuccess)
+        rc = shd_fail(ctx, SHD_ERR_CUDA, "timeline buffer");
+      else
+        m->trace_cap = cap;
+    }
     if (rc == SHD_OK) {
       cudaGraph_t g = nullptr;
       cudaError_t e = cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal);
@@ -790,7 +807,12 @@ extern "C" int shd_model_decode_async(shd_model* m, int n_steps) {
         m->prof_next = 0;
         m->prof_kind.clear();
         m->prof_bytes.clear();
-        rc = m->enqueue_decode_step(M);
+        m->trace_kind.clear();
+        if (m->profiling == 2) {
+          e = cudaMemsetAsync(m->d_trace, 0xFF, (size_t)m->trace_cap * 8 * sizeof(uint64_t), m->stream);
+          if (e != cudaSuccess) rc = shd_cuda_fail(ctx, e, "timeline preset");
+        }
+        if (rc == SHD_OK) rc = m->enqueue_decode_step(M);
         m->prof_active = false;
         m->prof_count = m->prof_next;
         e = cudaStreamEndCapture(m->stream, &g);
@@ -894,7 +916,7 @@ extern "C" int shd_model_forward_host(shd_model* m, int slot, const float* hc_ho
 }
 
 int shd_model::prof_mark(int kind, const shd_weight* w, bool begin) {
-  if (!prof_active) return SHD_OK;
+  if (!prof_active || profiling != 1) return SHD_OK;
   if (prof_next + 1 >= prof_events.size()) return SHD_OK;
   if (begin) {
     prof_kind.push_back(kind);
@@ -907,6 +929,12 @@ int shd_model::prof_mark(int kind, const shd_weight* w, bool begin) {
   return SHD_OK;
 }
 
+unsigned long long* shd_model::trace_slot(int kind) {
+  if (!prof_active || profiling != 2 || (int)trace_kind.size() >= trace_cap) return nullptr;
+  trace_kind.push_back(kind);
+  return d_trace + (size_t)8 * (trace_kind.size() - 1);
+}
+
 extern "C" int64_t shd_model_step_launches(const shd_model* m) { return m ? m->graph_launches : -1; }
 
 extern "C" int shd_model_set_profiling(shd_model* m, int on) {
@@ -915,7 +943,22 @@ extern "C" int shd_model_set_profiling(shd_model* m, int on) {
     cudaGraphExecDestroy(m->graph);
     m->graph = nullptr;
   }
-  m->profiling = on != 0;
+  m->profiling = (on == 1 || on == 2) ? on : 0;
+  return SHD_OK;
+}
+
+extern "C" int shd_model_timeline(shd_model* m, int cap, int32_t* kinds, uint64_t* stamps, int* n_out) {
+  if (!m || !n_out) return SHD_ERR_ARG;
+  shd_ctx* ctx = m->ctx;
+  SHD_REQUIRE(ctx, m->profiling == 2 && m->graph && !m->trace_kind.empty(),
+              "shd_model_timeline: no traced decode step yet (shd_model_set_profiling(m, 2), then decode)");
+  const int n = (int)m->trace_kind.size();
+  *n_out = n;
+  if (cap < n || !kinds || !stamps) return SHD_OK;  // size query
+  SHD_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
+  SHD_CHECK_CUDA(ctx, cudaStreamSynchronize(m->stream));
+  SHD_CHECK_CUDA(ctx, cudaMemcpy(stamps, m->d_trace, (size_t)n * 8 * sizeof(uint64_t), cudaMemcpyDeviceToHost));
+  for (int i = 0; i < n; ++i) kinds[i] = m->trace_kind[i];
   return SHD_OK;
 }
 

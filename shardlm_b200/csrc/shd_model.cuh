@@ -63,6 +63,13 @@ struct shd_model {
   std::vector<double> prof_bytes;
   size_t prof_next = 0, prof_count = 0;
   int prof_mark(int kind, const shd_weight* w, bool begin);
+  // timeline (profiling == 2): one slot of 8 u64 per traced launch of the captured step, preset
+  // to all ones by a memset node at the start of the step (TraceField in shd_common.cuh)
+  unsigned long long* d_trace = nullptr;
+  int trace_cap = 0;
+  std::vector<int> trace_kind;
+  unsigned long long* trace_slot(int kind);
+
   // launch one linear of the layer loop (tensor cores or the GEMV, with a pending norm)
   // out_planes / wrote_out: see launch_linear_tc (tensor-core path only)
   int op_gemv(const shd_weight* w, int M, int epi, const shd::GemvArgs& g, bool norm,

@@ -75,6 +75,7 @@ struct AttnArgs {
   int early_kv;
   int group_cap;           // 8: `groups` hold up to 8 q heads each; otherwise up to 4
   int* err;
+  unsigned long long* trace;  // launch timeline slot (nullable; TraceField in shd_common.cuh)
 };
 
 int launch_attention(shd_ctx* ctx, const AttnArgs& a, int M);

@@ -7,6 +7,7 @@
   python -m shardlm_b200.microbench attn   [--model qwen2.5-7b] [--kv-len 577] [--iters 20]
   python -m shardlm_b200.microbench prefill [--model qwen2.5-7b] [--prompt 512] [--layers 28]
   python -m shardlm_b200.microbench attn-prefill [--model qwen2.5-7b] [--rows 512] [--kv-len 512]
+  python -m shardlm_b200.microbench timeline [--model qwen2.5-7b] [--prompt 512] [--rows 1] [--dump f.npz]
 
 --graph times a captured CUDA graph of the launches instead of host-issued launches.
 Each weight kind is instantiated in enough copies to exceed the 126 MB L2, and launches rotate over
@@ -202,9 +203,90 @@ def prefill(args, ctx: Context):
     m.close()
 
 
+TRACE_KINDS = ["qkv", "o", "gateup", "down", "lm_head", "attention"]
+
+
+def timeline_summary(kinds: np.ndarray, st: np.ndarray) -> dict:
+    """Per kind, mean over its launches (microseconds) of: `cost` = its last CTA's exit minus the
+    previous traced launch's last exit (these sum to the step); `lead` = how long before that
+    previous exit its first CTA was resident; `dep` = from the previous exit to its first return
+    from the dependency wait; `prologue` = from that return to the last CTA's end of prologue;
+    `body` = from the end of prologue to the last exit; `exit_spread` = last minus first exit."""
+    ones = np.uint64(0xFFFFFFFFFFFFFFFF)
+    e0, e1 = st[:, 0].astype(np.float64), (~st[:, 1]).astype(np.float64)
+    w0, r1 = st[:, 2].astype(np.float64), (~st[:, 3]).astype(np.float64)
+    x0, x1 = st[:, 4].astype(np.float64), (~st[:, 5]).astype(np.float64)
+    assert not (st[:, [0, 2, 4]] == ones).any(), "a traced launch was not stamped"
+    out = {}
+    for k in range(len(TRACE_KINDS)):
+        idx = [i for i in range(1, len(kinds)) if kinds[i] == k]
+        if not idx:
+            continue
+        prev = np.array([x1[i - 1] for i in idx])
+        i = np.array(idx)
+        out[TRACE_KINDS[k]] = {
+            "n": len(idx),
+            "cost": round(float(np.mean(x1[i] - prev)) / 1e3, 2),
+            "lead": round(float(np.mean(prev - e0[i])) / 1e3, 2),
+            "dep": round(float(np.mean(w0[i] - prev)) / 1e3, 2),
+            "prologue": round(float(np.mean(r1[i] - w0[i])) / 1e3, 2),
+            "body": round(float(np.mean(x1[i] - r1[i])) / 1e3, 2),
+            "exit_spread": round(float(np.mean(x1[i] - x0[i])) / 1e3, 2),
+            "entry_spread": round(float(np.mean(e1[i] - e0[i])) / 1e3, 2),
+        }
+    out["traced_span_us"] = round(float(x1[-1] - e0[0]) / 1e3, 1)
+    return out
+
+
+def timeline(args, ctx: Context):
+    """Decode-step timeline from %globaltimer stamps inside the kernels of the captured step
+    (shd_model_timeline): where the step's time goes between and inside the launches, with the
+    programmatic overlap left intact."""
+    import ctypes as C
+
+    from ._lib import check, lib
+    from .model import SecureModel
+
+    sh = SHAPES[args.model].replace(n_layers=args.layers) if args.layers else SHAPES[args.model]
+    B = args.rows
+    m = SecureModel(ctx, sh, max_seq=args.prompt + 2 * args.iters + 16, max_batch=B)
+    m.load_random_weights(seed=0)
+    rng = np.random.default_rng(0)
+    for b in range(B):
+        m.prefill(rng.integers(0, sh.vocab, args.prompt).astype(np.int32), slot=b)
+    m.decode(4, B)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    m.decode_async(args.iters)
+    e.record()
+    torch.cuda.synchronize()
+    plain_ms = s.elapsed_time(e) / args.iters
+    check(lib().shd_model_set_profiling(m.handle, 2), ctx.ptr)
+    m.decode(4, B)
+    n = C.c_int()
+    check(lib().shd_model_timeline(m.handle, 0, None, None, C.byref(n)), ctx.ptr)
+    kinds = np.zeros(n.value, np.int32)
+    st = np.zeros((n.value, 8), np.uint64)
+    check(lib().shd_model_timeline(m.handle, n.value, kinds.ctypes.data, st.ctypes.data, C.byref(n)), ctx.ptr)
+    s.record()
+    m.decode_async(args.iters)
+    e.record()
+    torch.cuda.synchronize()
+    traced_ms = s.elapsed_time(e) / args.iters
+    check(lib().shd_model_set_profiling(m.handle, 0), ctx.ptr)
+    summ = timeline_summary(kinds, st)
+    print(json.dumps({"timeline": {"model": sh.name, "layers": sh.n_layers, "rows": B, "prompt": args.prompt,
+                                   "step_ms": round(plain_ms, 4), "traced_step_ms": round(traced_ms, 4),
+                                   "kinds": summ}}))
+    if args.dump:
+        np.savez(args.dump, kinds=kinds, stamps=st)
+    m.close()
+
+
 def main():
     p = argparse.ArgumentParser()
-    p.add_argument("what", choices=["linear", "beaver", "ring", "attn", "attn-prefill", "prefill"])
+    p.add_argument("what", choices=["linear", "beaver", "ring", "attn", "attn-prefill", "prefill", "timeline"])
+    p.add_argument("--dump", default="")
     p.add_argument("--prompt", type=int, default=512)
     p.add_argument("--layers", type=int, default=0)
     p.add_argument("--kv-len", type=int, default=577)
@@ -220,7 +302,7 @@ def main():
     GRAPH = args.graph
     ctx = Context(0)
     {"linear": linear, "beaver": beaver, "ring": ring, "attn": attn, "attn-prefill": attn_prefill,
-     "prefill": prefill}[args.what](args, ctx)
+     "prefill": prefill, "timeline": timeline}[args.what](args, ctx)
 
 
 if __name__ == "__main__":

@@ -276,3 +276,41 @@ def test_model_rejects_bad_requests(ctx):
     m.prefill([1, 2, 3])
     with pytest.raises(ShdError, match="max_seq"):
         m.decode_async(6)
+
+
+def test_decode_timeline_stamps_every_launch(ctx):
+    """The traced step graph (shd_model_set_profiling(m, 2)) stamps every GEMV and attention launch
+    in layer order, with consistent times, and decodes the same tokens as the untraced graph."""
+    import ctypes as C
+
+    from shardlm_b200._lib import check, lib
+    from shardlm_b200.microbench import timeline_summary
+    from shardlm_b200.model import SHAPES, SecureModel
+
+    shape = SHAPES["tiny"].replace(n_layers=3)
+    toks = np.random.default_rng(1).integers(0, shape.vocab, 7).astype(np.int32)
+    runs = []
+    for traced in (False, True):
+        m = SecureModel(ctx, shape, max_seq=32, share_seed=9)
+        m.load_random_weights(seed=2)
+        m.prefill(toks)
+        if traced:
+            check(lib().shd_model_set_profiling(m.handle, 2), ctx.ptr)
+        runs.append(m.decode(5)[:, 0])
+        if traced:
+            n = C.c_int()
+            check(lib().shd_model_timeline(m.handle, 0, None, None, C.byref(n)), ctx.ptr)
+            kinds = np.zeros(n.value, np.int32)
+            st = np.zeros((n.value, 8), np.uint64)
+            check(lib().shd_model_timeline(m.handle, n.value, kinds.ctypes.data, st.ctypes.data, C.byref(n)),
+                  ctx.ptr)
+        m.close()
+    assert np.array_equal(runs[0], runs[1])
+    assert kinds.tolist() == [0, 5, 1, 2, 3] * shape.n_layers + [4]
+    first = st[:, [0, 2, 4]].astype(np.int64)
+    last = (~st[:, [1, 3, 5]]).astype(np.int64)
+    assert (first > 0).all() and (last > 0).all()
+    assert (last[:, 2] >= first[:, 0]).all() and (last[:, 1] >= first[:, 1]).all()
+    assert (np.diff(last[:, 2]) >= 0).all()  # each launch ends after the one before it
+    summ = timeline_summary(kinds, st)
+    assert set(summ) >= {"qkv", "attention", "o", "gateup", "down", "lm_head"}
