@@ -3,8 +3,8 @@
 // crates/v2/server/src/routes/secure_inference_mpc.rs:568-663), followed by the reshare.
 //
 // Cluster flash decode. A cluster of 8 CTAs (64 warps) serves one (query row, head group), a group
-// being up to 4 query heads (8 for batched rows) that share one kv head, so each K/V row is read
-// once for the group. Positions are dealt to the warps in chunks of 32 / group positions; a warp
+// being up to 4 query heads that share one kv head, so each K/V row is read once for the group
+// (groups of 8 heads, for batched rows, run the tile kernel further down). Positions are dealt to the warps in chunks of 32 / group positions; a warp
 // holds its chunk's K and V rows in registers (each lane 1/32 of a row, coalesced 16-byte loads),
 // computes the chunk's 32 (position, head) scores with one reduce-scatter over the warp and keeps
 // an online softmax (running max, sum, weighted V sum) per head. There is no block barrier until
@@ -311,12 +311,273 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_kernel(const Attn
   if (tid == 0) trace_both(a.trace, TR_EXIT);
 }
 
+// Wide groups (8 query heads: batched rows, one group per kv head) use the tile kernel below: per
+// position the register-chunk kernel's shuffles double at 8 heads and its registers allow one CTA per
+// SM, while here a CTA walks its eighth of the positions in 32-position tiles staged in shared
+// memory (double-buffered cp.async), warps split head_dim and lanes the positions for the scores,
+// and two CTAs fit an SM. Measured on the 14B 8-row step: 40 us per layer against 63 us.
+constexpr int kAttnTile = 32;     // positions per tile
+
 template <int HD, int GS>
-static int launch_attn_t(shd_ctx* ctx, const AttnArgs& a, int M) {
-  static unsigned attr_devices = 0;
-  const size_t smem = sizeof(AttnSmem<HD, GS>);
+struct TileSmem {
+  static constexpr int KS = HD + 4;  // padded row stride (conflict-free column reads)
+  float k[2][kAttnTile][KS];         // double-buffered: the next tile loads during this one
+  float v[2][kAttnTile][HD];
+  float q[GS][HD];
+  float spart[kAttnThreads / 32][GS][kAttnTile];  // per-warp partial dots
+  float p[GS][kAttnTile];                         // tile weights
+  float m[GS], l[GS], alpha[GS];
+  float gather[kAttnCluster][GS][HD + 2];         // CTA 0: partials of the cluster
+};
+
+template <int HD, int GS>
+__global__ void __launch_bounds__(kAttnThreads) attn_tile_kernel(const AttnArgs a) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  TileSmem<HD, GS>& S = *reinterpret_cast<TileSmem<HD, GS>*>(smem_raw);
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int gi = blockIdx.y, m = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int NW = kAttnThreads / 32;  // 8 warps
+  constexpr int DW = HD / NW;            // dims per warp in the score phase (16 or 8)
+  if (tid == 0) {
+    pdl_trigger();
+    trace_both(a.trace, TR_ENTRY);
+  }
+  // the head groups are copied in before any kernel of the launch sequence runs
+  const int4 grp = a.groups[gi];
+  const int kvh = grp.x, qh0 = grp.y, G = grp.z;
+  const bool early = a.early_kv != 0;
+  if (!early) pdl_wait();  // positions, queries and the cache come from earlier kernels
+  const int kv_len = __ldcg(a.pos + m) + 1;
+  const int sq = a.seq ? __ldcg(a.seq + m) : 0;
+  const int per = (kv_len + kAttnCluster - 1) / kAttnCluster;
+  const int t0 = min(rank * per, kv_len), t1 = min(t0 + per, kv_len);
+  const float* K = a.Kcache + (size_t)sq * a.kv_seq_stride + (size_t)kvh * HD;
+  const float* V = a.Vcache + (size_t)sq * a.kv_seq_stride + (size_t)kvh * HD;
+  const bool mpc = a.variant == SHD_NL_MPC;
+
+  // K and V rows [tb + r_lo, tb + r_hi) of a tile: 16-byte asynchronous copies (L2 only); rows of
+  // the tile past the split's end are zero-filled with the first part
+  auto stage_rows = [&](int buf, int tb, int r_lo, int r_hi) {
+    const int nt = min(kAttnTile, t1 - tb);
+    for (int i = tid; i < (r_hi - r_lo) * (HD / 4); i += kAttnThreads) {
+      const int r = r_lo + i / (HD / 4), c4 = i % (HD / 4);
+      const int row = (r < nt) ? tb + r : tb;  // an in-range address even when nothing is copied
+      const uint32_t bytes = (r < nt) ? 16u : 0u;
+      cp_async16(&S.k[buf][r][4 * c4], K + (size_t)row * a.kvd + 4 * c4, bytes);
+      cp_async16(&S.v[buf][r][4 * c4], V + (size_t)row * a.kvd + 4 * c4, bytes);
+    }
+    cp_async_commit();
+  };
+  auto stage_tile = [&](int buf, int tb) { stage_rows(buf, tb, 0, kAttnTile); };
+  if (early) {
+    // every row of tile 0 but this step's own (kv_len - 1) before the wait, that row after it
+    const int r_new = kv_len - 1 - t0;  // within tile 0 when 0 <= r_new < kAttnTile
+    if (t0 < t1) {
+      if (r_new >= 0 && r_new < kAttnTile) {
+        stage_rows(0, t0, 0, r_new);
+        stage_rows(0, t0, r_new + 1, kAttnTile);
+      } else {
+        stage_tile(0, t0);
+      }
+    }
+    pdl_wait();  // queries and this step's K/V row come from the q/k/v kernel
+    if (tid == 0) {
+      trace_first(a.trace, TR_WAIT);
+      trace_last(a.trace, TR_READY);
+    }
+    if (t0 < t1 && r_new >= 0 && r_new < kAttnTile) stage_rows(0, t0, r_new, r_new + 1);
+  } else if (t0 < t1) {
+    stage_tile(0, t0);  // in flight while the queries load
+  }
+
+  for (int i = tid; i < GS * HD; i += kAttnThreads) {
+    const int g = i / HD, d = i % HD;
+    S.q[g][d] = (g < G) ? a.Q[(size_t)m * a.ldq + (size_t)(qh0 + g) * HD + d] : 0.0f;
+  }
+  if (tid < GS) {
+    S.m[tid] = -INFINITY;
+    S.l[tid] = 0.0f;
+  }
+  // PV mapping: thread -> dim d, heads g0 and g0 + 2 (kAttnThreads = 2 * HD for HD = 128)
+  constexpr int GPT = GS * HD / kAttnThreads;  // heads per thread: 2 (HD 128) or 1 (HD 64)
+  float acc[GPT];
+#pragma unroll
+  for (int j = 0; j < GPT; ++j) acc[j] = 0.0f;
+  const int pd = tid % HD, pg0 = tid / HD;  // head of acc[j] = pg0 + j * (kAttnThreads / HD)
+  __syncthreads();
+
+  // this warp's slice of the queries: in registers for groups of up to 4 heads, read from shared
+  // memory (the same float4 for every lane) for wider groups
+  constexpr bool kQReg = GS <= 4;
+  float qreg[kQReg ? GS : 1][kQReg ? DW : 1];
+  if constexpr (kQReg) {
+#pragma unroll
+    for (int g = 0; g < GS; ++g)
+#pragma unroll
+      for (int j = 0; j < DW; ++j) qreg[g][j] = S.q[g][warp * DW + j];
+  }
+
+  int buf = 0;
+  for (int tb = t0; tb < t1; tb += kAttnTile, buf ^= 1) {
+    const int nt = min(kAttnTile, t1 - tb);
+    if (tb + kAttnTile < t1) {
+      stage_tile(buf ^ 1, tb + kAttnTile);
+      cp_async_wait<1>();  // this tile's copies have landed (the next tile's may be in flight)
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    // partial dots: warp = dim slice, lane = position
+    {
+      float part[GS];
+#pragma unroll
+      for (int g = 0; g < GS; ++g) part[g] = 0.0f;
+#pragma unroll
+      for (int j = 0; j < DW; j += 4) {
+        const float4 kk = *reinterpret_cast<const float4*>(&S.k[buf][lane][warp * DW + j]);
+#pragma unroll
+        for (int g = 0; g < GS; ++g) {
+          float4 qq;
+          if constexpr (kQReg)
+            qq = make_float4(qreg[g][j + 0], qreg[g][j + 1], qreg[g][j + 2], qreg[g][j + 3]);
+          else
+            qq = *reinterpret_cast<const float4*>(&S.q[g][warp * DW + j]);
+          part[g] = __fmaf_rn(qq.x, kk.x, part[g]);
+          part[g] = __fmaf_rn(qq.y, kk.y, part[g]);
+          part[g] = __fmaf_rn(qq.z, kk.z, part[g]);
+          part[g] = __fmaf_rn(qq.w, kk.w, part[g]);
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < GS; ++g) S.spart[warp][g][lane] = part[g];
+    }
+    __syncthreads();
+    // scores and online softmax: warp g (< G) owns head g, lane = position
+    if (warp < G) {
+      const int g = warp;
+      float s = 0.0f;
+#pragma unroll
+      for (int w = 0; w < NW; ++w) s = __fadd_rn(s, S.spart[w][g][lane]);
+      s = (lane < nt) ? __fmul_rn(s, a.scale) : -INFINITY;
+      float tmax = s;
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
+      const float mold = S.m[g];
+      const float mnew = fmaxf(mold, tmax);
+      float x = __fsub_rn(s, mnew);
+      if (!mpc) x = fminf(fmaxf(x, -40.0f), 40.0f);
+      const float pe = (lane < nt) ? expf(x) : 0.0f;
+      float tsum = pe;
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) tsum = __fadd_rn(tsum, __shfl_xor_sync(0xffffffffu, tsum, o));
+      S.p[g][lane] = pe;
+      __syncwarp();
+      if (lane == 0) {
+        const float al = (mold == -INFINITY) ? 0.0f : expf(__fsub_rn(mold, mnew));
+        S.alpha[g] = al;
+        S.l[g] = __fmaf_rn(S.l[g], al, tsum);
+        S.m[g] = mnew;
+      }
+    }
+    __syncthreads();
+    // weighted V: thread -> (dim, its heads). Wide groups: each V element is loaded once for all of
+    // the thread's heads and the weights 4 positions at a time (rows past the tile's end have p = 0
+    // and V = 0); measured faster at 8-head groups, slower at 4 (single-row decode), which keeps
+    // the per-head loop.
+    if constexpr (GS <= 4) {
+#pragma unroll
+      for (int j = 0; j < GPT; ++j) {
+        const int g = pg0 + j * (kAttnThreads / HD);
+        if (g < G) {
+          float v = __fmul_rn(acc[j], S.alpha[g]);
+          for (int r = 0; r < nt; ++r) v = __fmaf_rn(S.p[g][r], S.v[buf][r][pd], v);
+          acc[j] = v;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < GPT; ++j) {
+        const int g = pg0 + j * (kAttnThreads / HD);
+        if (g < G) acc[j] = __fmul_rn(acc[j], S.alpha[g]);
+      }
+      for (int r = 0; r < nt; r += 4) {
+        const float v0 = S.v[buf][r][pd], v1 = S.v[buf][r + 1][pd];
+        const float v2 = S.v[buf][r + 2][pd], v3 = S.v[buf][r + 3][pd];
+#pragma unroll
+        for (int j = 0; j < GPT; ++j) {
+          const int g = pg0 + j * (kAttnThreads / HD);
+          if (g < G) {
+            const float4 pp = *reinterpret_cast<const float4*>(&S.p[g][r]);
+            float v = acc[j];
+            v = __fmaf_rn(pp.x, v0, v);
+            v = __fmaf_rn(pp.y, v1, v);
+            v = __fmaf_rn(pp.z, v2, v);
+            v = __fmaf_rn(pp.w, v3, v);
+            acc[j] = v;
+          }
+        }
+      }
+    }
+    __syncthreads();  // this buffer is refilled two tiles later
+  }
+
+  // gather the cluster's partials into CTA 0 (distributed shared memory), then combine in rank order
+  TileSmem<HD, GS>* root = cluster.map_shared_rank(&S, 0);
+#pragma unroll
+  for (int j = 0; j < GPT; ++j) {
+    const int g = pg0 + j * (kAttnThreads / HD);
+    if (g < G) root->gather[rank][g][2 + pd] = acc[j];
+  }
+  if (tid < G) {
+    root->gather[rank][tid][0] = S.m[tid];
+    root->gather[rank][tid][1] = S.l[tid];
+  }
+  cluster.sync();
+  if (rank != 0) {
+    if (tid == 0) trace_both(a.trace, TR_EXIT);
+    return;
+  }
+
+#pragma unroll
+  for (int j = 0; j < GPT; ++j) {
+    const int g = pg0 + j * (kAttnThreads / HD);
+    if (g >= G) continue;
+    float Mx = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < kAttnCluster; ++r) Mx = fmaxf(Mx, S.gather[r][g][0]);
+    float L = 0.0f, out = 0.0f;
+#pragma unroll
+    for (int r = 0; r < kAttnCluster; ++r) {
+      const float mr = S.gather[r][g][0];
+      if (mr == -INFINITY) continue;
+      const float w = expf(__fsub_rn(mr, Mx));
+      L = __fmaf_rn(S.gather[r][g][1], w, L);
+      out = __fmaf_rn(S.gather[r][g][2 + pd], w, out);
+    }
+    if (mpc && !(L > 1e-10f && isfinite(L))) {
+      // compute_mpc_attention_on_shares: weights 1/seq_len when the sum is not usable
+      float u = 0.0f;
+      for (int tt = 0; tt < kv_len; ++tt) u = __fmaf_rn(__fdiv_rn(1.0f, (float)kv_len), V[(size_t)tt * a.kvd + pd], u);
+      out = u;
+    } else {
+      out = __fdiv_rn(out, L);
+    }
+    const int h = qh0 + g;
+    const size_t o = (size_t)m * a.ldo + (size_t)h * HD + pd;
+    const float mk = a.mask ? a.mask[(size_t)m * a.ldmask + (size_t)h * HD + pd] : 0.0f;
+    a.Oc[o] = __fsub_rn(out, mk);
+    a.Os[o] = mk;
+  }
+  if (tid == 0) trace_both(a.trace, TR_EXIT);
+}
+
+template <typename Kern>
+static int launch_cluster(shd_ctx* ctx, Kern kernel, size_t smem, unsigned& attr_devices, const AttnArgs& a,
+                          int M) {
   if (!(attr_devices & (1u << (ctx->device & 31)))) {
-    SHD_CHECK_CUDA(ctx, cudaFuncSetAttribute(attn_decode_kernel<HD, GS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    SHD_CHECK_CUDA(ctx, cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attr_devices |= 1u << (ctx->device & 31);
   }
   cudaLaunchConfig_t cfg = {};
@@ -333,9 +594,19 @@ static int launch_attn_t(shd_ctx* ctx, const AttnArgs& a, int M) {
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  SHD_CHECK_CUDA(ctx, cudaLaunchKernelEx(&cfg, attn_decode_kernel<HD, GS>, a));
+  SHD_CHECK_CUDA(ctx, cudaLaunchKernelEx(&cfg, kernel, a));
   ctx->launches++;
   return SHD_OK;
+}
+
+// Groups of up to 4 query heads: the register-chunk kernel; 8-head groups: the tile kernel.
+template <int HD, int GS>
+static int launch_attn_t(shd_ctx* ctx, const AttnArgs& a, int M) {
+  static unsigned attr_devices = 0;
+  if constexpr (GS == 8)
+    return launch_cluster(ctx, attn_tile_kernel<HD, GS>, sizeof(TileSmem<HD, GS>), attr_devices, a, M);
+  else
+    return launch_cluster(ctx, attn_decode_kernel<HD, GS>, sizeof(AttnSmem<HD, GS>), attr_devices, a, M);
 }
 
 int launch_attention(shd_ctx* ctx, const AttnArgs& a, int M) {
