@@ -424,7 +424,8 @@ int shd_model_linear_times(shd_model* m, float* ms_out6, double* bytes_out6);
 /* Timeline: shd_model_set_profiling(m, 2) makes the captured decode step stamp %globaltimer (ns)
  * inside the kernels themselves, without cutting the programmatic overlap between them. After a
  * decode, shd_model_timeline returns one record per traced launch in launch order: kinds[i] as
- * above (0 qkv, 1 o, 2 gate/up, 3 down, 4 lm_head, 5 attention) and stamps[8 i + f] for
+ * above (0 qkv, 1 o, 2 gate/up, 3 down, 4 lm_head, 5 attention, 6 tensor-parallel peer-exchange
+ * receive; its field 3 is the last CTA's end of polling, before its wait) and stamps[8 i + f] for
  * f = 0 first CTA entry, 1 last CTA entry, 2 first return from the wait on the previous kernel,
  * 3 last end of the prologue (wait and fused norm), 4 first exit, 5 last exit (fields 1, 3, 5
  * stored complemented; all ones = not reached). Launches on the tensor-core path are not stamped.

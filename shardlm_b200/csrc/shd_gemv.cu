@@ -147,6 +147,10 @@ __global__ void __launch_bounds__(kGemvThreads, MINB) gemv_f32_kernel(const __gr
   }
   __syncthreads();
   if (threadIdx.x == 0) {
+    // A tensor-parallel push takes the exchange call after the last one whose receive kernel has
+    // started: that kernel advanced the call counter before releasing its dependents, and the next
+    // receive kernel (which advances it again) cannot start before this kernel releases its own.
+    if (a.tp_peer[0]) sm.flags[2] = *reinterpret_cast<const volatile int*>(a.tp_peer[a.tp_me]) + 1;
     pdl_trigger();
     trace_both(a.trace, TR_ENTRY);
   }
@@ -240,7 +244,7 @@ __global__ void __launch_bounds__(kGemvThreads, MINB) gemv_f32_kernel(const __gr
       }
       if (r == 0) continue;
     }
-    epilogue_f32<M, EPI>(a, ct, tsum, ctid, a.err);
+    epilogue_f32<M, EPI>(a, ct, tsum, ctid, a.err, (unsigned)sm.flags[2]);
     if (!consumer_sync(sm, cphase, lane)) {
       if (lane == 0) atomicOr(a.err, SHD_DEVERR_TIMEOUT_FULL);
       sm.flags[0] = 1;

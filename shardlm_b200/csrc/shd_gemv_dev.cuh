@@ -116,14 +116,16 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
   return ((unsigned long long)b << 32) | (unsigned)idx;
 }
 
+// push_epoch: the exchange call this launch pushes (read by the kernel before it released its
+// dependents, see gemv_f32_kernel).
 template <int M, int EPI>
-__device__ void epilogue_f32(const GemvArgs& a, int t, const float* tsum, int ctid, int* err) {
+__device__ void epilogue_f32(const GemvArgs& a, int t, const float* tsum, int ctid, int* err,
+                             unsigned push_epoch = 0) {
   if constexpr (EPI == EPI_STORE) {
     if (a.tp_peer[0]) {
       // push the tile to every rank: consecutive threads take consecutive rows of one (peer, share,
-      // row m), so each warp writes 256 contiguous bytes of one peer's slot. The call counter was
-      // last written by the previous receive kernel, which completed before this kernel launched.
-      const unsigned epoch = (unsigned)*reinterpret_cast<const volatile int*>(a.tp_peer[a.tp_me]) + 1u;
+      // row m), so each warp writes 256 contiguous bytes of one peer's slot.
+      const unsigned epoch = push_epoch;
       const unsigned long long tag = (unsigned long long)epoch << 32;
       const int W = a.tp_world;
       for (int idx = ctid; idx < kTileRows * M * 2 * W; idx += kConsumerWarps * 32) {

@@ -91,9 +91,15 @@ int nccl_fail(shd_ctx* ctx, ncclResult_t r, const char* what) {
 // hold identical sums. Fused form: the row-parallel GEMV's epilogue pushes each finished tile
 // itself (GemvArgs::tp_peer), and p2p_recv_kernel only polls and sums; it starts polling as soon as
 // it is resident, before the wait on the GEMV, and writes the sums after that wait (earlier
-// kernels may still read the buffer until then). Neither kernel releases its dependents early:
-// the next kernel starts only after the exchange has completed, which is what makes reading the
-// call counter at the start of the next exchange (or push) safe.
+// kernels may still read the buffer until then).
+// Call counters: p2p_allreduce_kernel advances its CTA's counter at its end and does not release
+// its dependents early. p2p_recv_kernel advances it at its START, fenced, before releasing its
+// dependents (the next GEMV's CTAs then stream their weights while the exchange completes): every
+// later kernel is launched only after all of this kernel's CTAs released, so it reads the advanced
+// counter. A pushing GEMV reads it at its start, before releasing its own dependents, since the
+// next receive kernel advances it as soon as it is released. Slot reuse stays safe because a rank
+// pushes call c + 2 only after its wait, i.e. after its receive of c + 1 completed, which needed
+// every peer's push of c + 1, which each made after its own receive of c completed.
 // ------------------------------------------------------------------------------------------------
 constexpr int kP2pPer = (int)(kP2pCapacity / ((size_t)kP2pCtas * kP2pThreads));  // values per thread
 static_assert(kP2pPer % 2 == 0, "values per thread come in pairs");
@@ -104,6 +110,7 @@ struct P2pArgs {
   uint8_t* peer[kP2pMaxWorld];  // every rank's receive buffer (peer[me] = local)
   int me, world;
   int* err;
+  unsigned long long* trace;  // launch timeline slot (nullable; TraceField in shd_common.cuh)
 };
 
 __device__ __forceinline__ unsigned long long ld_volatile_u64(const unsigned long long* p) {
@@ -175,7 +182,7 @@ __device__ bool p2p_collect(const P2pArgs& a, unsigned epoch, float (&acc)[kP2pP
   return true;
 }
 
-__device__ __forceinline__ void p2p_finish(const P2pArgs& a, const float (&acc)[kP2pPer], bool ok, unsigned epoch) {
+__device__ __forceinline__ void p2p_finish(const P2pArgs& a, const float (&acc)[kP2pPer], bool ok) {
   if (ok) {
 #pragma unroll
     for (int k = 0; k < kP2pPer; ++k) {
@@ -185,8 +192,6 @@ __device__ __forceinline__ void p2p_finish(const P2pArgs& a, const float (&acc)[
   } else {
     atomicOr(a.err, SHD_DEVERR_TIMEOUT_FULL);
   }
-  __syncthreads();  // every thread of the CTA has read the counter
-  if (threadIdx.x == 0) *reinterpret_cast<volatile int*>(p2p_counter(a)) = (int)epoch;
 }
 
 __global__ void __launch_bounds__(kP2pThreads) p2p_allreduce_kernel(const __grid_constant__ P2pArgs a) {
@@ -203,16 +208,31 @@ __global__ void __launch_bounds__(kP2pThreads) p2p_allreduce_kernel(const __grid
   }
   float acc[kP2pPer];
   const bool ok = p2p_collect(a, epoch, acc);
-  p2p_finish(a, acc, ok, epoch);
+  p2p_finish(a, acc, ok);
+  __syncthreads();  // every thread of the CTA has read the counter
+  if (threadIdx.x == 0) *reinterpret_cast<volatile int*>(p2p_counter(a)) = (int)epoch;
 }
 
 __global__ void __launch_bounds__(kP2pThreads) p2p_recv_kernel(const __grid_constant__ P2pArgs a) {
-  const unsigned epoch = (unsigned)*reinterpret_cast<const volatile int*>(p2p_counter(a)) + 1u;
+  __shared__ unsigned s_epoch;
+  if (threadIdx.x == 0) {
+    trace_both(a.trace, TR_ENTRY);
+    const unsigned e = (unsigned)*reinterpret_cast<const volatile int*>(p2p_counter(a)) + 1u;
+    *reinterpret_cast<volatile int*>(p2p_counter(a)) = (int)e;
+    __threadfence();  // the advanced counter is visible before any dependent is released
+    s_epoch = e;
+    pdl_trigger();
+  }
+  __syncthreads();
+  const unsigned epoch = s_epoch;
   // polling needs nothing from the previous kernel: only values tagged with this call's epoch count
   float acc[kP2pPer];
   const bool ok = p2p_collect(a, epoch, acc);
+  if (threadIdx.x == 0) trace_last(a.trace, TR_READY);
   pdl_wait();  // kernels before the pushing GEMV may read the output buffer until it completes
-  p2p_finish(a, acc, ok, epoch);
+  if (threadIdx.x == 0) trace_first(a.trace, TR_WAIT);
+  p2p_finish(a, acc, ok);
+  if (threadIdx.x == 0) trace_both(a.trace, TR_EXIT);
 }
 
 int p2p_setup(shd_ctx* ctx) {
@@ -327,8 +347,10 @@ int allreduce_f32(shd_ctx* ctx, float* buf, size_t n, cudaStream_t stream) {
 
 // Receive half of the fused exchange: the previous kernel (a GEMV with push fields) has pushed this
 // rank's partial shares; sum every rank's into buf.
-int allreduce_recv_f32(shd_ctx* ctx, float* buf, size_t n, cudaStream_t stream) {
+int allreduce_recv_f32(shd_ctx* ctx, float* buf, size_t n, cudaStream_t stream,
+                       unsigned long long* trace = nullptr) {
   P2pArgs a{};
+  a.trace = trace;
   a.buf = buf;
   a.n = n;
   for (int q = 0; q < ctx->tp_world; ++q) a.peer[q] = static_cast<uint8_t*>(ctx->p2p_peer[q]);
@@ -441,7 +463,9 @@ bool shd_model::tp_push(shd::GemvArgs& g, const shd_weight* w, int M, size_t n) 
   return true;
 }
 
-int shd_model::allreduce_recv(float* buf, size_t n) { return allreduce_recv_f32(ctx, buf, n, stream); }
+int shd_model::allreduce_recv(float* buf, size_t n) {
+  return allreduce_recv_f32(ctx, buf, n, stream, trace_slot(6));
+}
 
 int shd_model::allreduce_max_keys(int M) {
   if (ctx->tp_world <= 1) return SHD_OK;

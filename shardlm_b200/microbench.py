@@ -203,7 +203,7 @@ def prefill(args, ctx: Context):
     m.close()
 
 
-TRACE_KINDS = ["qkv", "o", "gateup", "down", "lm_head", "attention"]
+TRACE_KINDS = ["qkv", "o", "gateup", "down", "lm_head", "attention", "exchange"]
 
 
 def timeline_summary(kinds: np.ndarray, st: np.ndarray) -> dict:
@@ -247,9 +247,21 @@ def timeline(args, ctx: Context):
     from ._lib import check, lib
     from .model import SecureModel
 
+    import os
+
     sh = SHAPES[args.model].replace(n_layers=args.layers) if args.layers else SHAPES[args.model]
     B = args.rows
-    m = SecureModel(ctx, sh, max_seq=args.prompt + 2 * args.iters + 16, max_batch=B)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if world > 1:  # under torchrun: tensor parallel over the ranks, as bench.py
+        import torch.distributed as dist
+        from datetime import timedelta
+
+        from .tp import init_tensor_parallel
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", torch.cuda.current_device()))
+        init_tensor_parallel(ctx, rank, world)
+    m = SecureModel(ctx, sh, max_seq=args.prompt + 2 * args.iters + 16, max_batch=B, tp_rank=rank, tp_world=world)
     m.load_random_weights(seed=0)
     rng = np.random.default_rng(0)
     for b in range(B):
@@ -275,12 +287,16 @@ def timeline(args, ctx: Context):
     traced_ms = s.elapsed_time(e) / args.iters
     check(lib().shd_model_set_profiling(m.handle, 0), ctx.ptr)
     summ = timeline_summary(kinds, st)
-    print(json.dumps({"timeline": {"model": sh.name, "layers": sh.n_layers, "rows": B, "prompt": args.prompt,
-                                   "step_ms": round(plain_ms, 4), "traced_step_ms": round(traced_ms, 4),
-                                   "kinds": summ}}))
+    if rank == 0:
+        print(json.dumps({"timeline": {"model": sh.name, "layers": sh.n_layers, "rows": B, "prompt": args.prompt,
+                                       "tp": world, "step_ms": round(plain_ms, 4),
+                                       "traced_step_ms": round(traced_ms, 4), "kinds": summ}}))
     if args.dump:
-        np.savez(args.dump, kinds=kinds, stamps=st)
+        np.savez(args.dump + (f".rank{rank}" if world > 1 else ""), kinds=kinds, stamps=st)
     m.close()
+    if world > 1:
+        lib().shd_tp_destroy(ctx.ptr)
+        dist.destroy_process_group()
 
 
 def main():
@@ -300,7 +316,11 @@ def main():
     args = p.parse_args()
     global GRAPH
     GRAPH = args.graph
-    ctx = Context(0)
+    import os
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    ctx = Context(local)
     {"linear": linear, "beaver": beaver, "ring": ring, "attn": attn, "attn-prefill": attn_prefill,
      "prefill": prefill, "timeline": timeline}[args.what](args, ctx)
 
