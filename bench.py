@@ -222,7 +222,7 @@ def run_ours(args, shape):
     B = args.batch
     e2e_steps = args.e2e_steps if B == 1 else 0
     prof_steps = 3
-    max_seq = args.prompt + args.warmup + args.steps + prof_steps + e2e_steps + 8
+    max_seq = args.prompt + args.warmup + args.steps + 2 * prof_steps + e2e_steps + 8
     model = SecureModel(ctx, shape, max_seq=max_seq, max_batch=B, share_seed=0x5EED, tp_rank=rank, tp_world=world)
     model.load_random_weights(seed=0)
     rng = np.random.default_rng(0)  # seeded uniform prompt token ids
@@ -281,11 +281,17 @@ def run_ours(args, shape):
 
     stream = torch.cuda.current_stream()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sync = torch.zeros(1, device="cuda")
     with ClockSampler(local) as clocks:
         barrier()
         torch.cuda.synchronize()
         # profiler capture window (ncu --profile-from-start off sees exactly the timed launches)
         torch.cuda.profiler.start()
+        if world > 1:
+            # a device-side rendezvous right before the start event: every rank's timed region starts
+            # when the last rank's stream reaches it, so a rank whose host launches late does not
+            # stretch the others' first exchange inside their timed region
+            dist.all_reduce(sync)
         start.record(stream)
         model.decode_async(args.steps)
         end.record(stream)
@@ -308,6 +314,9 @@ def run_ours(args, shape):
     by5 = np.zeros(6, np.float64)
     _lib.check(lib.shd_model_linear_times(model.handle, ms5.ctypes.data, by5.ctypes.data), ctx.ptr)
     lib.shd_model_set_profiling(model.handle, 0)
+    # the same step with the overlap intact: %globaltimer stamps inside the kernels of the graph
+    # (shd_model_timeline), per kind the mean time from the previous launch's end to its own
+    timeline = in_graph_timeline(lib, _lib, model, ctx, prof_steps, by5)
 
     # e2e: generate_token_gpu semantics with host buffers (H2D hidden shares, D2H logit shares),
     # server-side embedding shares and client-side reconstruct + greedy sampling on the host
@@ -409,7 +418,8 @@ def run_ours(args, shape):
                          "per_kind_us_per_step": {k: round(float(ms5[i]) * 1e3, 1) for i, k in
                                                   enumerate(["qkv", "o", "gateup", "down", "lm_head", "attention"])},
                          "timing": "CUDA events around each launch in a profiled replay of the step graph "
-                                   "right after the timed region (events cut programmatic-launch overlap)"},
+                                   "right after the timed region (events cut programmatic-launch overlap)",
+                         "in_graph": timeline},
             "step_roofline": {"weight_bytes_per_token_per_gpu": int(weight_bytes),
                               "frac_of_hbm": round(weight_bytes / (ms_step * 1e-3) / 1e9 / peak, 4)},
             "e2e": e2e,
@@ -424,6 +434,46 @@ def run_ours(args, shape):
     if world > 1:
         _lib.lib().shd_tp_destroy(ctx.ptr)
         dist.destroy_process_group()
+
+
+def in_graph_timeline(lib, _lib, model, ctx, steps: int, by5) -> dict | None:
+    """Per kind (q/k/v, o, gate/up, down, lm_head, attention, TP exchange): the mean in-graph cost
+    (the launch's last CTA exit minus the previous launch's) over the step's launches, and for the
+    linears the weight bytes of one launch over that cost. None when some launch of the step runs
+    on a path that is not stamped (the tensor-core linear of batched decode)."""
+    import ctypes as C
+
+    from shardlm_b200.microbench import TRACE_KINDS, timeline_summary
+
+    lib.shd_model_set_profiling(model.handle, 2)
+    try:
+        model.decode_async(steps)
+        n = C.c_int()
+        _lib.check(lib.shd_model_timeline(model.handle, 0, None, None, C.byref(n)), ctx.ptr)
+        kinds = np.zeros(n.value, np.int32)
+        st = np.zeros((n.value, 8), np.uint64)
+        _lib.check(lib.shd_model_timeline(model.handle, n.value, kinds.ctypes.data, st.ctypes.data, C.byref(n)),
+                   ctx.ptr)
+    finally:
+        lib.shd_model_set_profiling(model.handle, 0)
+    if (st[:, [0, 2, 4]] == np.uint64(0xFFFFFFFFFFFFFFFF)).any():
+        return None
+    summ = timeline_summary(kinds, st)
+    out = {"us_per_launch": {}, "GBps": {}, "frac": {}}
+    peak = peaks()[0]
+    for i, k in enumerate(TRACE_KINDS):
+        if k not in summ:
+            continue
+        cost = summ[k]["cost"]
+        out["us_per_launch"][k] = cost
+        if i < 5 and cost > 0:
+            per_launch = by5[i] / max(1, int((kinds == i).sum()))
+            out["GBps"][k] = round(per_launch / (cost * 1e-6) / 1e9, 1)
+            out["frac"][k] = round(out["GBps"][k] / peak, 4)
+    out["span_us"] = summ["traced_span_us"]
+    out["timing"] = ("%globaltimer stamps inside every GEMV, attention and exchange launch of a traced replay "
+                     "of the step graph (shd_model_timeline); cost = last CTA exit minus the previous launch's")
+    return out
 
 
 def main():
