@@ -220,7 +220,7 @@ def run_ours(args, shape):
         init_tensor_parallel(ctx, rank, world)
 
     B = args.batch
-    e2e_steps = args.e2e_steps if B == 1 else 0
+    e2e_steps = args.e2e_steps
     prof_steps = 3
     max_seq = args.prompt + args.warmup + args.steps + 2 * prof_steps + e2e_steps + 8
     model = SecureModel(ctx, shape, max_seq=max_seq, max_batch=B, share_seed=0x5EED, tp_rank=rank, tp_world=world)
@@ -319,7 +319,8 @@ def run_ours(args, shape):
     timeline = in_graph_timeline(lib, _lib, model, ctx, prof_steps, by5)
 
     # e2e: generate_token_gpu semantics with host buffers (H2D hidden shares, D2H logit shares),
-    # server-side embedding shares and client-side reconstruct + greedy sampling on the host
+    # server-side embedding shares and client-side reconstruct + greedy sampling on the host; with
+    # several sequences, one shd_model_forward_host_rows call serves all of them per step
     e2e = None
     if e2e_steps > 0:
         embed_host = None
@@ -328,41 +329,52 @@ def run_ours(args, shape):
         del hw
         torch.cuda.empty_cache()
         hrng = np.random.default_rng(1)
-        tok = int(toks[-1, 0])
+        cur = [int(t) for t in toks[-1, :B]]
+
         # pinned host buffers, reused every step: the hidden shares going in, the logit shares out
-        def pinned(n):
-            return torch.empty(n, dtype=torch.float32, pin_memory=True).numpy()
+        def pinned(*shp):
+            return torch.empty(*shp, dtype=torch.float32, pin_memory=True).numpy()
 
-        c_buf, s_buf = pinned(shape.hidden), pinned(shape.hidden)
-        out = (pinned(shape.vocab), pinned(shape.vocab))
+        c_buf, s_buf = pinned(B, shape.hidden), pinned(B, shape.hidden)
+        out = (pinned(B, shape.vocab), pinned(B, shape.vocab))
         l_buf = np.empty(shape.vocab, np.float32)
-        slot = 0
+        slots = np.arange(B, dtype=np.int32)
 
-        def one(tok):
-            hrng.random(out=s_buf, dtype=np.float32)
-            np.subtract(embed_host[tok], s_buf, out=c_buf)
-            lc, ls = model.forward_host(c_buf, s_buf, slot=slot, out=out)
+        def greedy(lc, ls):
             # client reconstruct + greedy: the LAST index among equal maxima (Iterator::max_by)
             l = np.add(lc, ls, out=l_buf)
             i = int(np.argmax(l))
             ties = np.flatnonzero(l[i + 1:] == l[i])
             return i + 1 + int(ties[-1]) if ties.size else i
 
+        def one(cur):
+            hrng.random(out=s_buf, dtype=np.float32)
+            for b in range(B):
+                np.subtract(embed_host[cur[b]], s_buf[b], out=c_buf[b])
+            if B == 1:
+                lc, ls = model.forward_host(c_buf[0], s_buf[0], slot=0, out=(out[0][0], out[1][0]))
+                return [greedy(lc, ls)]
+            lc, ls = model.forward_host_rows(slots, c_buf, s_buf, out=out)
+            return [greedy(lc[b], ls[b]) for b in range(B)]
+
         for _ in range(2):
-            tok = one(tok)
+            cur = one(cur)
         barrier()
         t0 = time.perf_counter()
         for _ in range(e2e_steps - 2):
-            tok = one(tok)
+            cur = one(cur)
         el = time.perf_counter() - t0
         if world > 1:
             t = torch.tensor([el], device="cuda", dtype=torch.float64)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             el = float(t.item())
-        e2e = {"value": round((e2e_steps - 2) / el, 3), "unit": "tok/s",
-               "h2d_bytes_per_step": 2 * shape.hidden * 4, "d2h_bytes_per_step": 2 * shape.vocab * 4,
-               "path": "shd_model_forward_host (host shares in, host logit shares out, pinned host "
-                       "buffers), host argmax"}
+        e2e = {"value": round(B * (e2e_steps - 2) / el, 3), "unit": "tok/s",
+               "h2d_bytes_per_step": 2 * B * shape.hidden * 4 + (8 * B if B > 1 else 8),
+               "d2h_bytes_per_step": 2 * B * shape.vocab * 4,
+               "path": ("shd_model_forward_host (host shares in, host logit shares out, pinned host buffers), "
+                        "host argmax") if B == 1 else
+                       ("shd_model_forward_host_rows: the %d sequences' hidden shares in, their logit shares "
+                        "out in one call per step (pinned host buffers), host argmax per sequence" % B)}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

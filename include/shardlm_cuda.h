@@ -365,8 +365,9 @@ int shd_model_set_head(shd_model* m, const uint16_t* lm_head, const float* final
 int shd_model_set_masks(shd_model* m, const float* masks, int64_t stride);
 /* Forget all sequences. */
 int shd_model_reset(shd_model* m);
-/* Prefill a prompt into sequence slot `slot` (chunks of <= 8 positions); writes the greedy next
- * token to *next_token_host and leaves the slot ready to decode. Synchronous. */
+/* Prefill a prompt into sequence slot `slot` (chunks of up to 512 positions through the tensor-core
+ * linears and prefill attention); writes the greedy next token to *next_token_host and leaves the
+ * slot ready to decode. Synchronous. */
 int shd_model_prefill(shd_model* m, int slot, const int32_t* tokens_host, int n,
                       int32_t* next_token_host);
 /* Enqueue n_steps greedy decode steps for slots [0, n_active) from a captured CUDA graph; no host
@@ -379,6 +380,12 @@ int shd_model_read_tokens(shd_model* m, int count, int32_t* tokens_host);
  * full vocabulary on every rank). Synchronous. */
 int shd_model_forward_host(shd_model* m, int slot, const float* hc_host, const float* hs_host,
                            float* logits_c_host, float* logits_s_host);
+/* shd_model_forward_host for M sequences at once (generate_token_gpu of M sessions served in one
+ * pass): row r is the next position of slot slots[r] (distinct slots); hidden shares in as
+ * [M][hidden] client and server arrays, logit shares out as [M][vocab] arrays (the full vocabulary
+ * on every rank). One weight pass serves all rows. Synchronous. */
+int shd_model_forward_host_rows(shd_model* m, int M, const int32_t* slots, const float* hc_host,
+                                const float* hs_host, float* logits_c_host, float* logits_s_host);
 /* batched_prefill_gpu_v3 (secure_inference.rs:2299-2632) as the reference's route takes it: the
  * client's hidden-state shares of n prompt positions (host [n][h] each, get_embeddings_direct's
  * output) instead of token ids. Optional outputs (pairs, nullable): the last position's logit

@@ -100,6 +100,7 @@ SIGNATURES: dict[str, tuple] = {
     "shd_model_decode_async": (I32, [P, I32]),
     "shd_model_read_tokens": (I32, [P, I32, P]),
     "shd_model_forward_host": (I32, [P, I32, P, P, P, P]),
+    "shd_model_forward_host_rows": (I32, [P, I32, P, P, P, P, P]),
     "shd_model_seq_len": (I32, [P, I32]),
     "shd_model_step_launches": (I64, [P]),
     "shd_model_set_profiling": (I32, [P, I32]),

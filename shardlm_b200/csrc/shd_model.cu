@@ -571,7 +571,7 @@ int shd_model::enqueue_head(int M, int row, int cur, int variant, bool want_logi
 }
 
 // Decode head for all M rows (each its own slot): norm M rows, lm_head on M rows.
-int shd_model::enqueue_head_rows(int M, int cur, int variant) {
+int shd_model::enqueue_head_rows(int M, int cur, int variant, float* logits) {
   const int h = cfg.hidden;
   const float* lm = masks ? masks + (size_t)(cfg.n_layers - 1) * mask_stride : nullptr;
   float* Hc = Hbuf[cur];
@@ -582,6 +582,9 @@ int shd_model::enqueue_head_rows(int M, int cur, int variant) {
   if (rc) return rc;
   g.amax = amax;
   g.idx_offset = sh.vocab_begin;
+  if (logits) {
+    g.Yc = logits; g.Ys = logits + (size_t)M * V; g.ldy = V;
+  }
   g.trace = trace_slot(4);
   if ((rc = prof_mark(4, lm_head, true))) return rc;
   if ((rc = op_gemv(lm_head, M, EPI_LOGITS, g, fused))) return rc;
@@ -903,6 +906,68 @@ extern "C" int shd_model_forward_host_hidden(shd_model* m, int slot, const float
           hidden_c_host[i] = fin[i] + fin[2 * h + i];  // secure_add_gpu: per-share add
           hidden_s_host[i] = fin[h + i] + fin[3 * h + i];
         }
+    }
+  }
+  rc = m->leave(rc);
+  if (rc == SHD_OK) rc = shd_sync(ctx);
+  return rc;
+}
+
+extern "C" int shd_model_forward_host_rows(shd_model* m, int M, const int32_t* slots, const float* hc_host,
+                                           const float* hs_host, float* logits_c_host, float* logits_s_host) {
+  if (!m) return SHD_ERR_ARG;
+  shd_ctx* ctx = m->ctx;
+  SHD_REQUIRE(ctx, M >= 1 && M <= m->cfg.max_batch, "shd_model_forward_host_rows: rows must be 1..max_batch");
+  SHD_REQUIRE(ctx, slots && hc_host && hs_host && logits_c_host && logits_s_host,
+              "shd_model_forward_host_rows: null buffer");
+  std::vector<char> seen(m->cfg.max_batch, 0);
+  for (int r = 0; r < M; ++r) {
+    SHD_REQUIRE(ctx, slots[r] >= 0 && slots[r] < m->cfg.max_batch, "shd_model_forward_host_rows: slot out of range");
+    SHD_REQUIRE(ctx, !seen[slots[r]], "shd_model_forward_host_rows: a slot appears twice");
+    seen[slots[r]] = 1;
+    SHD_REQUIRE(ctx, m->len[slots[r]] < m->cfg.max_seq, "shd_model_forward_host_rows: sequence full");
+  }
+  int rc = m->check_ready();
+  if (rc) return rc;
+  SHD_CHECK_CUDA(ctx, cudaSetDevice(ctx->device));
+  if (!m->LOGrows) {
+    SHD_CHECK_CUDA(ctx, cudaMalloc(&m->LOGrows, (size_t)2 * m->cfg.max_batch * std::max(m->V, 1) * 4));
+    m->owned.push_back(m->LOGrows);
+  }
+  if ((rc = m->enter())) return rc;
+  const int h = m->cfg.hidden, vocab = m->cfg.vocab;
+  std::vector<int> meta(2 * (size_t)M);
+  for (int r = 0; r < M; ++r) {
+    meta[r] = m->len[slots[r]];
+    meta[M + r] = slots[r];
+  }
+  const size_t rows = (size_t)M * h * 4;
+  cudaError_t e = cudaMemcpyAsync(m->Hbuf[0], hc_host, rows, cudaMemcpyHostToDevice, m->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(m->Hbuf[0] + (size_t)M * h, hs_host, rows, cudaMemcpyHostToDevice, m->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(m->p_pos, meta.data(), (size_t)M * 4, cudaMemcpyHostToDevice, m->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(m->p_seq, meta.data() + M, (size_t)M * 4, cudaMemcpyHostToDevice, m->stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(m->Dbuf, 0, 2 * rows, m->stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(m->amax, 0, (size_t)M * 8, m->stream);
+  if (e != cudaSuccess) rc = shd_cuda_fail(ctx, e, "shd_model_forward_host_rows: upload");
+  int cur = 0;
+  if (rc == SHD_OK) rc = m->enqueue_layers(M, m->p_pos, m->p_seq, m->cfg.variant_decode, cur, true);
+  if (rc == SHD_OK) rc = m->enqueue_head_rows(M, cur, m->cfg.variant_decode, m->LOGrows);
+  if (rc == SHD_OK && ctx->tp_world <= 1) {
+    e = cudaMemcpyAsync(logits_c_host, m->LOGrows, (size_t)M * vocab * 4, cudaMemcpyDeviceToHost, m->stream);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(logits_s_host, m->LOGrows + (size_t)M * m->V, (size_t)M * vocab * 4, cudaMemcpyDeviceToHost,
+                          m->stream);
+    if (e != cudaSuccess) rc = shd_cuda_fail(ctx, e, "shd_model_forward_host_rows: logits");
+  }
+  for (int r = 0; r < M && rc == SHD_OK && ctx->tp_world > 1; ++r)
+    rc = m->gather_logits(logits_c_host + (size_t)r * vocab, logits_s_host + (size_t)r * vocab,
+                          m->LOGrows + (size_t)r * m->V, m->LOGrows + (size_t)(M + r) * m->V);
+  if (rc == SHD_OK) {
+    e = cudaStreamSynchronize(m->stream);
+    if (e != cudaSuccess) {
+      rc = shd_cuda_fail(ctx, e, "shd_model_forward_host_rows");
+    } else {
+      for (int r = 0; r < M; ++r) m->len[slots[r]] += 1;
     }
   }
   rc = m->leave(rc);

@@ -87,7 +87,8 @@ struct shd_model {
   // decode: one new K/V row per sequence row (attention may read the older rows before the wait)
   int enqueue_layers(int M, const int* d_pos, const int* d_seq, int variant, int& cur, bool decode);
   int enqueue_head(int M, int row, int cur, int variant, bool want_logits, int key_row);
-  int enqueue_head_rows(int M, int cur, int variant);
+  // logits (nullable): [2][M][V] local logit shares written beside the argmax keys
+  int enqueue_head_rows(int M, int cur, int variant, float* logits = nullptr);
   int enqueue_decode_step(int M);
   int prefill_impl(int slot, int n, const int32_t* tokens_host, const float* hc_host, const float* hs_host,
                    float* logits_c_host, float* logits_s_host, float* final_c_host, float* final_s_host,
@@ -100,5 +101,8 @@ struct shd_model {
   bool has_pend_norm = false;
   int allreduce_recv(float* buf, size_t n);
   int allreduce_max_keys(int M);
-  int gather_logits(float* lc_host, float* ls_host);
+  // the whole vocabulary's logit shares of one row to the host (src: local [V] client, server
+  // shares; null = LOGbuf)
+  int gather_logits(float* lc_host, float* ls_host, const float* src_c = nullptr, const float* src_s = nullptr);
+  float* LOGrows = nullptr;  // [2][max_batch][V] logit rows of shd_model_forward_host_rows (lazy)
 };

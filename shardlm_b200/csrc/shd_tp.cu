@@ -476,10 +476,14 @@ int shd_model::allreduce_max_keys(int M) {
 }
 
 // Logit shares of the whole vocabulary to the host on every rank.
-int shd_model::gather_logits(float* lc_host, float* ls_host) {
+int shd_model::gather_logits(float* lc_host, float* ls_host, const float* src_c, const float* src_s) {
+  if (!src_c) {
+    src_c = LOGbuf;
+    src_s = LOGbuf + V;
+  }
   if (ctx->tp_world <= 1) {
-    SHD_CHECK_CUDA(ctx, cudaMemcpyAsync(lc_host, LOGbuf, (size_t)V * 4, cudaMemcpyDeviceToHost, stream));
-    SHD_CHECK_CUDA(ctx, cudaMemcpyAsync(ls_host, LOGbuf + V, (size_t)V * 4, cudaMemcpyDeviceToHost, stream));
+    SHD_CHECK_CUDA(ctx, cudaMemcpyAsync(lc_host, src_c, (size_t)V * 4, cudaMemcpyDeviceToHost, stream));
+    SHD_CHECK_CUDA(ctx, cudaMemcpyAsync(ls_host, src_s, (size_t)V * 4, cudaMemcpyDeviceToHost, stream));
     return SHD_OK;
   }
   const int W = ctx->tp_world;
@@ -491,8 +495,8 @@ int shd_model::gather_logits(float* lc_host, float* ls_host) {
   float* send = gather_buf;
   float* recv = gather_buf + 2 * cnt;
   SHD_CHECK_CUDA(ctx, cudaMemsetAsync(send, 0, 2 * cnt * 4, stream));
-  SHD_CHECK_CUDA(ctx, cudaMemcpyAsync(send, LOGbuf, (size_t)V * 4, cudaMemcpyDeviceToDevice, stream));
-  SHD_CHECK_CUDA(ctx, cudaMemcpyAsync(send + cnt, LOGbuf + V, (size_t)V * 4, cudaMemcpyDeviceToDevice, stream));
+  SHD_CHECK_CUDA(ctx, cudaMemcpyAsync(send, src_c, (size_t)V * 4, cudaMemcpyDeviceToDevice, stream));
+  SHD_CHECK_CUDA(ctx, cudaMemcpyAsync(send + cnt, src_s, (size_t)V * 4, cudaMemcpyDeviceToDevice, stream));
   NcclApi* a = nccl_api();
   const ncclResult_t r = a->AllGather(send, recv, 2 * cnt, ncclFloat32, static_cast<ncclComm_t>(ctx->nccl_comm), stream);
   if (r != ncclSuccess) return nccl_fail(ctx, r, "ncclAllGather(logits)");

@@ -208,6 +208,20 @@ class SecureModel:
                                            out[0].ctypes.data, out[1].ctypes.data), self.ctx.ptr)
         return out
 
+    def forward_host_rows(self, slots, hc: np.ndarray, hs: np.ndarray, out=None):
+        """forward_host for several sequences in one pass: hc/hs [M][hidden], row r at the next
+        position of slots[r]; returns logit shares (lc, ls) as [M][vocab]."""
+        sl = np.ascontiguousarray(np.asarray(slots, dtype=np.int32))
+        M = sl.size
+        hc = np.ascontiguousarray(hc, dtype=np.float32).reshape(M, self.shape.hidden)
+        hs = np.ascontiguousarray(hs, dtype=np.float32).reshape(M, self.shape.hidden)
+        if out is None:
+            out = (np.empty((M, self.shape.vocab), np.float32), np.empty((M, self.shape.vocab), np.float32))
+        self.ctx.bind_stream()
+        check(lib().shd_model_forward_host_rows(self.handle, M, sl.ctypes.data, hc.ctypes.data, hs.ctypes.data,
+                                                out[0].ctypes.data, out[1].ctypes.data), self.ctx.ptr)
+        return out
+
     def forward_host_hidden(self, hc: np.ndarray, hs: np.ndarray, slot: int = 0):
         """forward_host that also returns the position's output hidden shares:
         (logits_c, logits_s, hidden_c, hidden_s)."""

@@ -314,3 +314,39 @@ def test_decode_timeline_stamps_every_launch(ctx):
     assert (np.diff(last[:, 2]) >= 0).all()  # each launch ends after the one before it
     summ = timeline_summary(kinds, st)
     assert set(summ) >= {"qkv", "attention", "o", "gateup", "down", "lm_head"}
+
+
+@pytest.mark.parametrize("rows", [3, 6])
+def test_forward_host_rows_match_oracle(ctx, orc, rows):
+    """shd_model_forward_host_rows: sequences prefilled with different prompts advance one position
+    each in one pass (rows given in reverse slot order); every row's logit shares match the oracle of
+    its own sequence, twice in a row. With 6 rows the linears and the lm_head run on the tensor
+    cores."""
+    from shardlm_b200.model import TINY, SecureModel
+
+    shape = TINY.replace(n_layers=2)
+    prompts = [np.array(p, np.int32) for p in ([5, 17, 300], [9, 2, 44, 11, 7], [999], [1, 2], [640, 3, 3, 8],
+                                               [77, 78, 79, 80, 81, 82])][:rows]
+    m = SecureModel(ctx, shape, max_seq=32, max_batch=rows, share_seed=5)
+    host = m.load_random_weights(seed=21, host_copy=True)
+    for b, p in enumerate(prompts):
+        m.prefill(p, slot=b)
+    om = [_oracle_for(orc, shape, host, 32) for _ in prompts]
+    for b, p in enumerate(prompts):
+        for i, t in enumerate(p):
+            hc, hs = orc.embed_shares(host["embed"], shape.hidden, int(t), 5, (b << 32) + i)
+            om[b].forward(hc, hs, variant=orc.NL_GPU, attn_variant=orc.NL_APPROX)
+    slots = list(reversed(range(rows)))
+    rng = np.random.default_rng(rows)
+    for _ in range(2):
+        x = rng.standard_normal((rows, shape.hidden)).astype(np.float32)
+        hs = rng.uniform(0, 1, (rows, shape.hidden)).astype(np.float32)
+        hc = (x - hs).astype(np.float32)
+        lc, ls = m.forward_host_rows(slots, hc, hs)
+        for r, b in enumerate(slots):
+            _, _, oc, os_ = om[b].forward(hc[r], hs[r], variant=orc.NL_APPROX, attn_variant=orc.NL_APPROX)
+            ref = oc + os_
+            err = np.max(np.abs(lc[r] + ls[r] - ref)) / np.max(np.abs(ref))
+            assert err < LOGIT_RTOL, (r, b, err)
+    for b, p in enumerate(prompts):
+        assert m.seq_len(b) == len(p) + 2
