@@ -159,6 +159,9 @@ class ClockSampler:
             self.nv = pynvml
             self.h = pynvml.nvmlDeviceGetHandleByIndex(device)
             self.max = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            # one query before the timed region: the first ones after nvmlInit are the slow ones
+            pynvml.nvmlDeviceGetClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            pynvml.nvmlDeviceGetCurrentClocksEventReasons(self.h)
             self.ok = True
         except Exception:
             self.max = None
@@ -190,6 +193,18 @@ class ClockSampler:
         names = [n for b, n in self.REASONS.items() if self.reasons & b and n != "gpu_idle"]
         return {"sm_mhz": int(np.median(self.samples)), "sm_max_mhz": int(self.max), "reasons": names,
                 "samples": len(self.samples)}
+
+    @staticmethod
+    def merge(per_rank: list) -> dict:
+        """Every rank's summary in one: the lowest median SM clock, the union of throttle reasons."""
+        ok = [c for c in per_rank if c.get("sm_mhz") is not None]
+        if not ok:
+            return per_rank[0]
+        low = min(ok, key=lambda c: c["sm_mhz"])
+        reasons = sorted({r for c in per_rank for r in c.get("reasons", [])})
+        return {"sm_mhz": low["sm_mhz"], "sm_max_mhz": low["sm_max_mhz"], "reasons": reasons,
+                "samples": sum(c.get("samples", 0) for c in ok), "ranks": len(per_rank),
+                "sm_mhz_per_rank": [c.get("sm_mhz") for c in per_rank]}
 
 
 # ------------------------------------------------------------------------------------------------
@@ -299,10 +314,14 @@ def run_ours(args, shape):
         torch.cuda.profiler.stop()
         barrier()
     ms = start.elapsed_time(end)
+    clock_summary = clocks.summary()
     if world > 1:
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
+        per_rank = [None] * world
+        dist.all_gather_object(per_rank, clock_summary)
+        clock_summary = ClockSampler.merge(per_rank)
     toks = model.read_tokens(args.steps, B)
     launches_per_step = int(lib.shd_model_step_launches(model.handle))
     # per-kernel timing of the share-wise linears: the same step graph re-captured with CUDA events
@@ -438,7 +457,7 @@ def run_ours(args, shape):
             "prefill": prefill,
             "cpu_baseline": cpu,
             "gpu_launches": launches_per_step * args.steps,
-            "clocks": clocks.summary(),
+            "clocks": clock_summary,
             "tokens_head": toks[:8, 0].tolist(),
         }
         print(json.dumps(line), flush=True)
