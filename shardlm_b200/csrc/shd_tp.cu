@@ -2,7 +2,8 @@
 // PyTorch process this resolves to the NCCL torch already loaded). All-reduce is linear over
 // additive shares, so the client and server partial shares of a row-parallel projection are summed
 // by ONE all-reduce of the packed [2][M][h] buffer. Vocabulary-parallel lm_head: the greedy token is
-// an all-reduce MAX of (orderable logit, global index) keys.
+// a max-reduce of (orderable logit, global index) keys. Decode-sized messages and the keys go over
+// NVLink peer memory (kernels below), larger ones through NCCL.
 //
 // The reference has no NCCL at all (crates/v2/core/src/comm.rs:95-136 sums on the host, TODO at
 // :105); its only TP is the plaintext DistributedEngine (crates/v2/model/src/distributed.rs:312-624).
@@ -106,7 +107,8 @@ static_assert(kP2pPer % 2 == 0, "values per thread come in pairs");
 
 struct P2pArgs {
   float* buf;        // local partial shares in (allreduce form), sums out
-  size_t n;          // values
+  unsigned long long* keys;  // max-keys form: local keys in, the maximum over ranks out
+  size_t n;          // values (keys)
   uint8_t* peer[kP2pMaxWorld];  // every rank's receive buffer (peer[me] = local)
   int me, world;
   int* err;
@@ -233,6 +235,55 @@ __global__ void __launch_bounds__(kP2pThreads) p2p_recv_kernel(const __grid_cons
   if (threadIdx.x == 0) trace_first(a.trace, TR_WAIT);
   p2p_finish(a, acc, ok);
   if (threadIdx.x == 0) trace_both(a.trace, TR_EXIT);
+}
+
+// Max-reduce of n greedy keys ((orderable logit bits) << 32 | vocabulary index) over the ranks, the
+// vocabulary-parallel lm_head's argmax. A key does not fit one {value, epoch} word, so it travels as
+// two: word 2i holds its high half, word 2i + 1 its low half, each tagged with the call's epoch. The
+// call takes the same counter steps as p2p_allreduce_kernel (read at the start, advanced at the end,
+// dependents not released early), so it interleaves with the other exchanges under one epoch
+// sequence; only CTA 0 has keys to move (n <= kP2pThreads).
+__global__ void __launch_bounds__(kP2pThreads) p2p_maxkeys_kernel(const __grid_constant__ P2pArgs a) {
+  const unsigned epoch = (unsigned)*reinterpret_cast<const volatile int*>(p2p_counter(a)) + 1u;
+  pdl_wait();  // the keys come from the lm_head kernel
+  const unsigned long long tag = (unsigned long long)epoch << 32;
+  const int p = (int)(epoch & 1u);
+  const int i = threadIdx.x;
+  if (blockIdx.x == 0 && i < (int)a.n) {
+    const unsigned long long key = a.keys[i];
+    const unsigned long long hi = tag | (key >> 32), lo = tag | (key & 0xffffffffull);
+    for (int q = 0; q < a.world; ++q) {
+      unsigned long long* dst = p2p_slot(a.peer[q], p, a.world, a.me);
+      st_volatile_u64(dst + 2 * i, hi);
+      st_volatile_u64(dst + 2 * i + 1, lo);
+    }
+    const unsigned long long* slot0 = p2p_slot(a.peer[a.me], p, a.world, 0);
+    const size_t stride = kP2pSlotBytes / 8;
+    unsigned long long best = 0ull;
+    bool ok = true;
+    const uint64_t t0 = globaltimer_ns();
+    for (int r = 0; r < a.world && ok; ++r) {
+      unsigned long long h, l;
+      while (true) {
+        h = ld_volatile_u64(slot0 + r * stride + 2 * i);
+        l = ld_volatile_u64(slot0 + r * stride + 2 * i + 1);
+        if ((unsigned)(h >> 32) == epoch && (unsigned)(l >> 32) == epoch) break;
+        if (globaltimer_ns() - t0 > SHD_WAIT_LIMIT_NS) {
+          ok = false;
+          break;
+        }
+        __nanosleep(64);
+      }
+      const unsigned long long k = ((h & 0xffffffffull) << 32) | (l & 0xffffffffull);
+      best = k > best ? k : best;
+    }
+    if (ok)
+      a.keys[i] = best;
+    else
+      atomicOr(a.err, SHD_DEVERR_TIMEOUT_FULL);
+  }
+  __syncthreads();  // every thread of the CTA has read the counter
+  if (threadIdx.x == 0) *reinterpret_cast<volatile int*>(p2p_counter(a)) = (int)epoch;
 }
 
 int p2p_setup(shd_ctx* ctx) {
@@ -469,6 +520,19 @@ int shd_model::allreduce_recv(float* buf, size_t n) {
 
 int shd_model::allreduce_max_keys(int M) {
   if (ctx->tp_world <= 1) return SHD_OK;
+  if (ctx->p2p_local && M <= kP2pThreads && (size_t)2 * M <= kP2pCapacity) {
+    // over the peer-memory slots: no NCCL kernel in the decode step
+    P2pArgs p{};
+    p.keys = amax;
+    p.n = (size_t)M;
+    for (int q = 0; q < ctx->tp_world; ++q) p.peer[q] = static_cast<uint8_t*>(ctx->p2p_peer[q]);
+    p.me = ctx->tp_rank;
+    p.world = ctx->tp_world;
+    p.err = ctx->d_err;
+    SHD_CHECK_CUDA(ctx, launch_pdl(p2p_maxkeys_kernel, dim3(kP2pCtas), dim3(kP2pThreads), 0, stream, p));
+    ctx->launches++;
+    return SHD_OK;
+  }
   NcclApi* a = nccl_api();
   const ncclResult_t r = a->AllReduce(amax, amax, (size_t)M, ncclUint64, ncclMax, static_cast<ncclComm_t>(ctx->nccl_comm), stream);
   if (r != ncclSuccess) return nccl_fail(ctx, r, "ncclAllReduce(argmax keys)");
